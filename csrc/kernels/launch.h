@@ -1,0 +1,100 @@
+// Host-side entry points of the sm_100a kernels. Streams are passed as
+// void* (a cudaStream_t) so callers need no CUDA headers. Every launcher
+// returns 0 or a cudaError_t value and never synchronises.
+#ifndef MPCOMM_B200_CSRC_KERNELS_LAUNCH_H_
+#define MPCOMM_B200_CSRC_KERNELS_LAUNCH_H_
+
+#include <cstddef>
+#include <cstdint>
+
+namespace mpcomm {
+namespace kern {
+
+// One H2D QoS window record in pinned, device-mapped host memory. The
+// kernel writes begin_ns when its first CTA starts and end_ns (release,
+// system scope) when its last CTA has finished all stores. The host QoS
+// engine treats begin != 0 && end == 0 as "window open".
+struct H2DWindow {
+    uint64_t begin_ns;
+    uint64_t end_ns;
+    int32_t gpu;
+    uint32_t armed;
+    uint64_t pad;
+};
+
+struct LaunchInfo {
+    int ctas = 0;
+    int threads = 0;
+    size_t smem = 0;
+    int path = 0;  // 1 = bulk (TMA) pipeline, 2 = vector SM kernel
+};
+
+enum MoverMode { kModeAuto = 0, kModeSm = 1, kModeTma = 2 };
+
+// dst[i*bs .. +bs) = pool[idx[i]*bs .. +bs) for i in [0, n).
+// pool_blocks > 0 enables the index bound check (out-of-range indices are
+// skipped and flagged in *status). `window`/`window_ctr` may be null.
+int h2d_gather(const void *pool, int64_t pool_blocks, const int64_t *idx, void *out, int64_t n,
+               int64_t bs, int mode, int max_ctas, void *stream, uint32_t *status,
+               H2DWindow *window, uint32_t *window_ctr, LaunchInfo *info);
+// pool[idx[i]*bs ..] = src[i*bs ..].
+int h2d_scatter(const void *src, const int64_t *idx, void *pool, int64_t pool_blocks, int64_t n,
+                int64_t bs, int mode, int max_ctas, void *stream, uint32_t *status,
+                H2DWindow *window, uint32_t *window_ctr, LaunchInfo *info);
+
+// One GPU-fabric work request: a contiguous copy between any two addresses
+// the device can reach (local HBM, IPC-mapped peer HBM, mapped host DRAM).
+struct CopyDesc {
+    const void *src;
+    void *dst;
+    uint64_t bytes;
+};
+constexpr int kMaxCopyDescs = 64;
+// Copies up to kMaxCopyDescs spans in one launch (descriptors travel in the
+// kernel's parameter block, no staging buffer).
+int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_t *status,
+               LaunchInfo *info);
+
+// CRC-32 (IEEE 802.3, reflected polynomial 0xEDB88320, init/xorout
+// 0xFFFFFFFF — the zlib/PNG variant) of n blocks of bs bytes each.
+// Uses a per-device scratch buffer owned by the library (grown on demand).
+int crc32_blocks(const void *data, int64_t n, int64_t bs, uint32_t *out, void *stream);
+// Same, with caller-provided scratch of crc32_scratch_words(n, bs) words.
+int crc32_blocks_scratch(const void *data, int64_t n, int64_t bs, uint32_t *out, uint32_t *scratch,
+                         size_t scratch_words, void *stream);
+size_t crc32_scratch_words(int64_t n, int64_t bs);
+// Host reference (table-driven, byte at a time); `crc` chains calls (0 to start).
+uint32_t crc32_host(const void *data, size_t len, uint32_t crc);
+
+// Fused PXN gather + forward: for each i, copies pool[idx[i]*bs ..] (host
+// DRAM mapped on this GPU) into dst[i*bs ..], where dst may be a peer GPU's
+// HBM (IPC-mapped). After every store of the launch has completed, the last
+// CTA publishes `flag_value` to *done_flag (system-scope release; the flag
+// may live in the peer's memory).
+int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx, void *dst,
+                       int64_t n, int64_t bs, int max_ctas, void *stream, uint32_t *status,
+                       uint64_t *done_flag, uint64_t flag_value, uint32_t *ctr, LaunchInfo *info);
+
+// NVLS broadcast: multimem stores of src[0..bytes) into a multicast address
+// (every GPU bound to the multicast object receives the bytes).
+int nvls_broadcast(const void *src, void *mc_dst, uint64_t bytes, int max_ctas, void *stream,
+                   LaunchInfo *info);
+// Fallback fan-out: the same bytes stored to up to 8 peer pointers.
+int p2p_fanout(const void *src, void *const *dsts, int ndst, uint64_t bytes, int max_ctas,
+               void *stream, LaunchInfo *info);
+// Bounded wait on a 64-bit flag written by another GPU or the host: waits
+// until *flag >= value or budget_ns elapses (then sets kStatusFlagTimeout).
+int wait_flag(const uint64_t *flag, uint64_t value, uint64_t budget_ns, void *stream,
+              uint32_t *status);
+
+// Kernels launched by this library since load (all devices).
+uint64_t launch_count();
+// SM count of device `dev` (cached per device).
+int sm_count(int dev);
+// Device-time budget of every bounded wait, ns (MPCOMM_KERNEL_WAIT_BUDGET_MS).
+uint64_t wait_budget_ns();
+
+}  // namespace kern
+}  // namespace mpcomm
+
+#endif  // MPCOMM_B200_CSRC_KERNELS_LAUNCH_H_

@@ -1,0 +1,489 @@
+// sm_100a data movers: paged gather/scatter between mapped host DRAM and HBM
+// (tmaGather/tmaScatter) and the GPU-fabric WR batch copy.
+//
+// Bulk path ("TMA"). Persistent grid, one CTA per SM, WARPS independent
+// pipelines per CTA. A pipeline is driven by lane 0 of its warp: it keeps
+// STAGES bulk loads (cp.async.bulk global->shared, mbarrier complete_tx) in
+// flight, turns each landed stage into a bulk store (shared->global,
+// bulk_group) and refills a stage as soon as the store reading it has
+// drained (wait_group.read 1). The other 31 lanes fetch tile descriptors
+// (block index -> addresses) 32 tiles at a time and hand them to lane 0 by
+// shuffle, so index loads never sit on the issue path.
+//
+// Compared with the reference kernel (src/mpcomm_tma_kernels.cu:144-192:
+// one load->wait->store->wait per lane, 128 x block_size of shared memory,
+// so 64 KiB pages cannot launch), pages are split into STAGE_BYTES tiles,
+// shared memory is fixed at WARPS x STAGES x STAGE_BYTES, and every wait
+// is bounded.
+//
+// Vector path ("SM"). One warp per tile, 16-byte loads, 4 in flight per
+// lane, 64-bit indexing and no per-element div/mod (reference :259-299 used
+// 32-bit indices and a div/mod per 16 bytes).
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdlib>
+#include <mutex>
+
+#include "kernels/common.cuh"
+
+namespace mpcomm {
+namespace kern {
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+constexpr int kWarps = 4;
+constexpr int kStages = 3;
+constexpr uint32_t kStageBytes = 16384;
+constexpr size_t kBulkSmem = static_cast<size_t>(kWarps) * kStages * kStageBytes +
+                             static_cast<size_t>(kWarps) * kStages * sizeof(uint64_t);
+constexpr int kVecWarps = 8;
+constexpr uint32_t kVecTileBytes = 65536;
+
+}  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+int sm_count(int dev) {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    if (dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> g(mu);
+    if (!cache[dev]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cache[dev] = v;
+    }
+    return cache[dev];
+}
+
+uint64_t wait_budget_ns() {
+    static const uint64_t v = [] {
+        const char *e = std::getenv("MPCOMM_KERNEL_WAIT_BUDGET_MS");
+        long long ms = e ? std::atoll(e) : 2000;
+        if (ms <= 0) ms = 2000;
+        return static_cast<uint64_t>(ms) * 1000000ull;
+    }();
+    return v;
+}
+
+uint32_t *default_status_word(int dev) {
+    static std::mutex mu;
+    static uint32_t *words[64] = {nullptr};
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> g(mu);
+    if (!words[dev]) {
+        void *p = nullptr;
+        if (cudaMalloc(&p, 256) != cudaSuccess) return nullptr;
+        cudaMemset(p, 0, 256);
+        words[dev] = static_cast<uint32_t *>(p);
+    }
+    return words[dev];
+}
+
+// ---------------------------------------------------------------------------
+// Tile sources
+// ---------------------------------------------------------------------------
+struct GatherSrc {
+    const char *pool;
+    const int64_t *idx;
+    char *out;
+    int64_t n, bs, pool_blocks, tpb;
+    uint32_t tile_bytes;
+    __device__ __forceinline__ int64_t count() const { return n * tpb; }
+    __device__ __forceinline__ Tile tile(int64_t t) const {
+        const int64_t b = t / tpb;
+        const int64_t off = (t - b * tpb) * static_cast<int64_t>(tile_bytes);
+        const int64_t rem = bs - off;
+        const uint32_t len = static_cast<uint32_t>(rem < tile_bytes ? rem : tile_bytes);
+        const int64_t p = __ldg(idx + b);
+        if (p < 0 || (pool_blocks > 0 && p >= pool_blocks)) return Tile{nullptr, nullptr, len, kBad};
+        const char *s = pool + p * bs + off;
+        char *d = out + b * bs + off;
+        return Tile{s, d, len, tile_kind(s, d, len)};
+    }
+};
+
+struct ScatterSrc {
+    const char *src;
+    const int64_t *idx;
+    char *pool;
+    int64_t n, bs, pool_blocks, tpb;
+    uint32_t tile_bytes;
+    __device__ __forceinline__ int64_t count() const { return n * tpb; }
+    __device__ __forceinline__ Tile tile(int64_t t) const {
+        const int64_t b = t / tpb;
+        const int64_t off = (t - b * tpb) * static_cast<int64_t>(tile_bytes);
+        const int64_t rem = bs - off;
+        const uint32_t len = static_cast<uint32_t>(rem < tile_bytes ? rem : tile_bytes);
+        const int64_t p = __ldg(idx + b);
+        if (p < 0 || (pool_blocks > 0 && p >= pool_blocks)) return Tile{nullptr, nullptr, len, kBad};
+        const char *s = src + b * bs + off;
+        char *d = pool + p * bs + off;
+        return Tile{s, d, len, tile_kind(s, d, len)};
+    }
+};
+
+struct BatchSrc {
+    CopyDesc d[kMaxCopyDescs];
+    int64_t start[kMaxCopyDescs + 1];
+    int n;
+    uint32_t tile_bytes;
+    __device__ __forceinline__ int64_t count() const { return start[n]; }
+    __device__ __forceinline__ Tile tile(int64_t t) const {
+        int lo = 0, hi = n;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (start[mid] <= t) lo = mid; else hi = mid;
+        }
+        const int64_t off = (t - start[lo]) * static_cast<int64_t>(tile_bytes);
+        const int64_t rem = static_cast<int64_t>(d[lo].bytes) - off;
+        const uint32_t len = static_cast<uint32_t>(rem < tile_bytes ? rem : tile_bytes);
+        const char *s = static_cast<const char *>(d[lo].src) + off;
+        char *dd = static_cast<char *>(d[lo].dst) + off;
+        return Tile{s, dd, len, tile_kind(s, dd, len)};
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Bulk (TMA engine) pipeline, one per warp.
+// ---------------------------------------------------------------------------
+template <int STAGES, uint32_t STAGE_BYTES, class Src>
+__device__ __forceinline__ void warp_bulk_pipeline(const Src &src, int64_t first, int64_t stride,
+                                                   char *stage_mem, uint64_t *bars,
+                                                   uint32_t *status, uint64_t budget) {
+    const int lane = threadIdx.x & 31;
+    const int64_t total = src.count();
+    if (first >= total) return;
+    const int64_t n = (total - 1 - first) / stride + 1;
+
+    if (lane == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_proxy_async_smem();
+    }
+    __syncwarp();
+
+    Tile mine{nullptr, nullptr, 0, kSkip};
+    int64_t win = -1;
+    // Lane-0 record of what each stage holds.
+    const char *st_src[STAGES];
+    char *st_dst[STAGES];
+    uint32_t st_bytes[STAGES];
+    uint32_t st_kind[STAGES];
+    int64_t issued = 0;
+
+    auto issue = [&](int64_t t, int s) {  // warp-collective
+        const int64_t w = t >> 5;
+        if (w != win) {
+            win = w;
+            const int64_t tt = (w << 5) + lane;
+            mine = tt < n ? src.tile(first + tt * stride) : Tile{nullptr, nullptr, 0, kSkip};
+        }
+        const int sl = static_cast<int>(t & 31);
+        const char *ts = reinterpret_cast<const char *>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(mine.src), sl));
+        char *td = reinterpret_cast<char *>(
+            __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(mine.dst), sl));
+        const uint32_t tb = __shfl_sync(0xffffffffu, mine.bytes, sl);
+        const uint32_t tk = __shfl_sync(0xffffffffu, mine.kind, sl);
+        if (lane == 0) {
+            st_src[s] = ts;
+            st_dst[s] = td;
+            st_bytes[s] = tb;
+            st_kind[s] = tk;
+            const bool bulk = tk == kBulk;
+            mbar_arrive_expect_tx(&bars[s], bulk ? tb : 0u);
+            if (bulk) bulk_load(stage_mem + static_cast<size_t>(s) * STAGE_BYTES, ts, tb, &bars[s]);
+        }
+        ++issued;
+    };
+
+    const int64_t pro = n < STAGES ? n : STAGES;
+    for (int64_t t = 0; t < pro; ++t) issue(t, static_cast<int>(t));
+
+    int64_t j = 0;
+    bool aborted = false;
+    for (; j < n; ++j) {
+        const int s = static_cast<int>(j % STAGES);
+        const uint32_t parity = static_cast<uint32_t>((j / STAGES) & 1);
+        uint32_t kind = kSkip;
+        const char *isrc = nullptr;
+        char *idst = nullptr;
+        uint32_t ibytes = 0;
+        int ok = 1;
+        if (lane == 0) {
+            if (!mbar_wait_bounded(&bars[s], parity, budget)) {
+                ok = 0;
+                atomicOr(status, kStatusLoadTimeout);
+            } else {
+                kind = st_kind[s];
+                if (kind == kBulk) {
+                    bulk_store(st_dst[s], stage_mem + static_cast<size_t>(s) * STAGE_BYTES,
+                               st_bytes[s]);
+                } else if (kind == kBad) {
+                    atomicOr(status, kStatusBadIndex);
+                }
+                isrc = st_src[s];
+                idst = st_dst[s];
+                ibytes = st_bytes[s];
+            }
+            bulk_commit();
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            aborted = true;
+            break;
+        }
+        kind = __shfl_sync(0xffffffffu, kind, 0);
+        if (kind == kInline) {
+            isrc = reinterpret_cast<const char *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(isrc), 0));
+            idst = reinterpret_cast<char *>(
+                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(idst), 0));
+            ibytes = __shfl_sync(0xffffffffu, ibytes, 0);
+            warp_copy_any(idst, isrc, ibytes);
+        }
+        if (j >= 1) {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            const int64_t t = j - 1 + STAGES;
+            if (t < n) issue(t, static_cast<int>((j - 1) % STAGES));
+        }
+    }
+    if (lane == 0) {
+        if (aborted) {
+            // Drain every load still in flight into this warp's stages before
+            // the CTA may exit (bounded again).
+            for (int64_t t = j; t < issued; ++t) {
+                if (!mbar_wait_bounded(&bars[t % STAGES], static_cast<uint32_t>((t / STAGES) & 1),
+                                       budget)) {
+                    atomicOr(status, kStatusDrainTimeout);
+                    break;
+                }
+            }
+        }
+        bulk_wait_all();
+    }
+    __syncwarp();
+}
+
+// Kernel epilogue: closes an H2D QoS window and/or publishes a completion
+// flag once the last CTA has drained all of its stores.
+struct Epilogue {
+    H2DWindow *win;
+    uint32_t *ctr;      // last-CTA detector (self-resetting), required if win or flag
+    uint64_t *flag;     // may point into a peer GPU's memory
+    uint64_t flag_value;
+};
+
+__device__ __forceinline__ void run_epilogue(const Epilogue &ep) {
+    if (!ep.win && !ep.flag) return;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        const uint32_t prev = atomicAdd(ep.ctr, 1u);
+        if (prev == gridDim.x - 1) {
+            *ep.ctr = 0u;
+            __threadfence_system();
+            if (ep.flag) st_release_sys_u64(ep.flag, ep.flag_value);
+            if (ep.win) st_release_sys_u64(&ep.win->end_ns, globaltimer_ns() | 1ull);
+        }
+    }
+}
+
+template <int WARPS, int STAGES, uint32_t STAGE_BYTES, class Src>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    bulk_mover_kernel(const __grid_constant__ Src src, uint32_t *status, uint64_t budget,
+                      const Epilogue ep) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int warp = threadIdx.x >> 5;
+    char *stage_mem = reinterpret_cast<char *>(smem_raw) +
+                      static_cast<size_t>(warp) * STAGES * STAGE_BYTES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(
+                         smem_raw + static_cast<size_t>(WARPS) * STAGES * STAGE_BYTES) +
+                     warp * STAGES;
+    window_open(ep.win);
+    warp_bulk_pipeline<STAGES, STAGE_BYTES>(src, static_cast<int64_t>(blockIdx.x) * WARPS + warp,
+                                            static_cast<int64_t>(gridDim.x) * WARPS, stage_mem,
+                                            bars, status, budget);
+    run_epilogue(ep);
+}
+
+template <class Src>
+__global__ void __launch_bounds__(kVecWarps * 32)
+    vector_mover_kernel(const __grid_constant__ Src src, uint32_t *status, const Epilogue ep) {
+    const int lane = threadIdx.x & 31;
+    const int64_t total = src.count();
+    const int64_t nw = static_cast<int64_t>(gridDim.x) * kVecWarps;
+    window_open(ep.win);
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kVecWarps + (threadIdx.x >> 5); t < total;
+         t += nw) {
+        const Tile tl = src.tile(t);
+        if (tl.kind == kBad) {
+            if (lane == 0) atomicOr(status, kStatusBadIndex);
+            continue;
+        }
+        warp_copy_any(tl.dst, tl.src, tl.bytes);
+    }
+    run_epilogue(ep);
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+namespace {
+
+template <class Src>
+int launch_bulk(const Src &src, int64_t tiles, int max_ctas, cudaStream_t st, uint32_t *status,
+                const Epilogue &ep, LaunchInfo *info) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::mutex mu;
+    static uint64_t configured = 0;  // bit per device
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (dev < 64 && !(configured & (1ull << dev))) {
+            cudaError_t e = cudaFuncSetAttribute(
+                bulk_mover_kernel<kWarps, kStages, kStageBytes, Src>,
+                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmem));
+            if (e != cudaSuccess) return e;
+            configured |= 1ull << dev;
+        }
+    }
+    const int sms = sm_count(dev);
+    int cap = max_ctas > 0 ? max_ctas : sms;
+    int64_t need = (tiles + kWarps - 1) / kWarps;
+    int ctas = static_cast<int>(need < cap ? need : cap);
+    if (ctas < 1) ctas = 1;
+    if (!status) status = default_status_word(dev);
+    bulk_mover_kernel<kWarps, kStages, kStageBytes, Src>
+        <<<ctas, kWarps * 32, kBulkSmem, st>>>(src, status, wait_budget_ns(), ep);
+    note_launch();
+    if (info) *info = LaunchInfo{ctas, kWarps * 32, kBulkSmem, 1};
+    return cudaGetLastError();
+}
+
+template <class Src>
+int launch_vector(const Src &src, int64_t tiles, int max_ctas, cudaStream_t st, uint32_t *status,
+                  const Epilogue &ep, LaunchInfo *info) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int sms = sm_count(dev);
+    int cap = (max_ctas > 0 ? max_ctas : sms) * 4;
+    int64_t need = (tiles + kVecWarps - 1) / kVecWarps;
+    int ctas = static_cast<int>(need < cap ? need : cap);
+    if (ctas < 1) ctas = 1;
+    if (!status) status = default_status_word(dev);
+    vector_mover_kernel<Src><<<ctas, kVecWarps * 32, 0, st>>>(src, status, ep);
+    note_launch();
+    if (info) *info = LaunchInfo{ctas, kVecWarps * 32, 0, 2};
+    return cudaGetLastError();
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// AUTO: the bulk pipeline needs 16-byte aligned spans; tiny blocks are
+// better served one warp per block.
+int pick_path(int mode, const void *a, const void *b, int64_t bs) {
+    const bool ok = aligned16(a) && aligned16(b) && (bs % 16) == 0;
+    if (mode == kModeTma) return ok ? 1 : -1;
+    if (mode == kModeSm) return 2;
+    return (ok && bs >= 1024) ? 1 : 2;
+}
+
+}  // namespace
+
+int h2d_gather(const void *pool, int64_t pool_blocks, const int64_t *idx, void *out, int64_t n,
+               int64_t bs, int mode, int max_ctas, void *stream, uint32_t *status,
+               H2DWindow *window, uint32_t *window_ctr, LaunchInfo *info) {
+    if (!pool || !idx || !out || n <= 0 || bs <= 0) return cudaErrorInvalidValue;
+    if (window && !window_ctr) return cudaErrorInvalidValue;
+    const int path = pick_path(mode, pool, out, bs);
+    if (path < 0) return cudaErrorMisalignedAddress;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    GatherSrc src;
+    src.pool = static_cast<const char *>(pool);
+    src.idx = idx;
+    src.out = static_cast<char *>(out);
+    src.n = n;
+    src.bs = bs;
+    src.pool_blocks = pool_blocks;
+    src.tile_bytes = path == 1 ? kStageBytes : kVecTileBytes;
+    src.tpb = (bs + src.tile_bytes - 1) / src.tile_bytes;
+    const Epilogue ep{window, window_ctr, nullptr, 0};
+    return path == 1 ? launch_bulk(src, src.n * src.tpb, max_ctas, st, status, ep, info)
+                     : launch_vector(src, src.n * src.tpb, max_ctas, st, status, ep, info);
+}
+
+int h2d_scatter(const void *srcp, const int64_t *idx, void *pool, int64_t pool_blocks, int64_t n,
+                int64_t bs, int mode, int max_ctas, void *stream, uint32_t *status,
+                H2DWindow *window, uint32_t *window_ctr, LaunchInfo *info) {
+    if (!pool || !idx || !srcp || n <= 0 || bs <= 0) return cudaErrorInvalidValue;
+    if (window && !window_ctr) return cudaErrorInvalidValue;
+    const int path = pick_path(mode, pool, srcp, bs);
+    if (path < 0) return cudaErrorMisalignedAddress;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    ScatterSrc src;
+    src.src = static_cast<const char *>(srcp);
+    src.idx = idx;
+    src.pool = static_cast<char *>(pool);
+    src.n = n;
+    src.bs = bs;
+    src.pool_blocks = pool_blocks;
+    src.tile_bytes = path == 1 ? kStageBytes : kVecTileBytes;
+    src.tpb = (bs + src.tile_bytes - 1) / src.tile_bytes;
+    const Epilogue ep{window, window_ctr, nullptr, 0};
+    return path == 1 ? launch_bulk(src, src.n * src.tpb, max_ctas, st, status, ep, info)
+                     : launch_vector(src, src.n * src.tpb, max_ctas, st, status, ep, info);
+}
+
+int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_t *status,
+               LaunchInfo *info) {
+    if (n <= 0 || n > kMaxCopyDescs || !descs) return cudaErrorInvalidValue;
+    BatchSrc src;
+    src.tile_bytes = kStageBytes;
+    int k = 0;
+    int64_t tiles = 0;
+    for (int i = 0; i < n; ++i) {
+        if (descs[i].bytes == 0) continue;
+        src.d[k] = descs[i];
+        src.start[k] = tiles;
+        tiles += static_cast<int64_t>((descs[i].bytes + kStageBytes - 1) / kStageBytes);
+        ++k;
+    }
+    if (k == 0) return cudaSuccess;
+    src.start[k] = tiles;
+    src.n = k;
+    return launch_bulk(src, tiles, max_ctas, static_cast<cudaStream_t>(stream), status,
+                       Epilogue{nullptr, nullptr, nullptr, 0}, info);
+}
+
+int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx, void *dst,
+                       int64_t n, int64_t bs, int max_ctas, void *stream, uint32_t *status,
+                       uint64_t *done_flag, uint64_t flag_value, uint32_t *ctr, LaunchInfo *info) {
+    if (!pool || !idx || !dst || n <= 0 || bs <= 0) return cudaErrorInvalidValue;
+    if (done_flag && !ctr) return cudaErrorInvalidValue;
+    const int path = pick_path(kModeAuto, pool, dst, bs);
+    GatherSrc src;
+    src.pool = static_cast<const char *>(pool);
+    src.idx = idx;
+    src.out = static_cast<char *>(dst);
+    src.n = n;
+    src.bs = bs;
+    src.pool_blocks = pool_blocks;
+    src.tile_bytes = path == 1 ? kStageBytes : kVecTileBytes;
+    src.tpb = (bs + src.tile_bytes - 1) / src.tile_bytes;
+    const Epilogue ep{nullptr, ctr, done_flag, flag_value};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return path == 1 ? launch_bulk(src, src.n * src.tpb, max_ctas, st, status, ep, info)
+                     : launch_vector(src, src.n * src.tpb, max_ctas, st, status, ep, info);
+}
+
+}  // namespace kern
+}  // namespace mpcomm

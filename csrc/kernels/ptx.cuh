@@ -1,0 +1,156 @@
+// Inline-PTX helpers for the sm_100a data movers.
+//
+// Bulk copies (cp.async.bulk, the TMA engine's non-tensor form) move whole
+// 16-byte-aligned spans between global memory (local HBM, NVLink peer HBM,
+// or pinned host DRAM reached through UVA) and shared memory, completing
+// loads on an mbarrier (complete_tx) and stores on bulk groups. None of the
+// loads here uses .multicast::cluster: sources may be peer GPU memory.
+//
+// Every wait is bounded by %globaltimer; a timed-out wait sets a bit in the
+// caller's status word instead of spinning forever.
+#pragma once
+
+#include <cstdint>
+
+namespace mpcomm {
+namespace kern {
+
+// Status bits written by kernels (atomicOr into a device word).
+enum : uint32_t {
+    kStatusLoadTimeout = 1u << 0,   // an mbarrier wait for a bulk load expired
+    kStatusDrainTimeout = 1u << 1,  // the post-timeout drain wait expired too
+    kStatusBadIndex = 1u << 2,      // a block index outside [0, pool_blocks)
+    kStatusFlagTimeout = 1u << 3,   // a peer flag wait expired
+};
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+// Makes prior generic-proxy shared-memory writes (mbarrier.init) visible to
+// the async proxy that will signal the barrier.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for `parity` to complete; false after `budget_ns` of device time.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint64_t budget_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > budget_ns) return false;
+    }
+}
+
+// Bulk load global -> shared, completing `bytes` on `bar`.
+// L2 policy: evict_first (streamed data, read once).
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gmem_src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .b64 pol;\n\t"
+        "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], pol;\n\t}" ::"r"(smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Bulk store shared -> global, tracked by the issuing thread's bulk groups.
+__device__ __forceinline__ void bulk_store(void *gmem_dst, const void *smem_src, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 pol;\n\t"
+        "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+        "cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, pol;\n\t}" ::"l"(
+            gmem_dst),
+        "r"(smem_u32(smem_src)), "r"(bytes)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// At most N bulk groups may still be reading their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// All bulk groups fully complete (global writes performed).
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void st_release_sys_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t *p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// 16-byte vector load/store with no L1 allocation for streamed data.
+__device__ __forceinline__ int4 ld_stream_v4(const int4 *p) {
+    int4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Plain (coherent) 16-byte load: used where the source may be written by a
+// peer GPU or the host during the kernel's lifetime.
+__device__ __forceinline__ int4 ld_v4(const int4 *p) {
+    int4 v;
+    asm volatile("ld.global.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_v4(int4 *p, int4 v) {
+    asm volatile("st.global.v4.s32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+}  // namespace kern
+}  // namespace mpcomm

@@ -1,0 +1,678 @@
+// "nvl" backend: B200 GPU fabric rails.
+//
+// One rail per visible GPU. A queue pair is a CUDA stream of that GPU; a
+// posted WR is resolved to a (src, dst) device-address pair and queued; the
+// doorbell (flush) turns every queued WR into one descriptor of a single
+// copy_batch launch — the sm_100a bulk-copy kernel — followed by an event.
+// poll() retires launches whose event completed and emits one completion
+// per WR, so the engine sees RC-verbs semantics.
+//
+// Reachable memory:
+//   * this process's device memory on any GPU (peer access enabled),
+//   * this process's host memory (pinned + mapped at registration; UVA),
+//   * another process's device memory on the same host: registrations are
+//     published in /dev/shm/mpcomm-nvl.<boot>.<pid> (key, range, CUDA IPC
+//     handle) and opened with cudaIpcOpenMemHandle on first use.
+// This replaces the reference's NVLink proxy copies (cuMemcpyPeerAsync +
+// host callbacks, src/mpcomm_pxn.cpp:638-814) with in-kernel stores.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <chrono>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <mutex>
+#include <unordered_map>
+
+#include "core/core.h"
+#include "cuda/gpu.h"
+#include "kernels/launch.h"
+#include "mpcomm.h"
+#include "mpcomm_log.h"
+#include "topo/topology.h"
+#include "transport/fabric.h"
+
+namespace mpcomm {
+namespace fabric {
+namespace {
+
+constexpr uint32_t kDirMagic = 0x4E564C44;  // "NVLD"
+constexpr size_t kDirSlots = 4096;
+
+struct DirRecord {
+    uint32_t key;
+    uint32_t state;  // 0 free, 1 valid, 2 being written
+    uint64_t addr;
+    uint64_t len;
+    uint64_t base;
+    uint64_t alloc_size;
+    int32_t device;
+    int32_t kind;  // 0 device memory, 1 host memory
+    unsigned char ipc[gpu::kIpcHandleBytes];
+};
+
+struct DirHeader {
+    uint32_t magic;
+    uint32_t slots;
+    uint64_t pid;
+};
+
+std::string boot_tag() {
+    static const std::string tag = [] {
+        char buf[64] = {0};
+        FILE *f = fopen("/proc/sys/kernel/random/boot_id", "r");
+        if (f) {
+            if (!fgets(buf, sizeof(buf), f)) buf[0] = 0;
+            fclose(f);
+        }
+        std::string s;
+        for (char c : std::string(buf))
+            if (std::isxdigit(static_cast<unsigned char>(c))) s.push_back(c);
+        return s.substr(0, 8).empty() ? std::string("00000000") : s.substr(0, 8);
+    }();
+    return tag;
+}
+
+std::string dir_path(long pid) {
+    return "/dev/shm/mpcomm-nvl." + boot_tag() + "." + std::to_string(pid);
+}
+
+struct Region {
+    uint32_t key;
+    uintptr_t addr;
+    size_t len;
+    bool device;
+    int dev;
+    uintptr_t base;
+    size_t alloc_size;
+    bool pinned_by_us;
+    int refs;
+    size_t slot;
+};
+
+// Process-wide registry of nvl registrations + the shared directory.
+class Registry {
+ public:
+    static Registry &get() {
+        static Registry r;
+        return r;
+    }
+
+    int add(void *addr, size_t len, uint32_t *key) {
+        std::lock_guard<std::mutex> g(mu_);
+        for (auto &kv : regions_) {
+            Region &r = kv.second;
+            if (r.addr == reinterpret_cast<uintptr_t>(addr) && r.len == len) {
+                ++r.refs;
+                *key = r.key;
+                return 0;
+            }
+        }
+        Region r{};
+        r.addr = reinterpret_cast<uintptr_t>(addr);
+        r.len = len;
+        gpu::PtrInfo info;
+        bool known = gpu::query_pointer(addr, &info);
+        unsigned char ipc[gpu::kIpcHandleBytes] = {0};
+        if (known && info.is_device) {
+            r.device = true;
+            r.dev = info.device;
+            r.base = info.base ? info.base : r.addr;
+            r.alloc_size = info.size ? info.size : len;
+            if (gpu::ipc_get_handle(reinterpret_cast<void *>(r.base), ipc) != 0) {
+                // Not exportable (e.g. VMM allocation): usable in-process only.
+                std::memset(ipc, 0, sizeof(ipc));
+            }
+        } else {
+            void *dptr = nullptr;
+            bool pinned = false;
+            int e = gpu::host_pin_mapped(addr, len, &dptr, &pinned);
+            if (e != 0) {
+                MPCOMM_LOG_ERROR("MPComm[nvl]: cannot pin host range %p+%zu: %s\n", addr, len,
+                                 gpu::error_string(e));
+                return MPCOMM_ERR_MEMORY;
+            }
+            if (dptr != addr) {
+                // Non-UVA mapping: the kernels would need a translated pointer.
+                if (pinned) gpu::host_unpin(addr);
+                MPCOMM_LOG_ERROR("MPComm[nvl]: host memory %p is not identity-mapped\n", addr);
+                return MPCOMM_ERR_MEMORY;
+            }
+            r.device = false;
+            r.dev = -1;
+            r.base = r.addr;
+            r.alloc_size = len;
+            r.pinned_by_us = pinned;
+        }
+        r.key = next_key_++;
+        r.refs = 1;
+        r.slot = publish(r, ipc);
+        regions_[r.key] = r;
+        *key = r.key;
+        return 0;
+    }
+
+    int remove(uint32_t key) {
+        std::lock_guard<std::mutex> g(mu_);
+        auto it = regions_.find(key);
+        if (it == regions_.end()) return MPCOMM_ERR_INVALID_ARG;
+        if (--it->second.refs > 0) return 0;
+        if (it->second.pinned_by_us) gpu::host_unpin(reinterpret_cast<void *>(it->second.addr));
+        if (dir_ && it->second.slot < kDirSlots) {
+            DirRecord *rec = records() + it->second.slot;
+            __atomic_store_n(&rec->state, 0u, __ATOMIC_RELEASE);
+        }
+        regions_.erase(it);
+        return 0;
+    }
+
+    bool lookup(uint32_t key, Region *out) {
+        std::lock_guard<std::mutex> g(mu_);
+        auto it = regions_.find(key);
+        if (it == regions_.end()) return false;
+        *out = it->second;
+        return true;
+    }
+
+    ~Registry() {
+        if (dir_) {
+            munmap(dir_, dir_bytes());
+            unlink(dir_path(getpid()).c_str());
+        }
+    }
+
+ private:
+    static size_t dir_bytes() { return sizeof(DirHeader) + kDirSlots * sizeof(DirRecord); }
+    DirRecord *records() {
+        return reinterpret_cast<DirRecord *>(static_cast<char *>(dir_) + sizeof(DirHeader));
+    }
+
+    size_t publish(const Region &r, const unsigned char *ipc) {
+        if (!dir_ && !dir_failed_) {
+            std::string p = dir_path(getpid());
+            int fd = open(p.c_str(), O_RDWR | O_CREAT | O_TRUNC, 0600);
+            if (fd >= 0 && ftruncate(fd, static_cast<off_t>(dir_bytes())) == 0) {
+                void *m = mmap(nullptr, dir_bytes(), PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+                if (m != MAP_FAILED) {
+                    dir_ = m;
+                    auto *h = static_cast<DirHeader *>(dir_);
+                    h->slots = kDirSlots;
+                    h->pid = static_cast<uint64_t>(getpid());
+                    __atomic_store_n(&h->magic, kDirMagic, __ATOMIC_RELEASE);
+                }
+            }
+            if (fd >= 0) close(fd);
+            if (!dir_) {
+                dir_failed_ = true;
+                MPCOMM_LOG_WARN("MPComm[nvl]: cannot create %s; remote processes will not reach "
+                                "this process's memory\n", p.c_str());
+            }
+        }
+        if (!dir_) return kDirSlots;
+        DirRecord *recs = records();
+        for (size_t i = 0; i < kDirSlots; ++i) {
+            if (__atomic_load_n(&recs[i].state, __ATOMIC_ACQUIRE) != 0) continue;
+            __atomic_store_n(&recs[i].state, 2u, __ATOMIC_RELAXED);
+            recs[i].key = r.key;
+            recs[i].addr = r.addr;
+            recs[i].len = r.len;
+            recs[i].base = r.base;
+            recs[i].alloc_size = r.alloc_size;
+            recs[i].device = r.dev;
+            recs[i].kind = r.device ? 0 : 1;
+            std::memcpy(recs[i].ipc, ipc, gpu::kIpcHandleBytes);
+            __atomic_store_n(&recs[i].state, 1u, __ATOMIC_RELEASE);
+            return i;
+        }
+        MPCOMM_LOG_WARN("MPComm[nvl]: registration directory full\n");
+        return kDirSlots;
+    }
+
+    std::mutex mu_;
+    std::map<uint32_t, Region> regions_;
+    uint32_t next_key_ = 0x10000;
+    void *dir_ = nullptr;
+    bool dir_failed_ = false;
+};
+
+// Cache of other processes' directories and opened IPC mappings.
+class RemoteMaps {
+ public:
+    static RemoteMaps &get() {
+        static RemoteMaps m;
+        return m;
+    }
+    // Resolves [addr, addr+len) of process `pid`'s registration `key` to a
+    // pointer usable by kernels of this process. 0 on success.
+    int resolve(long pid, uint32_t key, uintptr_t addr, size_t len, uintptr_t *out) {
+        std::lock_guard<std::mutex> g(mu_);
+        const DirRecord *dir = open_dir(pid);
+        if (!dir) return kWcRemAccessErr;
+        for (size_t i = 0; i < kDirSlots; ++i) {
+            if (__atomic_load_n(&dir[i].state, __ATOMIC_ACQUIRE) != 1 || dir[i].key != key) continue;
+            DirRecord rec;
+            std::memcpy(&rec, &dir[i], sizeof(rec));
+            if (addr < rec.addr || addr + len > rec.addr + rec.len) return kWcRemAccessErr;
+            if (rec.kind != 0) return kWcRemAccessErr;  // remote host memory: not mappable
+            auto mk = std::make_pair(pid, rec.base);
+            auto it = opened_.find(mk);
+            if (it == opened_.end()) {
+                bool any = false;
+                for (size_t b = 0; b < gpu::kIpcHandleBytes; ++b) any |= rec.ipc[b] != 0;
+                if (!any) return kWcRemAccessErr;
+                void *p = nullptr;
+                int e = gpu::ipc_open_handle(rec.ipc, &p);
+                if (e != 0) {
+                    MPCOMM_LOG_ERROR("MPComm[nvl]: cudaIpcOpenMemHandle(pid %ld) failed: %s\n", pid,
+                                     gpu::error_string(e));
+                    return kWcRemAccessErr;
+                }
+                it = opened_.emplace(mk, reinterpret_cast<uintptr_t>(p)).first;
+            }
+            *out = it->second + (addr - rec.base);
+            return 0;
+        }
+        return kWcRemAccessErr;
+    }
+
+ private:
+    const DirRecord *open_dir(long pid) {
+        auto it = dirs_.find(pid);
+        if (it != dirs_.end()) return it->second;
+        int fd = open(dir_path(pid).c_str(), O_RDONLY);
+        if (fd < 0) return nullptr;
+        size_t bytes = sizeof(DirHeader) + kDirSlots * sizeof(DirRecord);
+        void *m = mmap(nullptr, bytes, PROT_READ, MAP_SHARED, fd, 0);
+        close(fd);
+        if (m == MAP_FAILED) return nullptr;
+        auto *h = static_cast<const DirHeader *>(m);
+        if (__atomic_load_n(&h->magic, __ATOMIC_ACQUIRE) != kDirMagic) {
+            munmap(m, bytes);
+            return nullptr;
+        }
+        const DirRecord *recs =
+            reinterpret_cast<const DirRecord *>(static_cast<const char *>(m) + sizeof(DirHeader));
+        dirs_[pid] = recs;
+        return recs;
+    }
+
+    std::mutex mu_;
+    std::unordered_map<long, const DirRecord *> dirs_;
+    std::map<std::pair<long, uintptr_t>, uintptr_t> opened_;
+};
+
+// gid = "nvl:<boot8>:<pid>:<dev>"
+bool parse_gid(const std::string &gid, std::string *boot, long *pid, int *dev) {
+    if (gid.compare(0, 4, "nvl:") != 0) return false;
+    size_t a = gid.find(':', 4);
+    if (a == std::string::npos) return false;
+    size_t b = gid.find(':', a + 1);
+    if (b == std::string::npos) return false;
+    *boot = gid.substr(4, a - 4);
+    *pid = std::strtol(gid.c_str() + a + 1, nullptr, 10);
+    *dev = static_cast<int>(std::strtol(gid.c_str() + b + 1, nullptr, 10));
+    return true;
+}
+
+class NvlRail;
+
+struct Inflight {
+    void *event;
+    std::vector<uint64_t> wr_ids;
+    std::vector<uint32_t> lens;
+    std::chrono::steady_clock::time_point launched;
+    bool failed;
+};
+
+class NvlQp final : public QueuePair {
+ public:
+    NvlQp(NvlRail *rail, uint32_t qpn);
+    ~NvlQp() override;
+    uint32_t qp_num() const override { return qpn_; }
+    QpState state() const override { return state_.load(); }
+    int to_init() override {
+        state_ = QpState::kInit;
+        return 0;
+    }
+    int to_rtr(const EndpointInfo &remote) override;
+    int to_rts() override {
+        if (state_.load() != QpState::kRtr) return MPCOMM_ERR_CONNECTION;
+        state_ = QpState::kRts;
+        return 0;
+    }
+    int to_err() override;
+    int recover() override {
+        to_err();
+        state_ = QpState::kInit;
+        EndpointInfo r = remote_;
+        if (to_rtr(r) != 0) return MPCOMM_ERR_CONNECTION;
+        return to_rts();
+    }
+    int post(const WorkRequest *wrs, size_t n) override;
+    void flush() override;
+    // Retires completed launches into the rail CQ. Caller holds rail mutex.
+    void reap(std::deque<WorkCompletion> *cq);
+
+ private:
+    friend class NvlRail;
+    NvlRail *rail_;
+    uint32_t qpn_;
+    std::atomic<QpState> state_{QpState::kReset};
+    EndpointInfo remote_;
+    long remote_pid_ = -1;
+    int remote_dev_ = -1;
+    void *stream_ = nullptr;
+    uint32_t *status_ = nullptr;
+    std::vector<kern::CopyDesc> pending_;
+    std::vector<uint64_t> pending_ids_;
+    std::vector<uint32_t> pending_lens_;
+    bool pending_host_ = false;
+    std::deque<Inflight> inflight_;
+};
+
+class NvlRail final : public Rail {
+ public:
+    NvlRail(int dev, const Config &cfg) : dev_(dev), cfg_(cfg) {
+        name_ = "nvl_" + std::to_string(dev);
+        gid_ = "nvl:" + boot_tag() + ":" + std::to_string(getpid()) + ":" + std::to_string(dev);
+        std::string bdf = gpu::pci_bdf(dev);
+        numa_ = topo::pci_numa_node(bdf);
+        if (numa_ < 0) numa_ = 0;
+        pci_path_ = topo::pci_realpath(bdf);
+        sms_ = kern::sm_count(dev);
+    }
+    ~NvlRail() override {
+        std::lock_guard<std::mutex> g(mu_);
+        for (void *e : free_events_) gpu::event_destroy(e);
+    }
+    const std::string &name() const override { return name_; }
+    std::string gid() const override { return gid_; }
+    int numa_node() const override { return numa_; }
+    std::string pci_path() const override { return pci_path_; }
+    int gpu_ordinal() const override { return dev_; }
+
+    int register_memory(void *addr, size_t len, MemKey *out) override {
+        uint32_t key = 0;
+        int e = Registry::get().add(addr, len, &key);
+        if (e) return e;
+        out->lkey = out->rkey = key;
+        return 0;
+    }
+    int deregister_memory(void *, const MemKey &key) override { return Registry::get().remove(key.lkey); }
+
+    std::unique_ptr<QueuePair> create_qp() override {
+        std::lock_guard<std::mutex> g(mu_);
+        auto qp = std::make_unique<NvlQp>(this, next_qpn_++);
+        qps_.push_back(qp.get());
+        return qp;
+    }
+    void forget(NvlQp *qp) {
+        std::lock_guard<std::mutex> g(mu_);
+        qps_.erase(std::remove(qps_.begin(), qps_.end(), qp), qps_.end());
+    }
+
+    int poll(WorkCompletion *out, int max) override {
+        std::lock_guard<std::mutex> g(mu_);
+        if (cq_.size() < static_cast<size_t>(max)) {
+            gpu::set_device(dev_);
+            for (NvlQp *qp : qps_) qp->reap(&cq_);
+        }
+        int n = 0;
+        while (n < max && !cq_.empty()) {
+            out[n++] = cq_.front();
+            cq_.pop_front();
+        }
+        return n;
+    }
+
+    size_t preferred_chunk(const Config &cfg) const override {
+        return cfg.max_rdma_transfer_size_set ? cfg.max_rdma_transfer_size : cfg.nvl_chunk_size;
+    }
+    size_t preferred_outstanding(const Config &cfg) const override {
+        return cfg.max_outstanding_set ? cfg.max_outstanding_per_qp : cfg.nvl_outstanding_per_qp;
+    }
+    int set_stream(void *stream) override {
+        std::lock_guard<std::mutex> g(mu_);
+        override_stream_ = stream;
+        return 0;
+    }
+
+    // Launch geometry: a copy touching host memory is PCIe-bound and gets a
+    // small grid (leaves SMs free for H2D kernels); device-to-device copies
+    // share the GPU among the QPs (or take all of it on one caller stream).
+    int ctas_for(bool host) const {
+        if (cfg_.nvl_ctas_per_qp > 0) return cfg_.nvl_ctas_per_qp;
+        if (host) return sms_ < 32 ? sms_ : 32;
+        if (override_stream_) return sms_;
+        int q = static_cast<int>(cfg_.qps_per_connection);
+        int c = q > 0 ? sms_ / q : sms_;
+        return c < 1 ? 1 : c;
+    }
+    void *take_event() {
+        if (!free_events_.empty()) {
+            void *e = free_events_.back();
+            free_events_.pop_back();
+            return e;
+        }
+        return gpu::event_create(dev_);
+    }
+    void give_event(void *e) { free_events_.push_back(e); }
+
+    std::mutex mu_;
+    int dev_;
+    void *override_stream_ = nullptr;
+    std::deque<WorkCompletion> cq_;
+
+ private:
+    const Config &cfg_;
+    std::string name_, gid_, pci_path_;
+    int numa_ = 0;
+    int sms_ = 0;
+    uint32_t next_qpn_ = 1;
+    std::vector<NvlQp *> qps_;
+    std::vector<void *> free_events_;
+};
+
+NvlQp::NvlQp(NvlRail *rail, uint32_t qpn) : rail_(rail), qpn_(qpn) {
+    stream_ = gpu::stream_create(rail_->dev_);
+    int prev = gpu::current_device();
+    gpu::set_device(rail_->dev_);
+    status_ = static_cast<uint32_t *>(gpu::device_alloc(64));
+    if (status_) gpu::memset_device(status_, 0, 64);
+    if (prev >= 0) gpu::set_device(prev);
+}
+
+NvlQp::~NvlQp() {
+    if (stream_) gpu::stream_sync(stream_);
+    {
+        std::lock_guard<std::mutex> g(rail_->mu_);
+        for (auto &f : inflight_) rail_->give_event(f.event);
+        inflight_.clear();
+    }
+    rail_->forget(this);
+    gpu::stream_destroy(stream_);
+    gpu::device_free(status_);
+}
+
+int NvlQp::to_rtr(const EndpointInfo &remote) {
+    std::string boot;
+    long pid = -1;
+    int dev = -1;
+    if (!parse_gid(remote.gid, &boot, &pid, &dev) || boot != boot_tag()) {
+        MPCOMM_LOG_WARN("MPComm[nvl]: peer %s is not an nvl rail on this host\n", remote.gid.c_str());
+        return MPCOMM_ERR_CONNECTION;
+    }
+    if (pid == getpid() && dev != rail_->dev_) {
+        int e = gpu::enable_peer_access(rail_->dev_, dev);
+        if (e != 0) {
+            MPCOMM_LOG_WARN("MPComm[nvl]: no peer access %d->%d\n", rail_->dev_, dev);
+            return MPCOMM_ERR_CONNECTION;
+        }
+    }
+    remote_ = remote;
+    remote_pid_ = pid;
+    remote_dev_ = dev;
+    state_ = QpState::kRtr;
+    return 0;
+}
+
+int NvlQp::to_err() {
+    state_ = QpState::kErr;
+    std::lock_guard<std::mutex> g(rail_->mu_);
+    for (size_t i = 0; i < pending_ids_.size(); ++i)
+        rail_->cq_.push_back(WorkCompletion{pending_ids_[i], kWcFlushErr, 0});
+    pending_.clear();
+    pending_ids_.clear();
+    pending_lens_.clear();
+    for (auto &f : inflight_) f.failed = true;
+    return 0;
+}
+
+int NvlQp::post(const WorkRequest *wrs, size_t n) {
+    QpState s = state_.load();
+    if (s != QpState::kRts && s != QpState::kErr) return MPCOMM_ERR_CONNECTION;
+    std::lock_guard<std::mutex> g(rail_->mu_);
+    for (size_t i = 0; i < n; ++i) {
+        const WorkRequest &wr = wrs[i];
+        if (s == QpState::kErr) {
+            rail_->cq_.push_back(WorkCompletion{wr.wr_id, kWcFlushErr, 0});
+            continue;
+        }
+        Region lr;
+        if (!Registry::get().lookup(wr.lkey, &lr) || wr.local_addr < lr.addr ||
+            wr.local_addr + wr.length > lr.addr + lr.len) {
+            rail_->cq_.push_back(WorkCompletion{wr.wr_id, kWcLocProtErr, 0});
+            continue;
+        }
+        uintptr_t rptr = 0;
+        bool remote_host = false;
+        if (remote_pid_ == getpid()) {
+            Region rr;
+            if (!Registry::get().lookup(wr.rkey, &rr) || wr.remote_addr < rr.addr ||
+                wr.remote_addr + wr.length > rr.addr + rr.len) {
+                rail_->cq_.push_back(WorkCompletion{wr.wr_id, kWcRemAccessErr, 0});
+                continue;
+            }
+            if (rr.device && rr.dev != rail_->dev_) gpu::enable_peer_access(rail_->dev_, rr.dev);
+            rptr = wr.remote_addr;
+            remote_host = !rr.device;
+        } else {
+            int st = RemoteMaps::get().resolve(remote_pid_, wr.rkey, wr.remote_addr, wr.length, &rptr);
+            if (st != 0) {
+                rail_->cq_.push_back(WorkCompletion{wr.wr_id, st, 0});
+                continue;
+            }
+        }
+        if (lr.device && lr.dev != rail_->dev_) gpu::enable_peer_access(rail_->dev_, lr.dev);
+        kern::CopyDesc d;
+        if (wr.op == Opcode::kWrite) {
+            d.src = reinterpret_cast<const void *>(wr.local_addr);
+            d.dst = reinterpret_cast<void *>(rptr);
+        } else {
+            d.src = reinterpret_cast<const void *>(rptr);
+            d.dst = reinterpret_cast<void *>(wr.local_addr);
+        }
+        d.bytes = wr.length;
+        pending_.push_back(d);
+        pending_ids_.push_back(wr.wr_id);
+        pending_lens_.push_back(wr.length);
+        pending_host_ |= remote_host || !lr.device;
+    }
+    return 0;
+}
+
+void NvlQp::flush() {
+    std::lock_guard<std::mutex> g(rail_->mu_);
+    if (pending_.empty()) return;
+    gpu::set_device(rail_->dev_);
+    void *stream = rail_->override_stream_ ? rail_->override_stream_ : stream_;
+    const int ctas = rail_->ctas_for(pending_host_);
+    size_t i = 0;
+    while (i < pending_.size()) {
+        size_t n = pending_.size() - i;
+        if (n > static_cast<size_t>(kern::kMaxCopyDescs)) n = kern::kMaxCopyDescs;
+        Inflight f;
+        f.event = nullptr;
+        f.failed = false;
+        f.wr_ids.assign(pending_ids_.begin() + i, pending_ids_.begin() + i + n);
+        f.lens.assign(pending_lens_.begin() + i, pending_lens_.begin() + i + n);
+        int e = kern::copy_batch(pending_.data() + i, static_cast<int>(n), ctas, stream, status_, nullptr);
+        if (e == 0) {
+            f.event = rail_->take_event();
+            if (!f.event || gpu::event_record(f.event, stream) != 0) e = -1;
+        }
+        if (e != 0) {
+            MPCOMM_LOG_ERROR("MPComm[nvl]: copy launch failed on %s: %s\n", rail_->name().c_str(),
+                             e > 0 ? gpu::error_string(e) : "event");
+            for (size_t k = 0; k < n; ++k)
+                rail_->cq_.push_back(WorkCompletion{f.wr_ids[k], kWcGeneralErr, 0});
+            if (f.event) rail_->give_event(f.event);
+        } else {
+            f.launched = std::chrono::steady_clock::now();
+            inflight_.push_back(std::move(f));
+        }
+        i += n;
+    }
+    pending_.clear();
+    pending_ids_.clear();
+    pending_lens_.clear();
+    pending_host_ = false;
+}
+
+void NvlQp::reap(std::deque<WorkCompletion> *cq) {
+    while (!inflight_.empty()) {
+        Inflight &f = inflight_.front();
+        int q = gpu::event_query(f.event);
+        if (q == 0) return;
+        bool bad = f.failed || q < 0;
+        if (!bad) {
+            // A kernel can only have timed out if it ran at least the wait
+            // budget; only then is the device status word read back.
+            double ran = std::chrono::duration<double>(std::chrono::steady_clock::now() - f.launched).count();
+            if (ran * 1e9 >= 0.9 * static_cast<double>(kern::wait_budget_ns())) {
+                uint32_t st = 0;
+                gpu::copy_d2h_sync(&st, status_, sizeof(st));
+                if (st) {
+                    bad = true;
+                    gpu::memset_device(status_, 0, sizeof(uint32_t));
+                }
+            }
+        }
+        for (size_t k = 0; k < f.wr_ids.size(); ++k)
+            cq->push_back(WorkCompletion{f.wr_ids[k], bad ? kWcGeneralErr : kWcSuccess,
+                                         bad ? 0u : f.lens[k]});
+        rail_->give_event(f.event);
+        inflight_.pop_front();
+    }
+}
+
+class NvlBackend final : public Backend {
+ public:
+    const char *name() const override { return "nvl"; }
+    int open(const Config &cfg, const std::vector<std::string> &filter,
+             std::vector<std::unique_ptr<Rail>> *rails) override {
+        int n = gpu::device_count();
+        for (int d = 0; d < n; ++d) {
+            std::string nm = "nvl_" + std::to_string(d);
+            if (!filter.empty()) {
+                bool ok = false;
+                for (auto &f : filter) ok |= (f == nm);
+                if (!ok) continue;
+            }
+            rails->push_back(std::make_unique<NvlRail>(d, cfg));
+        }
+        return rails->empty() ? MPCOMM_ERR_DEVICE : MPCOMM_SUCCESS;
+    }
+};
+
+}  // namespace
+
+std::unique_ptr<Backend> make_nvl_backend() { return std::make_unique<NvlBackend>(); }
+int nvl_device_count() { return gpu::device_count(); }
+
+}  // namespace fabric
+}  // namespace mpcomm

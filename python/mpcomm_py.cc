@@ -1,0 +1,468 @@
+// Python binding: module `mpcomm._mpcomm`, re-exported by the `mpcomm`
+// package. Method names, argument names, defaults and return shapes follow
+// the reference module (python/mpcomm_py.cpp:687-900); addresses are ints.
+// The GIL is released in every call that can block (wait, connect, query,
+// H2D launches) — the reference released it only in wait_transfer.
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "kernels/launch.h"
+#include "mpcomm.h"
+#include "transport/loopback_hooks.h"
+
+namespace py = pybind11;
+using namespace mpcomm;
+
+namespace {
+
+class PyMPComm {
+ public:
+    int init(const std::string &id, const std::string &devs, int port) {
+        py::gil_scoped_release r;
+        return c_.init(id, devs, port);
+    }
+    void shutdown() {
+        py::gil_scoped_release r;
+        c_.shutdown();
+    }
+    int register_memory(uintptr_t a, size_t l) {
+        py::gil_scoped_release r;
+        return c_.registerMemory(reinterpret_cast<void *>(a), l);
+    }
+    int unregister_memory(uintptr_t a) { return c_.unregisterMemory(reinterpret_cast<void *>(a)); }
+    int connect(const std::string &id, const std::string &addr, int port) {
+        py::gil_scoped_release r;
+        return c_.connect(id, addr, port);
+    }
+    int start_accept_thread() { return c_.startAcceptThread(); }
+    void stop_accept_thread() {
+        py::gil_scoped_release r;
+        c_.stopAcceptThread();
+    }
+    int update_remote_memory_info(const std::string &id, const std::vector<uint32_t> &k) {
+        return c_.updateRemoteMemoryInfo(id, k);
+    }
+    uint32_t get_rkey(size_t nic, uintptr_t a) { return c_.getRkey(nic, reinterpret_cast<void *>(a)); }
+    std::vector<uint32_t> get_all_rkeys(uintptr_t a) {
+        std::vector<uint32_t> v;
+        for (size_t i = 0; i < c_.getNumNics(); ++i) v.push_back(c_.getRkey(i, reinterpret_cast<void *>(a)));
+        return v;
+    }
+    uint64_t scatter_async(uintptr_t l, const std::vector<std::string> &h, const std::vector<uintptr_t> &r,
+                           const std::vector<size_t> &n) {
+        return c_.scatterAsync(l, h, r, n);
+    }
+    uint64_t gather_async(uintptr_t l, const std::vector<std::string> &h, const std::vector<uintptr_t> &r,
+                          const std::vector<size_t> &n) {
+        return c_.gatherAsync(l, h, r, n);
+    }
+    uint64_t broadcast_async(uintptr_t l, size_t len, const std::vector<std::string> &h,
+                             const std::vector<uintptr_t> &r) {
+        return c_.broadcastAsync(l, len, h, r);
+    }
+    uint64_t put_async(uintptr_t l, const std::string &h, uintptr_t r, size_t n) { return c_.putAsync(l, h, r, n); }
+    uint64_t get_async(uintptr_t l, const std::string &h, uintptr_t r, size_t n) { return c_.getAsync(l, h, r, n); }
+    uint64_t mp_replicate_async(const std::string &type, const std::vector<std::string> &h, uintptr_t l,
+                                const std::vector<uintptr_t> &r, const std::vector<size_t> &n) {
+        if (type == "scatter") return c_.scatterAsync(l, h, r, n);
+        if (type == "gather") return c_.gatherAsync(l, h, r, n);
+        if (type == "broadcast") return n.empty() ? INVALID_TRANSFER_HANDLE : c_.broadcastAsync(l, n[0], h, r);
+        return INVALID_TRANSFER_HANDLE;
+    }
+    bool is_transfer_complete(uint64_t h) { return c_.isTransferComplete(h); }
+    int wait_transfer(uint64_t h, int timeout_ms) {
+        py::gil_scoped_release r;
+        return c_.waitTransfer(h, timeout_ms);
+    }
+    py::dict get_transfer_result(uint64_t h) {
+        TransferResult t = c_.getTransferResult(h);
+        py::dict d;
+        d["error_code"] = t.error_code;
+        d["bytes_transferred"] = t.bytes_transferred;
+        d["elapsed_ms"] = t.elapsed_ms;
+        return d;
+    }
+    void release_transfer(uint64_t h) { c_.releaseTransfer(h); }
+    size_t get_num_nics() const { return c_.getNumNics(); }
+    std::string get_local_host_id() const { return c_.getLocalHostId(); }
+    int get_tcp_port() const { return c_.getTcpPort(); }
+    std::string get_gid(size_t i) const { return c_.getGid(i); }
+    std::string get_device_name(size_t i) const { return c_.getDeviceName(i); }
+    std::vector<std::string> get_active_devices() const { return c_.getActiveDevices(); }
+    size_t get_qps_per_connection() const { return c_.getQpsPerConnection(); }
+    size_t get_max_rdma_transfer_size() const { return c_.getMaxRdmaTransferSize(); }
+    void set_nic_throttle(size_t o, size_t c) { c_.setNicThrottle(o, c); }
+    void clear_nic_throttle() { c_.clearNicThrottle(); }
+    void enable_h2d_qos(uint64_t r, uint64_t b) { c_.enableH2DQoS(r, b); }
+    void set_h2d_qos_policy(uint64_t r, uint64_t b) { c_.setH2DQoSPolicy(r, b); }
+    bool is_h2d_qos_enabled() const { return c_.isH2DQoSEnabled(); }
+    void disable_h2d_qos() { c_.disableH2DQoS(); }
+    uint64_t get_nic_completed_bytes() const { return c_.getNicCompletedBytes(); }
+    py::list get_pcie_domain_stats() const {
+        py::list out;
+        for (auto &s : c_.getPcieDomainStats()) {
+            py::dict d;
+            d["gpu"] = s.gpu_device_id;
+            d["posted_bytes"] = s.posted_bytes;
+            d["completed_bytes"] = s.completed_bytes;
+            d["in_flight_bytes"] = s.in_flight_bytes;
+            d["in_flight_bytes_max"] = s.in_flight_bytes_max;
+            d["post_count"] = s.post_count;
+            d["defer_count"] = s.defer_count;
+            out.append(d);
+        }
+        return out;
+    }
+    void reset_pcie_domain_stats() { c_.resetPcieDomainStats(); }
+    bool is_pcie_domain_stat_enabled() const { return c_.isPcieDomainStatEnabled(); }
+    py::dict get_throttle_latency() const {
+        uint64_t s = 0, w = 0, d = 0;
+        size_t snap = 0;
+        const bool drained = c_.getThrottleLatency(&s, &w, &d, &snap);
+        py::dict r;
+        r["set_ns"] = s;
+        r["worker_seen_ns"] = w;
+        r["drained_ns"] = d;
+        r["snapshot_outstanding_wqes"] = snap;
+        r["drained"] = drained;
+        r["worker_us"] = w > s ? (w - s) / 1000.0 : 0.0;
+        r["drain_us"] = (drained && d > w && w > 0) ? (d - w) / 1000.0 : 0.0;
+        r["effective_us"] = (drained && d > s) ? (d - s) / 1000.0 : 0.0;
+        return r;
+    }
+    int write_bytes_to_buffer(uintptr_t a, const py::bytes &data, size_t len) {
+        std::string s = data;
+        if (s.size() < len) return MPCOMM_ERR_INVALID_ARG;
+        std::memcpy(reinterpret_cast<void *>(a), s.data(), len);
+        return MPCOMM_SUCCESS;
+    }
+    py::bytes read_bytes_from_buffer(uintptr_t a, size_t len) {
+        return py::bytes(reinterpret_cast<const char *>(a), len);
+    }
+    int publish_buffer(uintptr_t a, size_t l, int numa) {
+        return c_.publishBuffer(reinterpret_cast<void *>(a), l, numa);
+    }
+    int unpublish_buffer(uintptr_t a) { return c_.unpublishBuffer(reinterpret_cast<void *>(a)); }
+    void unpublish_all_buffers() { c_.unpublishAllBuffers(); }
+    size_t get_published_buffer_count() { return c_.getPublishedBufferCount(); }
+
+    static py::dict entry_dict(uint64_t addr, uint64_t len, int numa, int gpu, const std::vector<size_t> &aff,
+                               const std::vector<uint32_t> &rkeys) {
+        py::dict d;
+        d["addr"] = addr;
+        d["length"] = len;
+        d["numa_node"] = numa;
+        d["gpu_device_id"] = gpu;
+        d["pcie_affine_nic_indices"] = aff;
+        d["rkeys"] = rkeys;
+        return d;
+    }
+    py::dict query_remote_buffers(const std::string &id, const std::string &addr, int port) {
+        RemoteBufferInfo info;
+        int rc;
+        {
+            py::gil_scoped_release r;
+            rc = c_.queryRemoteBuffer(id, addr, port, info);
+        }
+        py::dict out;
+        if (rc != 0) return out;
+        out["host_id"] = info.host_id;
+        py::list bl;
+        for (auto &b : info.buffers)
+            bl.append(entry_dict(b.addr, b.length, b.numa_node, b.gpu_device_id, b.pcie_affine_nic_indices, b.rkeys));
+        out["buffers"] = bl;
+        return out;
+    }
+    py::dict query_remote_buffer_by_numa(const std::string &id, const std::string &addr, int port, int numa) {
+        RemoteBufferEntry e;
+        int rc;
+        {
+            py::gil_scoped_release r;
+            rc = c_.queryRemoteBufferByNuma(id, addr, port, numa, e);
+        }
+        if (rc != 0) return py::dict();
+        return entry_dict(e.addr, e.length, e.numa_node, e.gpu_device_id, e.pcie_affine_nic_indices, e.rkeys);
+    }
+    py::dict get_published_buffer_info() {
+        py::dict out;
+        const PublishedBufferInfo *info = c_.getPublishedBufferInfo();
+        if (!info || info->buffers.empty()) return out;
+        py::list bl;
+        for (auto &b : info->buffers)
+            bl.append(entry_dict(b.addr, b.length, b.numa_node, b.gpu_device_id, b.pcie_affine_nic_indices, b.rkeys));
+        out["buffers"] = bl;
+        return out;
+    }
+    py::list get_numa_topology() const {
+        py::list out;
+        for (auto &t : c_.getNumaTopology()) {
+            py::dict d;
+            d["numa_node"] = t.numa_node;
+            d["local_nics"] = t.local_nics;
+            d["remote_nics"] = t.remote_nics;
+            out.append(d);
+        }
+        return out;
+    }
+    py::list get_nic_topology() const {
+        py::list out;
+        for (auto &t : c_.getNicTopology()) {
+            py::dict d;
+            d["nic_name"] = t.nic_name;
+            d["numa_node"] = t.numa_node;
+            out.append(d);
+        }
+        return out;
+    }
+    int get_nic_numa_node(const std::string &n) const { return c_.getNicNumaNode(n); }
+    int get_numa_node_for_addr(uintptr_t a) const { return c_.getNumaNodeForAddr(reinterpret_cast<void *>(a)); }
+    std::vector<size_t> get_local_nic_indices_for_numa(int n) const { return c_.getLocalNicIndicesForNuma(n); }
+    int get_gpu_numa_node(int g) const { return c_.getGpuNumaNode(g); }
+    uintptr_t map_dram_to_gpu(uintptr_t h, size_t l) {
+        py::gil_scoped_release r;
+        return c_.mapDRAMtoGPU(reinterpret_cast<void *>(h), l);
+    }
+    int unmap_dram_from_gpu(uintptr_t h) {
+        py::gil_scoped_release r;
+        return c_.unmapDRAMfromGPU(reinterpret_cast<void *>(h));
+    }
+    int tma_gather(uintptr_t dram, uintptr_t idx, uintptr_t dst, int n, int bs, int max_sm, int mode,
+                   uintptr_t stream) {
+        py::gil_scoped_release r;
+        return c_.tmaGatherOnStream(dram, reinterpret_cast<const int64_t *>(idx), reinterpret_cast<void *>(dst),
+                                    n, bs, max_sm, static_cast<H2DMode>(mode), reinterpret_cast<void *>(stream));
+    }
+    int tma_scatter(uintptr_t src, uintptr_t idx, uintptr_t dram, int n, int bs, int max_sm, int mode,
+                    uintptr_t stream) {
+        py::gil_scoped_release r;
+        return c_.tmaScatterOnStream(reinterpret_cast<void *>(src), reinterpret_cast<const int64_t *>(idx), dram,
+                                     n, bs, max_sm, static_cast<H2DMode>(mode), reinterpret_cast<void *>(stream));
+    }
+    int set_fabric_stream(uintptr_t s) { return c_.setFabricStream(reinterpret_cast<void *>(s)); }
+    std::string get_fabric_name() const { return c_.getFabricName(); }
+
+ private:
+    MPComm c_;
+};
+
+int check(int e) { return e; }
+
+}  // namespace
+
+PYBIND11_MODULE(_mpcomm, m) {
+    m.doc() = "mpcomm native module: memory-pool communication for B200 (sm_100a)";
+
+    py::enum_<MPCommError>(m, "MPCommError")
+        .value("SUCCESS", MPCOMM_SUCCESS)
+        .value("ERR_DEVICE", MPCOMM_ERR_DEVICE)
+        .value("ERR_CONTEXT", MPCOMM_ERR_CONTEXT)
+        .value("ERR_MEMORY", MPCOMM_ERR_MEMORY)
+        .value("ERR_CONNECTION", MPCOMM_ERR_CONNECTION)
+        .value("ERR_TRANSFER", MPCOMM_ERR_TRANSFER)
+        .value("ERR_TIMEOUT", MPCOMM_ERR_TIMEOUT)
+        .value("ERR_INVALID_ARG", MPCOMM_ERR_INVALID_ARG)
+        .value("ERR_INVALID_HANDLE", MPCOMM_ERR_INVALID_HANDLE)
+        .value("ERR_PENDING", MPCOMM_ERR_PENDING)
+        .export_values();
+    m.attr("INVALID_TRANSFER_HANDLE") = INVALID_TRANSFER_HANDLE;
+    m.attr("H2D_MODE_AUTO") = static_cast<int>(H2D_MODE_AUTO);
+    m.attr("H2D_MODE_SM") = static_cast<int>(H2D_MODE_SM);
+    m.attr("H2D_MODE_TMA") = static_cast<int>(H2D_MODE_TMA);
+
+    using C = PyMPComm;
+    py::class_<C>(m, "MPComm")
+        .def(py::init<>())
+        .def("init", &C::init, py::arg("local_host_id"), py::arg("device_names") = "", py::arg("tcp_port") = 0)
+        .def("shutdown", &C::shutdown)
+        .def("register_memory", &C::register_memory, py::arg("addr"), py::arg("length"))
+        .def("unregister_memory", &C::unregister_memory, py::arg("addr"))
+        .def("connect", &C::connect, py::arg("remote_host_id"), py::arg("remote_tcp_addr"),
+             py::arg("remote_tcp_port"))
+        .def("start_accept_thread", &C::start_accept_thread)
+        .def("stop_accept_thread", &C::stop_accept_thread)
+        .def("update_remote_memory_info", &C::update_remote_memory_info, py::arg("remote_host_id"),
+             py::arg("rkeys"))
+        .def("get_rkey", &C::get_rkey, py::arg("nic_index"), py::arg("addr"))
+        .def("get_all_rkeys", &C::get_all_rkeys, py::arg("addr"))
+        .def("scatter_async", &C::scatter_async, py::arg("local_addr"), py::arg("host_list"),
+             py::arg("remote_addrs"), py::arg("lengths"))
+        .def("gather_async", &C::gather_async, py::arg("local_addr"), py::arg("host_list"),
+             py::arg("remote_addrs"), py::arg("lengths"))
+        .def("broadcast_async", &C::broadcast_async, py::arg("local_addr"), py::arg("length"),
+             py::arg("host_list"), py::arg("remote_addrs"))
+        .def("put_async", &C::put_async, py::arg("local_addr"), py::arg("remote_host_id"),
+             py::arg("remote_addr"), py::arg("length"))
+        .def("get_async", &C::get_async, py::arg("local_addr"), py::arg("remote_host_id"),
+             py::arg("remote_addr"), py::arg("length"))
+        .def("mp_replicate_async", &C::mp_replicate_async, py::arg("comm_type"), py::arg("host_list"),
+             py::arg("local_addr"), py::arg("remote_addrs"), py::arg("lengths"))
+        .def("is_transfer_complete", &C::is_transfer_complete, py::arg("handle"))
+        .def("wait_transfer", &C::wait_transfer, py::arg("handle"), py::arg("timeout_ms") = -1)
+        .def("get_transfer_result", &C::get_transfer_result, py::arg("handle"))
+        .def("release_transfer", &C::release_transfer, py::arg("handle"))
+        .def("get_num_nics", &C::get_num_nics)
+        .def("get_local_host_id", &C::get_local_host_id)
+        .def("get_tcp_port", &C::get_tcp_port)
+        .def("get_gid", &C::get_gid, py::arg("nic_index"))
+        .def("get_device_name", &C::get_device_name, py::arg("nic_index"))
+        .def("get_active_devices", &C::get_active_devices)
+        .def_static("get_nic_filter_env_var_name", [] { return std::string(MPComm::getNicFilterEnvVarName()); })
+        .def_static("get_qps_per_connection_env_var_name",
+                    [] { return std::string(MPComm::getQpsPerConnectionEnvVarName()); })
+        .def_static("get_pcie_stat_enable_env_var_name",
+                    [] { return std::string(MPComm::getPcieStatEnableEnvVarName()); })
+        .def("get_qps_per_connection", &C::get_qps_per_connection)
+        .def("get_max_rdma_transfer_size", &C::get_max_rdma_transfer_size)
+        .def("set_nic_throttle", &C::set_nic_throttle, py::arg("max_outstanding_per_qp"), py::arg("chunk_size") = 0)
+        .def("clear_nic_throttle", &C::clear_nic_throttle)
+        .def("enable_h2d_qos", &C::enable_h2d_qos, py::arg("rate_bytes_per_sec") = 0, py::arg("burst_bytes") = 0)
+        .def("set_h2d_qos_policy", &C::set_h2d_qos_policy, py::arg("rate_bytes_per_sec"), py::arg("burst_bytes") = 0)
+        .def("is_h2d_qos_enabled", &C::is_h2d_qos_enabled)
+        .def("disable_h2d_qos", &C::disable_h2d_qos)
+        .def("get_nic_completed_bytes", &C::get_nic_completed_bytes)
+        .def("get_pcie_domain_stats", &C::get_pcie_domain_stats)
+        .def("reset_pcie_domain_stats", &C::reset_pcie_domain_stats)
+        .def("is_pcie_domain_stat_enabled", &C::is_pcie_domain_stat_enabled)
+        .def("get_throttle_latency", &C::get_throttle_latency)
+        .def("write_bytes_to_buffer", &C::write_bytes_to_buffer, py::arg("addr"), py::arg("data"), py::arg("length"))
+        .def("read_bytes_from_buffer", &C::read_bytes_from_buffer, py::arg("addr"), py::arg("length"))
+        .def("publish_buffer", &C::publish_buffer, py::arg("addr"), py::arg("length"), py::arg("numa_node") = -1)
+        .def("unpublish_buffer", &C::unpublish_buffer, py::arg("addr"))
+        .def("unpublish_all_buffers", &C::unpublish_all_buffers)
+        .def("get_published_buffer_count", &C::get_published_buffer_count)
+        .def("query_remote_buffers", &C::query_remote_buffers, py::arg("remote_host_id"),
+             py::arg("remote_tcp_addr"), py::arg("remote_tcp_port"))
+        .def("query_remote_buffer_by_numa", &C::query_remote_buffer_by_numa, py::arg("remote_host_id"),
+             py::arg("remote_tcp_addr"), py::arg("remote_tcp_port"), py::arg("numa_node") = -1)
+        .def("query_remote_buffer",
+             [](C &c, const std::string &id, const std::string &a, int p) {
+                 return c.query_remote_buffer_by_numa(id, a, p, -1);
+             },
+             py::arg("remote_host_id"), py::arg("remote_tcp_addr"), py::arg("remote_tcp_port"))
+        .def("get_published_buffer_info", &C::get_published_buffer_info)
+        .def("get_numa_topology", &C::get_numa_topology)
+        .def("get_nic_topology", &C::get_nic_topology)
+        .def("get_nic_numa_node", &C::get_nic_numa_node, py::arg("nic_name"))
+        .def("get_numa_node_for_addr", &C::get_numa_node_for_addr, py::arg("addr"))
+        .def("get_local_nic_indices_for_numa", &C::get_local_nic_indices_for_numa, py::arg("numa_node"))
+        .def("get_gpu_numa_node", &C::get_gpu_numa_node, py::arg("gpu_device_id"))
+        .def("map_dram_to_gpu", &C::map_dram_to_gpu, py::arg("host_addr"), py::arg("length"))
+        .def("unmap_dram_from_gpu", &C::unmap_dram_from_gpu, py::arg("host_addr"))
+        .def("tma_gather", &C::tma_gather, py::arg("dram_dev_ptr"), py::arg("indices_ptr"), py::arg("gpu_dst_ptr"),
+             py::arg("num_blocks"), py::arg("block_size"), py::arg("max_sm_count") = 0, py::arg("mode") = 0,
+             py::arg("stream") = 0,
+             "Gather blocks from mapped DRAM into HBM. mode: 0=AUTO, 1=SM, 2=TMA. stream: cudaStream_t "
+             "(0 = legacy default stream).")
+        .def("tma_scatter", &C::tma_scatter, py::arg("gpu_src_ptr"), py::arg("indices_ptr"),
+             py::arg("dram_dev_ptr"), py::arg("num_blocks"), py::arg("block_size"), py::arg("max_sm_count") = 0,
+             py::arg("mode") = 0, py::arg("stream") = 0)
+        .def("set_fabric_stream", &C::set_fabric_stream, py::arg("stream"))
+        .def("get_fabric_name", &C::get_fabric_name)
+        .def_static("get_kernel_launch_count", [] { return MPComm::getKernelLaunchCount(); });
+
+    // ---- kernel entry points (used by mpcomm.ops) ----
+    m.def("crc32_blocks",
+          [](uintptr_t data, int64_t n, int64_t bs, uintptr_t out, uintptr_t stream) {
+              py::gil_scoped_release r;
+              return check(kern::crc32_blocks(reinterpret_cast<const void *>(data), n, bs,
+                                              reinterpret_cast<uint32_t *>(out), reinterpret_cast<void *>(stream)));
+          },
+          py::arg("data"), py::arg("num_blocks"), py::arg("block_size"), py::arg("out"), py::arg("stream") = 0);
+    m.def("crc32_host",
+          [](py::bytes b, uint32_t crc) {
+              std::string s = b;
+              return kern::crc32_host(s.data(), s.size(), crc);
+          },
+          py::arg("data"), py::arg("crc") = 0);
+    m.def("crc32_host_ptr",
+          [](uintptr_t p, size_t len, uint32_t crc) {
+              py::gil_scoped_release r;
+              return kern::crc32_host(reinterpret_cast<const void *>(p), len, crc);
+          },
+          py::arg("addr"), py::arg("length"), py::arg("crc") = 0);
+    m.def("paged_gather",
+          [](uintptr_t pool, int64_t pool_blocks, uintptr_t idx, uintptr_t out, int64_t n, int64_t bs, int mode,
+             int max_ctas, uintptr_t stream) {
+              py::gil_scoped_release r;
+              kern::LaunchInfo li;
+              int e = kern::h2d_gather(reinterpret_cast<const void *>(pool), pool_blocks,
+                                       reinterpret_cast<const int64_t *>(idx), reinterpret_cast<void *>(out), n, bs,
+                                       mode, max_ctas, reinterpret_cast<void *>(stream), nullptr, nullptr, nullptr,
+                                       &li);
+              return py::make_tuple(e, li.ctas, li.path);
+          },
+          py::arg("pool"), py::arg("pool_blocks"), py::arg("indices"), py::arg("out"), py::arg("num_blocks"),
+          py::arg("block_size"), py::arg("mode") = 0, py::arg("max_ctas") = 0, py::arg("stream") = 0);
+    m.def("paged_scatter",
+          [](uintptr_t src, uintptr_t idx, uintptr_t pool, int64_t pool_blocks, int64_t n, int64_t bs, int mode,
+             int max_ctas, uintptr_t stream) {
+              py::gil_scoped_release r;
+              kern::LaunchInfo li;
+              int e = kern::h2d_scatter(reinterpret_cast<const void *>(src), reinterpret_cast<const int64_t *>(idx),
+                                        reinterpret_cast<void *>(pool), pool_blocks, n, bs, mode, max_ctas,
+                                        reinterpret_cast<void *>(stream), nullptr, nullptr, nullptr, &li);
+              return py::make_tuple(e, li.ctas, li.path);
+          },
+          py::arg("src"), py::arg("indices"), py::arg("pool"), py::arg("pool_blocks"), py::arg("num_blocks"),
+          py::arg("block_size"), py::arg("mode") = 0, py::arg("max_ctas") = 0, py::arg("stream") = 0);
+    m.def("copy_spans",
+          [](const std::vector<uintptr_t> &src, const std::vector<uintptr_t> &dst, const std::vector<uint64_t> &len,
+             int max_ctas, uintptr_t stream) {
+              if (src.size() != dst.size() || src.size() != len.size() || src.size() > kern::kMaxCopyDescs)
+                  return static_cast<int>(MPCOMM_ERR_INVALID_ARG);
+              std::vector<kern::CopyDesc> d(src.size());
+              for (size_t i = 0; i < src.size(); ++i)
+                  d[i] = kern::CopyDesc{reinterpret_cast<const void *>(src[i]), reinterpret_cast<void *>(dst[i]), len[i]};
+              py::gil_scoped_release r;
+              return kern::copy_batch(d.data(), static_cast<int>(d.size()), max_ctas,
+                                      reinterpret_cast<void *>(stream), nullptr, nullptr);
+          },
+          py::arg("src"), py::arg("dst"), py::arg("lengths"), py::arg("max_ctas") = 0, py::arg("stream") = 0);
+    m.def("pxn_gather_forward",
+          [](uintptr_t pool, int64_t pool_blocks, uintptr_t idx, uintptr_t dst, int64_t n, int64_t bs, int max_ctas,
+             uintptr_t stream, uintptr_t flag, uint64_t flag_value, uintptr_t ctr) {
+              py::gil_scoped_release r;
+              return kern::pxn_gather_forward(reinterpret_cast<const void *>(pool), pool_blocks,
+                                              reinterpret_cast<const int64_t *>(idx), reinterpret_cast<void *>(dst), n,
+                                              bs, max_ctas, reinterpret_cast<void *>(stream), nullptr,
+                                              reinterpret_cast<uint64_t *>(flag), flag_value,
+                                              reinterpret_cast<uint32_t *>(ctr), nullptr);
+          },
+          py::arg("pool"), py::arg("pool_blocks"), py::arg("indices"), py::arg("dst"), py::arg("num_blocks"),
+          py::arg("block_size"), py::arg("max_ctas") = 0, py::arg("stream") = 0, py::arg("done_flag") = 0,
+          py::arg("flag_value") = 1, py::arg("counter") = 0);
+    m.def("nvls_broadcast",
+          [](uintptr_t src, uintptr_t mc, uint64_t bytes, int max_ctas, uintptr_t stream) {
+              py::gil_scoped_release r;
+              return kern::nvls_broadcast(reinterpret_cast<const void *>(src), reinterpret_cast<void *>(mc), bytes,
+                                          max_ctas, reinterpret_cast<void *>(stream), nullptr);
+          },
+          py::arg("src"), py::arg("mc_dst"), py::arg("bytes"), py::arg("max_ctas") = 0, py::arg("stream") = 0);
+    m.def("p2p_fanout",
+          [](uintptr_t src, const std::vector<uintptr_t> &dsts, uint64_t bytes, int max_ctas, uintptr_t stream) {
+              std::vector<void *> d;
+              for (auto p : dsts) d.push_back(reinterpret_cast<void *>(p));
+              py::gil_scoped_release r;
+              return kern::p2p_fanout(reinterpret_cast<const void *>(src), d.data(), static_cast<int>(d.size()),
+                                      bytes, max_ctas, reinterpret_cast<void *>(stream), nullptr);
+          },
+          py::arg("src"), py::arg("dsts"), py::arg("bytes"), py::arg("max_ctas") = 0, py::arg("stream") = 0);
+    m.def("wait_flag",
+          [](uintptr_t flag, uint64_t value, uint64_t budget_ns, uintptr_t stream, uintptr_t status) {
+              py::gil_scoped_release r;
+              return kern::wait_flag(reinterpret_cast<const uint64_t *>(flag), value, budget_ns,
+                                     reinterpret_cast<void *>(stream), reinterpret_cast<uint32_t *>(status));
+          },
+          py::arg("flag"), py::arg("value"), py::arg("budget_ns"), py::arg("stream") = 0, py::arg("status") = 0);
+    m.def("kernel_launch_count", [] { return kern::launch_count(); });
+    m.def("kernel_wait_budget_ns", [] { return kern::wait_budget_ns(); });
+
+    // ---- host-side fault hooks of the loopback fabric (tests) ----
+    m.def("_lo_inject_wc_errors", &fabric::loopback_inject_wc_errors, py::arg("gid"), py::arg("count"));
+    m.def("_lo_set_port_active", &fabric::loopback_set_port_active, py::arg("gid"), py::arg("active"));
+    m.def("_lo_set_wr_delay_us", &fabric::loopback_set_wr_delay_us, py::arg("gid"), py::arg("us"));
+}

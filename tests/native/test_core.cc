@@ -1,0 +1,154 @@
+// Native unit tests of the engine's building blocks (no GPU, no network).
+// Run by tests/test_native.py; exits non-zero on the first failure.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <set>
+#include <thread>
+#include <vector>
+
+#include "core/core.h"
+#include "ctrl/wire.h"
+#include "topo/topology.h"
+
+using namespace mpcomm;
+
+static int g_checks = 0;
+#define CHECK(cond)                                                                    \
+    do {                                                                               \
+        ++g_checks;                                                                    \
+        if (!(cond)) {                                                                 \
+            std::fprintf(stderr, "%s:%d: CHECK failed: %s\n", __FILE__, __LINE__, #cond); \
+            std::exit(1);                                                              \
+        }                                                                              \
+    } while (0)
+
+static void test_wrid() {
+    const uint64_t id = WrId::encode(3, 7, 0xBEEF, 0x12345678);
+    CHECK(id == 0x0307BEEF12345678ull);
+    CHECK(WrId::rail(id) == 3 && WrId::qp(id) == 7 && WrId::handle(id) == 0xBEEF &&
+          WrId::chunk(id) == 0x12345678);
+    // fields are masked, never bleed into neighbours
+    const uint64_t m = WrId::encode(0x1FF, 0x1FF, 0x1FFFF, 0x1FFFFFFFFull);
+    CHECK(WrId::rail(m) == 0xFF && WrId::qp(m) == 0xFF && WrId::handle(m) == 0xFFFF &&
+          WrId::chunk(m) == 0xFFFFFFFF);
+}
+
+static void test_handle_pool() {
+    HandlePool p;
+    std::set<uint64_t> seen;
+    for (int i = 0; i < 65535; ++i) {
+        uint64_t h = p.allocate();
+        CHECK(h >= 1 && h <= 65535);
+        CHECK(seen.insert(h).second);
+    }
+    CHECK(p.allocate() == 0);  // exhausted -> INVALID_TRANSFER_HANDLE
+    p.release(42);
+    CHECK(p.allocate() == 42);  // recycled
+    p.release(0);               // ignored
+    CHECK(p.allocate() == 0);
+}
+
+static void test_mpsc_ring() {
+    MpscRing r(1024);
+    const int producers = 4, per = 20000;
+    std::vector<std::thread> ts;
+    for (int t = 0; t < producers; ++t)
+        ts.emplace_back([&r, t] {
+            for (int i = 0; i < per; ++i)
+                while (!r.try_push(static_cast<uint64_t>(t) * per + i + 1)) cpu_relax();
+        });
+    std::vector<int> last(producers, -1);
+    size_t got = 0;
+    while (got < static_cast<size_t>(producers * per)) {
+        uint64_t v;
+        if (!r.try_pop(&v)) continue;
+        ++got;
+        int t = static_cast<int>((v - 1) / per), i = static_cast<int>((v - 1) % per);
+        CHECK(i > last[t]);  // FIFO per producer
+        last[t] = i;
+    }
+    for (auto &t : ts) t.join();
+    uint64_t v;
+    CHECK(!r.try_pop(&v));
+}
+
+static void test_chunk_plan() {
+    ChunkPlan p;
+    p.build(0x1000, {0x100000, 0x200000, 0x300000}, {300, 0, 250}, 128, false);
+    CHECK(p.total() == 3 + 0 + 2);
+    Chunk c = p.get(0);
+    CHECK(c.host_idx == 0 && c.local_addr == 0x1000 && c.remote_addr == 0x100000 && c.length == 128);
+    c = p.get(2);
+    CHECK(c.host_idx == 0 && c.length == 300 - 256 && c.remote_addr == 0x100000 + 256);
+    c = p.get(3);  // skips the empty host
+    CHECK(c.host_idx == 2 && c.local_addr == 0x1000 + 300 && c.remote_addr == 0x300000 && c.length == 128);
+    c = p.get(4);
+    CHECK(c.length == 250 - 128);
+    // broadcast: every host reads from local offset 0
+    ChunkPlan b;
+    b.build(0x5000, {0x10, 0x20}, {100, 100}, 64, true);
+    CHECK(b.total() == 4);
+    CHECK(b.get(2).local_addr == 0x5000 && b.get(2).host_idx == 1 && b.get(3).local_addr == 0x5000 + 64);
+}
+
+static void test_token_bucket() {
+    TokenBucket tb;
+    tb.configure(0, 0);
+    CHECK(!tb.consume(1));  // rate 0 pauses
+    tb.configure(1000000000ull, 1 << 20);  // 1 GB/s
+    std::this_thread::sleep_for(std::chrono::milliseconds(2));
+    CHECK(tb.consume(1 << 20));    // ~2 MB accrued, capped at the 1 MiB burst
+    CHECK(!tb.consume(1 << 20));   // drained
+    CHECK(default_qos_burst(0) == 0);
+    CHECK(default_qos_burst(1000) == 4096);
+    CHECK(default_qos_burst(1ull << 40) == 65536);
+    CHECK(default_qos_burst(200000000) == 20000);
+}
+
+static void test_topology_parsers() {
+    auto v = topo::parse_cpulist("0-3,8,10-11");
+    CHECK(v.size() == 7 && v[0] == 0 && v[3] == 3 && v[4] == 8 && v[6] == 11);
+    CHECK(topo::parse_cpulist("").empty());
+    CHECK(topo::name_suffix("mlx5_3") == 3 && topo::name_suffix("mlx5_bond_12") == 12 &&
+          topo::name_suffix("eth") == -1 && topo::name_suffix("nvl_0") == 0);
+    CHECK(topo::common_path_components("/sys/devices/pci0000:10/0000:10:01.0/0000:11:00.0",
+                                       "/sys/devices/pci0000:10/0000:10:01.0/0000:12:00.0") == 4);
+    auto aff = topo::best_affinity("/sys/devices/pci0000:10/0000:10:01.0/0000:11:00.0",
+                                   {"/sys/devices/pci0000:20/0000:20:01.0/0000:21:00.0",
+                                    "/sys/devices/pci0000:10/0000:10:01.0/0000:13:00.0",
+                                    "/sys/devices/pci0000:10/0000:10:02.0/0000:14:00.0"});
+    CHECK(aff.size() == 1 && aff[0] == 1);
+    // sharing only the root complex is not affinity
+    CHECK(topo::best_affinity("/sys/devices/pci0000:10/a", {"/sys/devices/pci0000:10/b"}).empty());
+}
+
+static void test_wire_layout() {
+    RemoteEndpointInfo e;
+    std::memset(&e, 0, sizeof(e));
+    std::strcpy(e.gid, "fe:80");
+    e.lid = 0x1234;
+    e.qp_num = 0xA1B2C3D4;
+    e.rkey = 0x55;
+    e.addr = 7;
+    e.length = 9;
+    const unsigned char *b = reinterpret_cast<const unsigned char *>(&e);
+    CHECK(sizeof(e) == 96);
+    CHECK(b[64] == 0x34 && b[65] == 0x12);                 // lid, host-endian (LE)
+    CHECK(b[68] == 0xD4 && b[71] == 0xA1);                 // qp_num
+    CHECK(b[72] == 0x55 && b[80] == 7 && b[88] == 9);
+    CHECK(kMsgTypeBufferQuery == 0x4D504251 && kMsgTypeQosControlOpen == 0x4D505143 &&
+          kQosControlFrameMagic == 0x4D505146);
+}
+
+int main() {
+    test_wrid();
+    test_handle_pool();
+    test_mpsc_ring();
+    test_chunk_plan();
+    test_token_bucket();
+    test_topology_parsers();
+    test_wire_layout();
+    std::printf("native core tests passed (%d checks)\n", g_checks);
+    return 0;
+}

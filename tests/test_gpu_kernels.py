@@ -1,0 +1,237 @@
+"""GPU tests of the sm_100a kernels against plain PyTorch / zlib references.
+
+Every comparison is bit-exact: these kernels move bytes. Cases mirror the
+reference's user_examples/test_tma.py (gather, per-block scatter, round
+trip, alignment sweep 16..1024 B) plus the B200 additions (64 KiB pages,
+index bound check, bounded waits, CRC-32, fabric copies).
+"""
+import random
+import zlib
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+import mpcomm  # noqa: E402
+from mpcomm import ops  # noqa: E402
+
+
+def _pool(pages, bs, seed=0, pinned=True):
+    g = torch.Generator().manual_seed(seed)
+    t = torch.randint(0, 256, (pages, bs), dtype=torch.uint8, generator=g)
+    return t.pin_memory() if pinned else t.cuda()
+
+
+@pytest.mark.parametrize("bs", [16, 272, 1024, 4096, 65536, 65536 + 48])
+@pytest.mark.parametrize("mode", [ops.MODE_AUTO, ops.MODE_SM, ops.MODE_TMA])
+def test_paged_gather_bitexact(bs, mode):
+    pages, n = 64, 40
+    pool = _pool(pages, bs, seed=bs)
+    idx = torch.randperm(pages, generator=torch.Generator().manual_seed(1))[:n].cuda()
+    out = ops.paged_gather(pool, idx, mode=mode)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), pool[idx.cpu()])
+
+
+@pytest.mark.parametrize("bs", [16, 1040, 65536])
+@pytest.mark.parametrize("mode", [ops.MODE_AUTO, ops.MODE_SM, ops.MODE_TMA])
+def test_paged_scatter_bitexact(bs, mode):
+    pages, n = 48, 20
+    pool = _pool(pages, bs, seed=3)
+    before = pool.clone()
+    idx = torch.randperm(pages, generator=torch.Generator().manual_seed(2))[:n].cuda()
+    src = torch.randint(0, 256, (n, bs), dtype=torch.uint8, device="cuda")
+    ops.paged_scatter(src, idx, pool, mode=mode)
+    torch.cuda.synchronize()
+    expect = before.clone()
+    expect[idx.cpu()] = src.cpu()
+    assert torch.equal(pool, expect)
+
+
+def test_gather_scatter_round_trip_device_pool():
+    pages, bs, n = 128, 8192, 128
+    pool = _pool(pages, bs, seed=5, pinned=False)
+    idx = torch.randperm(pages, device="cuda")
+    staged = ops.paged_gather(pool, idx)
+    back = torch.zeros_like(pool)
+    ops.paged_scatter(staged, idx, back)
+    torch.cuda.synchronize()
+    assert torch.equal(back, pool)
+
+
+@pytest.mark.parametrize("offset", [1, 4, 8, 12])
+def test_sm_mode_handles_unaligned_blocks(offset):
+    pages, bs, n = 16, 1000, 10
+    raw = torch.randint(0, 256, (pages * bs + 64,), dtype=torch.uint8).pin_memory()
+    base = raw.data_ptr() + offset
+    idx = torch.randperm(pages)[:n].cuda()
+    out = torch.empty(n * bs, dtype=torch.uint8, device="cuda")
+    err, _, path = mpcomm._native.paged_gather(base, pages, idx.data_ptr(), out.data_ptr(), n, bs,
+                                               ops.MODE_AUTO, 0, torch.cuda.current_stream().cuda_stream)
+    assert err == 0 and path == 2  # AUTO falls back to the vector kernel
+    torch.cuda.synchronize()
+    ref = raw[offset:offset + pages * bs].view(pages, bs)[idx.cpu()].reshape(-1)
+    assert torch.equal(out.cpu(), ref)
+
+
+def test_tma_mode_rejects_misaligned():
+    pool = torch.zeros(4 * 1024 + 16, dtype=torch.uint8).pin_memory()
+    idx = torch.zeros(2, dtype=torch.int64, device="cuda")
+    out = torch.empty(2 * 1000, dtype=torch.uint8, device="cuda")
+    err, _, _ = mpcomm._native.paged_gather(pool.data_ptr(), 4, idx.data_ptr(), out.data_ptr(), 2, 1000,
+                                            ops.MODE_TMA, 0, 0)
+    assert err != 0  # misaligned block size: refused, not silently rerouted
+
+
+def test_out_of_range_index_is_skipped():
+    pages, bs = 8, 4096
+    pool = _pool(pages, bs)
+    idx = torch.tensor([0, 99, 2, -1], dtype=torch.int64, device="cuda")
+    out = torch.full((4, bs), 7, dtype=torch.uint8, device="cuda")
+    ops.paged_gather(pool, idx, out=out)
+    torch.cuda.synchronize()
+    o = out.cpu()
+    assert torch.equal(o[0], pool[0]) and torch.equal(o[2], pool[2])
+    assert (o[1] == 7).all() and (o[3] == 7).all()  # bad indices never touch memory
+
+
+@pytest.mark.parametrize("bs", [1, 15, 4096, (512 << 10) + 3, 3 << 20])
+def test_crc32_matches_zlib(bs):
+    n = 5
+    data = torch.randint(0, 256, (n * bs,), dtype=torch.uint8, generator=torch.Generator().manual_seed(bs))
+    got = ops.crc32_blocks(data.cuda(), n).cpu().tolist()
+    raw = data.numpy().tobytes()
+    want = [zlib.crc32(raw[i * bs:(i + 1) * bs]) for i in range(n)]
+    assert [g & 0xFFFFFFFF for g in got] == want
+
+
+def test_copy_spans_mixed_alignment():
+    src = torch.randint(0, 256, (1 << 22,), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros_like(src)
+    spans = [(0, 0, 1 << 20), ((1 << 20) + 3, (1 << 20) + 3, 65537), (2 << 20, (3 << 20) + 5, 1000)]
+    ops.copy_spans([src.data_ptr() + a for a, _, _ in spans], [dst.data_ptr() + b for _, b, _ in spans],
+                   [n for _, _, n in spans])
+    torch.cuda.synchronize()
+    for a, b, n in spans:
+        assert torch.equal(dst[b:b + n], src[a:a + n])
+
+
+def test_bounded_flag_wait_times_out_and_context_survives():
+    """A wait on a flag nothing sets ends with a status bit, not a hang."""
+    flag = torch.zeros(1, dtype=torch.int64, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.wait_flag(flag.data_ptr(), 1, budget_ns=50_000_000, status_ptr=status.data_ptr())
+    torch.cuda.synchronize()
+    assert status.item() & 8  # kStatusFlagTimeout
+    # The context is still usable.
+    x = torch.arange(1024, device="cuda")
+    assert int(x.sum().item()) == 1024 * 1023 // 2
+    flag.fill_(1)
+    status.zero_()
+    ops.wait_flag(flag.data_ptr(), 1, budget_ns=50_000_000, status_ptr=status.data_ptr())
+    torch.cuda.synchronize()
+    assert status.item() == 0
+
+
+def test_pxn_forward_local_flag():
+    """Fused gather + forward into a (here local) destination with a done flag."""
+    pages, bs, n = 32, 65536, 12
+    pool = _pool(pages, bs, seed=9)
+    idx = torch.randperm(pages)[:n].cuda()
+    dst = torch.empty((n, bs), dtype=torch.uint8, device="cuda")
+    flag = torch.zeros(1, dtype=torch.int64, device="cuda")
+    ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.pxn_gather_forward(pool.data_ptr(), pages, idx, dst.data_ptr(), bs, done_flag=flag.data_ptr(),
+                           flag_value=77, counter=ctr.data_ptr())
+    torch.cuda.synchronize()
+    assert flag.item() == 77 and ctr.item() == 0
+    assert torch.equal(dst.cpu(), pool[idx.cpu()])
+
+
+def _fabric_pair():
+    comm = mpcomm.MPComm()
+    assert comm.init("gpu-test") == 0
+    assert comm.get_fabric_name() == "nvl"
+    assert comm.start_accept_thread() == 0
+    return comm
+
+
+@pytest.mark.parametrize("nbytes", [4096, (1 << 20) + 13, 96 << 20])
+def test_fabric_put_get_hbm_dram(nbytes):
+    comm = _fabric_pair()
+    try:
+        src = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda")
+        back = torch.zeros_like(src)
+        pool = torch.zeros(nbytes, dtype=torch.uint8).pin_memory()
+        for t in (src, back, pool):
+            assert comm.register_memory(t.data_ptr(), t.numel()) == 0
+        assert comm.publish_buffer(pool.data_ptr(), nbytes) == 0
+        port = comm.get_tcp_port()
+        assert comm.connect("pool", "127.0.0.1", port) == 0
+        assert comm.query_remote_buffers("pool", "127.0.0.1", port)
+        torch.cuda.synchronize()
+        h = comm.put_async(src.data_ptr(), "pool", pool.data_ptr(), nbytes)
+        assert comm.wait_transfer(h, 60000) == 0
+        r = comm.get_transfer_result(h)
+        assert r["bytes_transferred"] == nbytes
+        comm.release_transfer(h)
+        h = comm.get_async(back.data_ptr(), "pool", pool.data_ptr(), nbytes)
+        assert comm.wait_transfer(h, 60000) == 0
+        comm.release_transfer(h)
+        torch.cuda.synchronize()
+        assert torch.equal(pool.cuda(), src)
+        assert torch.equal(back, src)
+    finally:
+        comm.shutdown()
+
+
+def test_fabric_scatter_gather_hbm_to_hbm():
+    comm = _fabric_pair()
+    try:
+        n, seg = 4, (8 << 20) + 16
+        src = torch.randint(0, 256, (n * seg,), dtype=torch.uint8, device="cuda")
+        remote = torch.zeros(n * seg, dtype=torch.uint8, device="cuda")
+        back = torch.zeros_like(src)
+        for t in (src, remote, back):
+            assert comm.register_memory(t.data_ptr(), t.numel()) == 0
+        assert comm.publish_buffer(remote.data_ptr(), remote.numel()) == 0
+        port = comm.get_tcp_port()
+        assert comm.connect("peer", "127.0.0.1", port) == 0
+        assert comm.query_remote_buffers("peer", "127.0.0.1", port)
+        torch.cuda.synchronize()
+        hosts = ["peer"] * n
+        # scatter segments in reverse order
+        raddrs = [remote.data_ptr() + (n - 1 - i) * seg for i in range(n)]
+        h = comm.scatter_async(src.data_ptr(), hosts, raddrs, [seg] * n)
+        assert comm.wait_transfer(h, 60000) == 0
+        comm.release_transfer(h)
+        h = comm.gather_async(back.data_ptr(), hosts, raddrs, [seg] * n)
+        assert comm.wait_transfer(h, 60000) == 0
+        comm.release_transfer(h)
+        torch.cuda.synchronize()
+        assert torch.equal(back, src)
+        for i in range(n):
+            assert torch.equal(remote[(n - 1 - i) * seg:(n - i) * seg], src[i * seg:(i + 1) * seg])
+    finally:
+        comm.shutdown()
+
+
+def test_tma_gather_api_with_mapping_and_qos_window():
+    """tmaGather through MPComm with H2D QoS on: the kernel opens and closes its window."""
+    comm = mpcomm.MPComm()
+    assert comm.init("qos") == 0
+    try:
+        comm.enable_h2d_qos(0, 0)
+        pages, bs, n = 256, 65536, 64
+        kv = _pool(pages, bs, seed=11)
+        dram = comm.map_dram_to_gpu(kv.data_ptr(), kv.numel())
+        assert dram
+        idx = torch.tensor(random.Random(1).sample(range(pages), n), dtype=torch.int64, device="cuda")
+        out = torch.empty(n * bs, dtype=torch.uint8, device="cuda")
+        assert comm.tma_gather(dram, idx.data_ptr(), out.data_ptr(), n, bs) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(n, bs).cpu(), kv[idx.cpu()])
+        assert comm.unmap_dram_from_gpu(kv.data_ptr()) == 0
+    finally:
+        comm.shutdown()
