@@ -387,12 +387,15 @@ PYBIND11_MODULE(_mpcomm, m) {
     m.def("paged_gather",
           [](uintptr_t pool, int64_t pool_blocks, uintptr_t idx, uintptr_t out, int64_t n, int64_t bs, int mode,
              int max_ctas, uintptr_t stream) {
-              py::gil_scoped_release r;
               kern::LaunchInfo li;
-              int e = kern::h2d_gather(reinterpret_cast<const void *>(pool), pool_blocks,
+              int e;
+              {
+                  py::gil_scoped_release r;
+                  e = kern::h2d_gather(reinterpret_cast<const void *>(pool), pool_blocks,
                                        reinterpret_cast<const int64_t *>(idx), reinterpret_cast<void *>(out), n, bs,
                                        mode, max_ctas, reinterpret_cast<void *>(stream), nullptr, nullptr, nullptr,
                                        &li);
+              }
               return py::make_tuple(e, li.ctas, li.path);
           },
           py::arg("pool"), py::arg("pool_blocks"), py::arg("indices"), py::arg("out"), py::arg("num_blocks"),
@@ -400,11 +403,14 @@ PYBIND11_MODULE(_mpcomm, m) {
     m.def("paged_scatter",
           [](uintptr_t src, uintptr_t idx, uintptr_t pool, int64_t pool_blocks, int64_t n, int64_t bs, int mode,
              int max_ctas, uintptr_t stream) {
-              py::gil_scoped_release r;
               kern::LaunchInfo li;
-              int e = kern::h2d_scatter(reinterpret_cast<const void *>(src), reinterpret_cast<const int64_t *>(idx),
+              int e;
+              {
+                  py::gil_scoped_release r;
+                  e = kern::h2d_scatter(reinterpret_cast<const void *>(src), reinterpret_cast<const int64_t *>(idx),
                                         reinterpret_cast<void *>(pool), pool_blocks, n, bs, mode, max_ctas,
                                         reinterpret_cast<void *>(stream), nullptr, nullptr, nullptr, &li);
+              }
               return py::make_tuple(e, li.ctas, li.path);
           },
           py::arg("src"), py::arg("indices"), py::arg("pool"), py::arg("pool_blocks"), py::arg("num_blocks"),
