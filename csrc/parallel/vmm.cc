@@ -1,0 +1,198 @@
+#include "parallel/vmm.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <unistd.h>
+
+#include <cstring>
+
+#include "cuda/gpu.h"
+#include "mpcomm_log.h"
+
+namespace mpcomm {
+namespace vmm {
+
+namespace {
+
+template <typename Fn>
+Fn sym(const char *name) {
+    return reinterpret_cast<Fn>(gpu::driver_symbol(name));
+}
+
+constexpr int kNoDriver = CUDA_ERROR_NOT_FOUND;
+
+int cu_device(int ordinal, CUdevice *out) {
+    auto fn = sym<CUresult (*)(CUdevice *, int)>("cuDeviceGet");
+    return fn ? fn(out, ordinal) : kNoDriver;
+}
+
+CUmulticastObjectProp mc_prop(size_t size, int ndev) {
+    CUmulticastObjectProp p;
+    std::memset(&p, 0, sizeof(p));
+    p.numDevices = static_cast<unsigned>(ndev);
+    p.size = size;
+    p.handleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+    return p;
+}
+
+}  // namespace
+
+int ipc_export(const void *ptr, unsigned char handle[64], uint64_t *offset) {
+    gpu::PtrInfo pi;
+    if (!gpu::query_pointer(ptr, &pi) || !pi.is_device || !pi.base) return CUDA_ERROR_INVALID_VALUE;
+    int e = gpu::ipc_get_handle(reinterpret_cast<void *>(pi.base), handle);
+    if (e) return e;
+    *offset = reinterpret_cast<uintptr_t>(ptr) - pi.base;
+    return 0;
+}
+
+int ipc_import(const unsigned char handle[64], void **base) { return gpu::ipc_open_handle(handle, base); }
+
+int ipc_release(void *base) { return gpu::ipc_close(base); }
+
+int multicast_supported(int dev) {
+    auto fn = sym<CUresult (*)(int *, CUdevice_attribute, CUdevice)>("cuDeviceGetAttribute");
+    CUdevice d;
+    if (!fn || cu_device(dev, &d)) return 0;
+    int v = 0;
+    if (fn(&v, CU_DEVICE_ATTRIBUTE_MULTICAST_SUPPORTED, d) != CUDA_SUCCESS) return 0;
+    return v;
+}
+
+int multicast_granularity(size_t size, int ndev, size_t *gran) {
+    auto fn = sym<CUresult (*)(size_t *, const CUmulticastObjectProp *, CUmulticastGranularity_flags)>(
+        "cuMulticastGetGranularity");
+    if (!fn) return kNoDriver;
+    CUmulticastObjectProp p = mc_prop(size, ndev);
+    return fn(gran, &p, CU_MULTICAST_GRANULARITY_MINIMUM);
+}
+
+int multicast_create(size_t size, int ndev, uint64_t *mc, int *fd) {
+    auto create = sym<CUresult (*)(CUmemGenericAllocationHandle *, const CUmulticastObjectProp *)>(
+        "cuMulticastCreate");
+    auto exp = sym<CUresult (*)(void *, CUmemGenericAllocationHandle, CUmemAllocationHandleType,
+                                unsigned long long)>("cuMemExportToShareableHandle");
+    if (!create || !exp) return kNoDriver;
+    CUmulticastObjectProp p = mc_prop(size, ndev);
+    CUmemGenericAllocationHandle h = 0;
+    CUresult r = create(&h, &p);
+    if (r != CUDA_SUCCESS) return r;
+    int f = -1;
+    r = exp(&f, h, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0);
+    if (r != CUDA_SUCCESS) {
+        auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
+        if (rel) rel(h);
+        return r;
+    }
+    *mc = h;
+    *fd = f;
+    return 0;
+}
+
+int multicast_import(int fd, uint64_t *mc) {
+    auto imp = sym<CUresult (*)(CUmemGenericAllocationHandle *, void *, CUmemAllocationHandleType)>(
+        "cuMemImportFromShareableHandle");
+    if (!imp) return kNoDriver;
+    CUmemGenericAllocationHandle h = 0;
+    CUresult r = imp(&h, reinterpret_cast<void *>(static_cast<uintptr_t>(fd)),
+                     CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+    if (r == CUDA_SUCCESS) *mc = h;
+    return r;
+}
+
+int multicast_add_device(uint64_t mc, int dev) {
+    auto fn = sym<CUresult (*)(CUmemGenericAllocationHandle, CUdevice)>("cuMulticastAddDevice");
+    CUdevice d;
+    if (!fn) return kNoDriver;
+    int e = cu_device(dev, &d);
+    return e ? e : fn(mc, d);
+}
+
+namespace {
+
+int map_rw(CUmemGenericAllocationHandle h, size_t size, int dev, void **va) {
+    auto reserve = sym<CUresult (*)(CUdeviceptr *, size_t, size_t, CUdeviceptr, unsigned long long)>(
+        "cuMemAddressReserve");
+    auto map = sym<CUresult (*)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long)>(
+        "cuMemMap");
+    auto access = sym<CUresult (*)(CUdeviceptr, size_t, const CUmemAccessDesc *, size_t)>("cuMemSetAccess");
+    auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
+    auto vfree = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree");
+    if (!reserve || !map || !access || !unmap || !vfree) return kNoDriver;
+    CUdeviceptr p = 0;
+    CUresult r = reserve(&p, size, 0, 0, 0);
+    if (r != CUDA_SUCCESS) return r;
+    r = map(p, size, 0, h, 0);
+    if (r != CUDA_SUCCESS) {
+        vfree(p, size);
+        return r;
+    }
+    CUmemAccessDesc a;
+    std::memset(&a, 0, sizeof(a));
+    a.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    a.location.id = dev;
+    a.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+    r = access(p, size, &a, 1);
+    if (r != CUDA_SUCCESS) {
+        unmap(p, size);
+        vfree(p, size);
+        return r;
+    }
+    *va = reinterpret_cast<void *>(p);
+    return 0;
+}
+
+}  // namespace
+
+int multicast_bind_local(uint64_t mc, size_t size, int dev, uint64_t *mem, void **uc_va) {
+    auto create = sym<CUresult (*)(CUmemGenericAllocationHandle *, size_t, const CUmemAllocationProp *,
+                                   unsigned long long)>("cuMemCreate");
+    auto bind = sym<CUresult (*)(CUmemGenericAllocationHandle, size_t, CUmemGenericAllocationHandle, size_t,
+                                 size_t, unsigned long long)>("cuMulticastBindMem");
+    auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
+    if (!create || !bind || !rel) return kNoDriver;
+    CUmemAllocationProp p;
+    std::memset(&p, 0, sizeof(p));
+    p.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    p.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    p.location.id = dev;
+    p.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;
+    CUmemGenericAllocationHandle h = 0;
+    CUresult r = create(&h, size, &p, 0);
+    if (r != CUDA_SUCCESS) return r;
+    r = bind(mc, 0, h, 0, size, 0);
+    if (r != CUDA_SUCCESS) {
+        rel(h);
+        return r;
+    }
+    int e = map_rw(h, size, dev, uc_va);
+    if (e) {
+        rel(h);
+        return e;
+    }
+    *mem = h;
+    return 0;
+}
+
+int multicast_map(uint64_t mc, size_t size, int dev, void **mc_va) { return map_rw(mc, size, dev, mc_va); }
+
+int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev) {
+    auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
+    auto vfree = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree");
+    auto unbind = sym<CUresult (*)(CUmemGenericAllocationHandle, CUdevice, size_t, size_t)>("cuMulticastUnbind");
+    auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
+    if (!unmap || !vfree || !rel) return kNoDriver;
+    for (void *va : {mc_va, uc_va}) {
+        if (!va) continue;
+        unmap(reinterpret_cast<CUdeviceptr>(va), size);
+        vfree(reinterpret_cast<CUdeviceptr>(va), size);
+    }
+    CUdevice d;
+    if (mc && mem && unbind && cu_device(dev, &d) == 0) unbind(mc, d, 0, size);
+    if (mem) rel(mem);
+    if (mc) rel(mc);
+    return 0;
+}
+
+}  // namespace vmm
+}  // namespace mpcomm

@@ -1,0 +1,47 @@
+// Cross-process GPU memory plumbing for one NVSwitch box.
+//
+//  * CUDA IPC: export/open the allocation that holds a device pointer, so a
+//    peer process can store into it from its own kernels (P2P over NVLink).
+//  * NVLS multicast: a multicast object bound to one physical allocation per
+//    GPU; a kernel's `multimem.st` to the multicast address is replicated by
+//    the NVSwitch into every bound allocation. Handles cross processes as
+//    POSIX file descriptors (the caller passes them over a Unix socket).
+// All driver calls go through cudaGetDriverEntryPoint, so the library still
+// loads without a driver. Every function returns 0 or a CUresult.
+#ifndef MPCOMM_B200_CSRC_PARALLEL_VMM_H_
+#define MPCOMM_B200_CSRC_PARALLEL_VMM_H_
+
+#include <cstddef>
+#include <cstdint>
+
+namespace mpcomm {
+namespace vmm {
+
+// IPC handle (64 bytes) of the allocation containing `ptr`; *offset = ptr - base.
+int ipc_export(const void *ptr, unsigned char handle[64], uint64_t *offset);
+// Maps a peer allocation into this process (peer access enabled lazily).
+int ipc_import(const unsigned char handle[64], void **base);
+int ipc_release(void *base);
+
+// 1 if `dev` supports multicast objects.
+int multicast_supported(int dev);
+// Minimum granularity for a multicast object spanning `ndev` devices.
+int multicast_granularity(size_t size, int ndev, size_t *gran);
+// Creates a multicast object (root only) and exports it as a POSIX fd.
+int multicast_create(size_t size, int ndev, uint64_t *mc, int *fd);
+// Imports an exported multicast object from its fd.
+int multicast_import(int fd, uint64_t *mc);
+// Adds `dev` to the object (every participant, before any bind).
+int multicast_add_device(uint64_t mc, int dev);
+// Allocates `size` bytes on `dev`, binds them to the multicast object at
+// offset 0 and maps them at a unicast address (*uc_va, readable by `dev`).
+int multicast_bind_local(uint64_t mc, size_t size, int dev, uint64_t *mem, void **uc_va);
+// Maps the multicast object itself (*mc_va: target of multimem stores).
+int multicast_map(uint64_t mc, size_t size, int dev, void **mc_va);
+// Unmaps/unbinds/releases everything created above (any argument may be 0).
+int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev);
+
+}  // namespace vmm
+}  // namespace mpcomm
+
+#endif  // MPCOMM_B200_CSRC_PARALLEL_VMM_H_

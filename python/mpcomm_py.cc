@@ -10,8 +10,10 @@
 #include <string>
 #include <vector>
 
+#include "cuda/gpu.h"
 #include "kernels/launch.h"
 #include "mpcomm.h"
+#include "parallel/vmm.h"
 #include "transport/loopback_hooks.h"
 
 namespace py = pybind11;
@@ -466,6 +468,66 @@ PYBIND11_MODULE(_mpcomm, m) {
           py::arg("flag"), py::arg("value"), py::arg("budget_ns"), py::arg("stream") = 0, py::arg("status") = 0);
     m.def("kernel_launch_count", [] { return kern::launch_count(); });
     m.def("kernel_wait_budget_ns", [] { return kern::wait_budget_ns(); });
+
+    // ---- cross-process GPU memory (mpcomm.parallel) ----
+    m.def("ipc_export", [](uintptr_t ptr) {
+        unsigned char h[64] = {0};
+        uint64_t off = 0;
+        int e = vmm::ipc_export(reinterpret_cast<const void *>(ptr), h, &off);
+        return py::make_tuple(e, py::bytes(reinterpret_cast<const char *>(h), 64), off);
+    });
+    m.def("ipc_import", [](py::bytes handle) -> py::tuple {
+        std::string s = handle;
+        if (s.size() != 64) return py::make_tuple(static_cast<int>(MPCOMM_ERR_INVALID_ARG), 0);
+        void *base = nullptr;
+        int e = vmm::ipc_import(reinterpret_cast<const unsigned char *>(s.data()), &base);
+        return py::make_tuple(e, reinterpret_cast<uintptr_t>(base));
+    });
+    m.def("ipc_release", [](uintptr_t base) { return vmm::ipc_release(reinterpret_cast<void *>(base)); });
+    m.def("host_register", [](uintptr_t ptr, size_t len) {
+        void *d = nullptr;
+        bool pinned = false;
+        int e;
+        {
+            py::gil_scoped_release r;
+            e = gpu::host_pin_mapped(reinterpret_cast<void *>(ptr), len, &d, &pinned);
+        }
+        return py::make_tuple(e, reinterpret_cast<uintptr_t>(d), pinned);
+    });
+    m.def("host_unregister", [](uintptr_t ptr) { return gpu::host_unpin(reinterpret_cast<void *>(ptr)); });
+    m.def("multicast_supported", &vmm::multicast_supported, py::arg("device"));
+    m.def("multicast_granularity", [](size_t size, int ndev) {
+        size_t g = 0;
+        int e = vmm::multicast_granularity(size, ndev, &g);
+        return py::make_tuple(e, g);
+    });
+    m.def("multicast_create", [](size_t size, int ndev) {
+        uint64_t mc = 0;
+        int fd = -1;
+        int e = vmm::multicast_create(size, ndev, &mc, &fd);
+        return py::make_tuple(e, mc, fd);
+    });
+    m.def("multicast_import", [](int fd) {
+        uint64_t mc = 0;
+        int e = vmm::multicast_import(fd, &mc);
+        return py::make_tuple(e, mc);
+    });
+    m.def("multicast_add_device", &vmm::multicast_add_device, py::arg("mc"), py::arg("device"));
+    m.def("multicast_bind_local", [](uint64_t mc, size_t size, int dev) {
+        uint64_t mem = 0;
+        void *va = nullptr;
+        int e = vmm::multicast_bind_local(mc, size, dev, &mem, &va);
+        return py::make_tuple(e, mem, reinterpret_cast<uintptr_t>(va));
+    });
+    m.def("multicast_map", [](uint64_t mc, size_t size, int dev) {
+        void *va = nullptr;
+        int e = vmm::multicast_map(mc, size, dev, &va);
+        return py::make_tuple(e, reinterpret_cast<uintptr_t>(va));
+    });
+    m.def("multicast_teardown", [](uint64_t mc, uint64_t mem, uintptr_t uc, uintptr_t mcva, size_t size, int dev) {
+        return vmm::multicast_teardown(mc, mem, reinterpret_cast<void *>(uc), reinterpret_cast<void *>(mcva), size,
+                                       dev);
+    });
 
     // ---- host-side fault hooks of the loopback fabric (tests) ----
     m.def("_lo_inject_wc_errors", &fabric::loopback_inject_wc_errors, py::arg("gid"), py::arg("count"));

@@ -1,0 +1,150 @@
+"""Multi-GPU test cases, one process per GPU (run by tests/test_multigpu.py
+under torch.distributed.run). Each case verifies bit-exactly and exits
+non-zero on any mismatch.
+
+  putget  GPU fabric PUT/GET/scatter between processes: rank r writes into
+          rank r^1's published HBM buffer over NVLink (CUDA IPC).
+  pxn     fused gather + forward: pages of a host pool shared by all ranks are
+          gathered by rank (r+1)%N and stored into rank r's HBM; a done flag
+          lands in rank r's memory.
+  nvls    NVLS multicast broadcast from rank 0 (falls back to P2P fan-out
+          where multicast is unavailable) of a rollout-style batch.
+"""
+import argparse
+import os
+import sys
+import zlib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import mpcomm  # noqa: E402
+from mpcomm import ops, parallel  # noqa: E402
+
+
+def case_putget(rank, world):
+    peer = rank ^ 1
+    if peer >= world:
+        return
+    n = (48 << 20) + 64
+    mine = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda",
+                         generator=torch.Generator(device="cuda").manual_seed(100 + rank))
+    inbox = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    back = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    comm = mpcomm.MPComm()
+    assert comm.init(f"r{rank}") == 0 and comm.get_fabric_name() == "nvl"
+    assert comm.start_accept_thread() == 0
+    for t in (mine, inbox, back):
+        assert comm.register_memory(t.data_ptr(), t.numel()) == 0
+    assert comm.publish_buffer(inbox.data_ptr(), n) == 0
+    ports = [None] * world
+    dist.all_gather_object(ports, comm.get_tcp_port())
+    dist.barrier()
+    assert comm.connect("peer", "127.0.0.1", ports[peer]) == 0
+    info = comm.query_remote_buffers("peer", "127.0.0.1", ports[peer])
+    remote = info["buffers"][0]["addr"]
+    torch.cuda.synchronize()
+    h = comm.put_async(mine.data_ptr(), "peer", remote, n)
+    assert comm.wait_transfer(h, 60000) == 0, "cross-process PUT failed"
+    comm.release_transfer(h)
+    dist.barrier()  # both PUTs done
+    crcs = [None] * world
+    dist.all_gather_object(crcs, (zlib.crc32(mine.cpu().numpy().tobytes()),
+                                  zlib.crc32(inbox.cpu().numpy().tobytes())))
+    assert crcs[rank][1] == crcs[peer][0], "peer data did not arrive intact"
+    h = comm.get_async(back.data_ptr(), "peer", remote, n)
+    assert comm.wait_transfer(h, 60000) == 0, "cross-process GET failed"
+    comm.release_transfer(h)
+    torch.cuda.synchronize()
+    assert torch.equal(back, mine)  # what we wrote to the peer reads back
+    dist.barrier()
+    comm.shutdown()
+
+
+def case_pxn(rank, world):
+    bs, pages, n = 65536, 4096, 256
+    name = "mpcomm-test-pxn"
+    if rank == 0:
+        pool = parallel.SharedHostPool(name, pages * bs, create=True)
+        g = torch.Generator().manual_seed(7)
+        pool.tensor.copy_(torch.randint(0, 256, (pages * bs,), dtype=torch.uint8, generator=g))
+    dist.barrier()
+    if rank != 0:
+        pool = parallel.SharedHostPool(name, pages * bs, create=False)
+    dist.barrier()
+    bufs = parallel.PeerBuffers(n * bs)
+    flags = parallel.PeerBuffers(64)
+    ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # what every rank wants
+    wants = [torch.randperm(pages, generator=torch.Generator().manual_seed(3 + r))[:n] for r in range(world)]
+    requester = (rank - 1) % world  # this rank gathers for requester
+    idx = wants[requester].cuda()
+    dist.barrier()
+    ops.pxn_gather_forward(pool.dev_ptr, pages, idx, bufs.ptrs[requester], bs,
+                           done_flag=flags.ptrs[requester], flag_value=42, counter=ctr.data_ptr())
+    torch.cuda.synchronize()
+    dist.barrier()
+    got = bufs.local.view(n, bs).cpu()
+    ref = pool.tensor.view(pages, bs)[wants[rank]]
+    assert torch.equal(got, ref), "forwarded pages differ"
+    assert flags.local.view(torch.int64)[0].item() == 42, "done flag not published"
+    dist.barrier()
+    bufs.close()
+    flags.close()
+    pool.close(unlink=(rank == 0))
+
+
+def case_nvls(rank, world):
+    nbytes = 8 << 20
+    src = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda",
+                        generator=torch.Generator(device="cuda").manual_seed(5))
+    try:
+        grp = parallel.NvlsGroup(nbytes)
+        used = "nvls"
+    except RuntimeError as e:
+        grp = None
+        used = f"fanout ({e})"
+    if grp is not None:
+        grp.uc[:nbytes].zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 0:
+            ops.nvls_broadcast(src, grp.mc_ptr, nbytes)
+            torch.cuda.synchronize()
+        dist.barrier()
+        assert torch.equal(grp.uc[:nbytes], src), "NVLS broadcast mismatch"
+        dist.barrier()
+        grp.close()
+    bufs = parallel.PeerBuffers(nbytes)
+    dist.barrier()
+    if rank == 0:
+        ops.p2p_fanout(src, [bufs.ptrs[r] for r in range(1, world)], nbytes)
+        torch.cuda.synchronize()
+    dist.barrier()
+    if rank != 0:
+        assert torch.equal(bufs.local, src), "P2P fan-out mismatch"
+    dist.barrier()
+    bufs.close()
+    if rank == 0:
+        print(f"nvls case used: {used}", flush=True)
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("case", choices=["putget", "pxn", "nvls", "all"])
+    a = p.parse_args()
+    rank, world, _ = parallel.init_from_env("gloo")
+    cases = ["putget", "pxn", "nvls"] if a.case == "all" else [a.case]
+    for c in cases:
+        globals()[f"case_{c}"](rank, world)
+        if rank == 0:
+            print(f"case {c} ok", flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
