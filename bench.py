@@ -170,22 +170,30 @@ def main():
     torch.cuda.synchronize()
     assert torch.equal(crc_src, crc_dst), "PUT/GET round trip corrupted data"
 
-    # Copy-engine roofline of the same path (cudaMemcpyAsync, timing only).
+    # Copy-engine roofline of the same path (cudaMemcpyAsync; timing only),
+    # run on every rank at once so it includes the host-memory ceiling the
+    # ranks share; aggregate = world * bytes / max-over-ranks time.
     ce = []
     s_ce = torch.cuda.Stream(device=dev)
     for d2h in (True, False):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(s_ce):
-            for it in range(3):
-                if it == 2:
-                    a.record(s_ce)
+            (pool.copy_(src, non_blocking=True) if d2h else dst.copy_(pool, non_blocking=True))
+        s_ce.synchronize()
+        barrier()
+        with torch.cuda.stream(s_ce):
+            a.record(s_ce)
+            for _ in range(2):
                 if d2h:
                     pool.copy_(src, non_blocking=True)
                 else:
                     dst.copy_(pool, non_blocking=True)
             b.record(s_ce)
         s_ce.synchronize()
-        ce.append(total / (a.elapsed_time(b) * 1e-3) / 1e9)
+        t = torch.tensor([a.elapsed_time(b) / 2], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ce.append(world * total / (t.item() * 1e-3) / 1e9)
 
     # ---- device-timed region ----
     launches0 = mpcomm.MPComm.get_kernel_launch_count()
@@ -263,11 +271,14 @@ def main():
             "put_gbs": round(world * total / (put_ms * 1e-3) / 1e9, 3),
             "get_gbs": round(world * total / (get_ms * 1e-3) / 1e9, 3),
             "roofline": {
-                "what": "copy-engine cudaMemcpyAsync on the same pinned buffers (per GPU)",
+                "what": "copy-engine cudaMemcpyAsync on the same pinned buffers, all ranks at once "
+                        "(aggregate GB/s)",
                 "ce_d2h_gbs": round(ce[0], 3),
                 "ce_h2d_gbs": round(ce[1], 3),
-                "put_frac": round(total / (put_ms * 1e-3) / 1e9 / ce[0], 4),
-                "get_frac": round(total / (get_ms * 1e-3) / 1e9 / ce[1], 4),
+                "put_frac": round(world * total / (put_ms * 1e-3) / 1e9 / ce[0], 4),
+                "get_frac": round(world * total / (get_ms * 1e-3) / 1e9 / ce[1], 4),
+                "step_frac": round(2 * world * total / (ms * 1e-3) / 1e9 /
+                                   (2 / (1 / ce[0] + 1 / ce[1])), 4),
             },
             "clocks": {"sm_mhz": cs["sm_mhz"], "sm_max_mhz": cs["sm_max_mhz"], "reasons": cs["reasons"]},
             "gpu_launches": int(launches),

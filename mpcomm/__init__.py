@@ -45,6 +45,19 @@ except ImportError as _e:  # pragma: no cover - exercised only on broken install
     ) from _e
 
 
+_SUBPACKAGES = ("ops", "parallel", "models", "utils", "bench")
+
+
+def __getattr__(name):
+    # Subpackages import torch; load them on first use so `import mpcomm`
+    # stays light for C-API-style users.
+    if name in _SUBPACKAGES:
+        import importlib
+
+        return importlib.import_module(f".{name}", __name__)
+    raise AttributeError(f"module 'mpcomm' has no attribute {name!r}")
+
+
 def native_library_path() -> str:
     """Absolute path of the loaded native module (for provenance checks)."""
     return _native.__file__
