@@ -6,12 +6,19 @@
 //     R(A || B) = shift(R(A), |B|) ^ R(B),  shift(c, L) = c * x^(8L) mod P
 //     CRC(M)    = shift(0xFFFFFFFF, |M|) ^ R(M) ^ 0xFFFFFFFF.
 // This is the polynomial-combination identity behind zlib's crc32_combine
-// (Mark Adler); the code below is written from the algebra. Each thread
-// computes R() of a 2 KiB segment with slicing-by-4 tables held in shared
-// memory, a CTA folds its 256 segments (512 KiB piece) with a shuffle/shared
-// memory tree, and a finalize pass folds the pieces of each block.
-// Multiplication by x^(8*2^k) uses a 41-entry table of powers, so a shift
-// costs popcount(L) carry-less multiplies.
+// (Mark Adler); the code below is written from the algebra.
+//
+// Kernel layout. A CTA of 256 threads owns a 256 KiB piece of a block; each
+// thread computes R() of its 1 KiB segment as two independent 512 B streams
+// (two dependency chains in flight) with slicing-by-4 tables, then the
+// segments are folded by a shuffle tree and across warps. Shared-memory
+// lookups use 8 bank-interleaved copies of every table (lane l reads copy
+// l % 8), so only the 4 lanes sharing a copy can collide on a bank. A
+// finalize kernel folds the pieces of each block with one CTA per block:
+// each thread folds a contiguous run of pieces (one multiply per piece by
+// x^(8 * 256 KiB)), then a tree combines the runs. Multiplication by
+// x^(8*2^k) uses a 41-entry table of powers, so a shift costs popcount(L)
+// carry-less multiplies.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -25,8 +32,12 @@ namespace {
 
 constexpr uint32_t kPoly = 0xEDB88320u;
 constexpr int kCrcThreads = 256;
-constexpr uint32_t kSegBytes = 2048;
-constexpr uint64_t kPieceBytes = static_cast<uint64_t>(kCrcThreads) * kSegBytes;
+constexpr uint32_t kHalfBytes = 512;            // one dependency chain
+constexpr uint32_t kSegBytes = 2 * kHalfBytes;  // per thread
+constexpr uint64_t kPieceBytes = static_cast<uint64_t>(kCrcThreads) * kSegBytes;  // 256 KiB
+constexpr int kPieceLog2 = 18;
+constexpr int kCopies = 8;
+constexpr int kFinThreads = 256;
 
 struct Powers {
     uint32_t x[41];  // x[k] = x^(8 * 2^k) mod P, reflected
@@ -59,56 +70,93 @@ Powers make_powers() {
     return p;
 }
 
+// Table T[s][e] replicated kCopies times: word ((s * 256 + e) * kCopies + c).
+__device__ __forceinline__ uint32_t lookup(const uint32_t *tab, int s, uint32_t e, int c) {
+    return tab[((s * 256 + e) << 3) + c];
+}
+
+__device__ __forceinline__ uint32_t step4(const uint32_t *tab, uint32_t c, uint32_t w, int cp) {
+    c ^= w;
+    return lookup(tab, 3, c & 0xFFu, cp) ^ lookup(tab, 2, (c >> 8) & 0xFFu, cp) ^
+           lookup(tab, 1, (c >> 16) & 0xFFu, cp) ^ lookup(tab, 0, c >> 24, cp);
+}
+
+// R() of [p, p+len) (len <= kHalfBytes). Vector loads when 16-byte aligned.
+__device__ __forceinline__ uint32_t crc_span(const uint32_t *tab, const unsigned char *p, uint32_t len, int cp) {
+    uint32_t c = 0, i = 0;
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+        for (; i + 16 <= len; i += 16) {
+            const int4 v = *reinterpret_cast<const int4 *>(p + i);
+            c = step4(tab, c, static_cast<uint32_t>(v.x), cp);
+            c = step4(tab, c, static_cast<uint32_t>(v.y), cp);
+            c = step4(tab, c, static_cast<uint32_t>(v.z), cp);
+            c = step4(tab, c, static_cast<uint32_t>(v.w), cp);
+        }
+    }
+    for (; i < len; ++i) c = (c >> 8) ^ lookup(tab, 0, (c ^ p[i]) & 0xFFu, cp);
+    return c;
+}
+
 __global__ void __launch_bounds__(kCrcThreads)
     crc_pieces_kernel(const unsigned char *__restrict__ data, int64_t bs, int64_t ppb,
                       uint32_t *__restrict__ piece_crc, const __grid_constant__ Powers pw) {
-    __shared__ uint32_t tab[4][256];
+    __shared__ uint32_t tab[4 * 256 * kCopies];  // 32 KiB
+    __shared__ uint32_t t0[256];
     __shared__ uint32_t warp_crc[kCrcThreads / 32];
     __shared__ uint32_t warp_len[kCrcThreads / 32];
     const int tid = threadIdx.x;
     {
         uint32_t c = static_cast<uint32_t>(tid);
         for (int k = 0; k < 8; ++k) c = (c & 1u) ? (c >> 1) ^ kPoly : (c >> 1);
-        tab[0][tid] = c;
+        t0[tid] = c;
     }
     __syncthreads();
     {
-        uint32_t c = tab[0][tid];
-        for (int s = 1; s < 4; ++s) {
-            c = (c >> 8) ^ tab[0][c & 0xFFu];
-            tab[s][tid] = c;
+        uint32_t c = t0[tid];
+        for (int s = 0; s < 4; ++s) {
+            if (s) c = (c >> 8) ^ t0[c & 0xFFu];
+#pragma unroll
+            for (int k = 0; k < kCopies; ++k) tab[((s * 256 + tid) << 3) + k] = c;
         }
     }
     __syncthreads();
 
+    const int cp = tid & (kCopies - 1);
     const int64_t block = blockIdx.y;
     const int64_t piece = blockIdx.x;
     const int64_t piece_off = piece * static_cast<int64_t>(kPieceBytes);
     int64_t piece_len = bs - piece_off;
     if (piece_len > static_cast<int64_t>(kPieceBytes)) piece_len = kPieceBytes;
-    const unsigned char *base = data + block * bs + piece_off;
+    const unsigned char *base = data + block * bs + piece_off + static_cast<int64_t>(tid) * kSegBytes;
 
-    const int64_t s0 = static_cast<int64_t>(tid) * kSegBytes;
-    int64_t slen = piece_len - s0;
-    if (slen < 0) slen = 0;
-    if (slen > kSegBytes) slen = kSegBytes;
-    uint32_t c = 0;
-    const unsigned char *p = base + s0;
-    int64_t i = 0;
-    if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
-        for (; i + 16 <= slen; i += 16) {
-            const int4 v = *reinterpret_cast<const int4 *>(p + i);
-            const uint32_t w[4] = {static_cast<uint32_t>(v.x), static_cast<uint32_t>(v.y),
-                                   static_cast<uint32_t>(v.z), static_cast<uint32_t>(v.w)};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                c ^= w[q];
-                c = tab[3][c & 0xFFu] ^ tab[2][(c >> 8) & 0xFFu] ^ tab[1][(c >> 16) & 0xFFu] ^
-                    tab[0][c >> 24];
-            }
+    int64_t slen = piece_len - static_cast<int64_t>(tid) * kSegBytes;
+    slen = slen < 0 ? 0 : (slen > kSegBytes ? kSegBytes : slen);
+    const uint32_t la = static_cast<uint32_t>(slen < kHalfBytes ? slen : kHalfBytes);
+    const uint32_t lb = static_cast<uint32_t>(slen) - la;
+    // Two independent chains interleaved by the compiler's scheduler.
+    uint32_t ca, cb;
+    if (la == kHalfBytes && lb == kHalfBytes && (reinterpret_cast<uintptr_t>(base) & 15u) == 0) {
+        ca = 0;
+        cb = 0;
+        const unsigned char *pb = base + kHalfBytes;
+#pragma unroll 2
+        for (uint32_t i = 0; i < kHalfBytes; i += 16) {
+            const int4 va = *reinterpret_cast<const int4 *>(base + i);
+            const int4 vb = *reinterpret_cast<const int4 *>(pb + i);
+            ca = step4(tab, ca, static_cast<uint32_t>(va.x), cp);
+            cb = step4(tab, cb, static_cast<uint32_t>(vb.x), cp);
+            ca = step4(tab, ca, static_cast<uint32_t>(va.y), cp);
+            cb = step4(tab, cb, static_cast<uint32_t>(vb.y), cp);
+            ca = step4(tab, ca, static_cast<uint32_t>(va.z), cp);
+            cb = step4(tab, cb, static_cast<uint32_t>(vb.z), cp);
+            ca = step4(tab, ca, static_cast<uint32_t>(va.w), cp);
+            cb = step4(tab, cb, static_cast<uint32_t>(vb.w), cp);
         }
+    } else {
+        ca = crc_span(tab, base, la, cp);
+        cb = crc_span(tab, base + la, lb, cp);
     }
-    for (; i < slen; ++i) c = (c >> 8) ^ tab[0][(c ^ p[i]) & 0xFFu];
+    uint32_t c = gf2_shift(ca, lb, pw.x) ^ cb;
 
     // Fold segments in order: (crc, len) pairs, left absorbs right.
     uint32_t len = static_cast<uint32_t>(slen);
@@ -134,18 +182,48 @@ __global__ void __launch_bounds__(kCrcThreads)
     }
 }
 
-__global__ void crc_finalize_kernel(const uint32_t *__restrict__ piece_crc, int64_t n, int64_t bs,
-                                    int64_t ppb, uint32_t *__restrict__ out,
-                                    const __grid_constant__ Powers pw) {
-    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (b >= n) return;
-    uint32_t acc = 0;
-    for (int64_t p = 0; p < ppb; ++p) {
-        int64_t len = bs - p * static_cast<int64_t>(kPieceBytes);
-        if (len > static_cast<int64_t>(kPieceBytes)) len = kPieceBytes;
-        acc = gf2_shift(acc, static_cast<uint64_t>(len), pw.x) ^ piece_crc[b * ppb + p];
+// One CTA per block: thread t folds pieces [t*k, (t+1)*k) in order, then the
+// runs are folded by a shuffle tree and across warps.
+__global__ void __launch_bounds__(kFinThreads)
+    crc_finalize_kernel(const uint32_t *__restrict__ piece_crc, int64_t n, int64_t bs, int64_t ppb,
+                        uint32_t *__restrict__ out, const __grid_constant__ Powers pw) {
+    __shared__ uint32_t wc[kFinThreads / 32];
+    __shared__ uint64_t wl[kFinThreads / 32];
+    const int64_t b = blockIdx.x;
+    const int tid = threadIdx.x;
+    const int64_t per = (ppb + kFinThreads - 1) / kFinThreads;
+    const int64_t p0 = tid * per, p1 = p0 + per < ppb ? p0 + per : ppb;
+    uint32_t c = 0;
+    uint64_t len = 0;
+    for (int64_t p = p0; p < p1; ++p) {
+        int64_t l = bs - p * static_cast<int64_t>(kPieceBytes);
+        if (l > static_cast<int64_t>(kPieceBytes)) l = kPieceBytes;
+        // all pieces but the block's last are exactly 2^18 bytes: one multiply
+        c = (l == static_cast<int64_t>(kPieceBytes) ? gf2_mul(c, pw.x[kPieceLog2])
+                                                      : gf2_shift(c, static_cast<uint64_t>(l), pw.x)) ^
+            piece_crc[b * ppb + p];
+        len += static_cast<uint64_t>(l);
     }
-    out[b] = gf2_shift(0xFFFFFFFFu, static_cast<uint64_t>(bs), pw.x) ^ acc ^ 0xFFFFFFFFu;
+    const int lane = tid & 31;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+        const uint32_t oc = __shfl_down_sync(0xffffffffu, c, 1 << k);
+        const uint64_t ol = __shfl_down_sync(0xffffffffu, len, 1 << k);
+        if ((lane & ((2 << k) - 1)) == 0) {
+            c = gf2_shift(c, ol, pw.x) ^ oc;
+            len += ol;
+        }
+    }
+    if (lane == 0) {
+        wc[tid >> 5] = c;
+        wl[tid >> 5] = len;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t acc = 0;
+        for (int w = 0; w < kFinThreads / 32; ++w) acc = gf2_shift(acc, wl[w], pw.x) ^ wc[w];
+        out[b] = gf2_shift(0xFFFFFFFFu, static_cast<uint64_t>(bs), pw.x) ^ acc ^ 0xFFFFFFFFu;
+    }
 }
 
 const Powers &powers() {
@@ -173,9 +251,7 @@ int crc32_blocks_scratch(const void *data, int64_t n, int64_t bs, uint32_t *out,
     note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int fin_threads = 128;
-    crc_finalize_kernel<<<static_cast<unsigned>((n + fin_threads - 1) / fin_threads), fin_threads, 0,
-                          st>>>(scratch, n, bs, ppb, out, powers());
+    crc_finalize_kernel<<<static_cast<unsigned>(n), kFinThreads, 0, st>>>(scratch, n, bs, ppb, out, powers());
     note_launch();
     return cudaGetLastError();
 }
@@ -194,7 +270,7 @@ int crc32_blocks(const void *data, int64_t n, int64_t bs, uint32_t *out, void *s
         std::lock_guard<std::mutex> g(mu);
         if (caps[dev] < need) {
             // The old buffer may still be read by queued work on another
-            // stream, so it is not freed; it is small (4 bytes / 512 KiB).
+            // stream, so it is not freed; it is small (4 bytes / 256 KiB).
             void *p = nullptr;
             cudaError_t e = cudaMalloc(&p, need * sizeof(uint32_t));
             if (e != cudaSuccess) return e;
