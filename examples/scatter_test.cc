@@ -1,0 +1,199 @@
+// scatter_test — PUT/GET/scatter/gather/broadcast bandwidth tool over the
+// MPComm C++ API (parity: reference user_examples/scatter_test.cpp, the tool
+// behind its README numbers; option names kept where they overlap).
+//
+//   target:     scatter_test --mode target --host-id T --tcp-port 5000 --buffer-size 4G [--gpu 0]
+//   initiator:  scatter_test --target T:10.0.0.2:5000 --size 1G --batch-size 4 \
+//                            --test-type put,get --iterations 10 --warmup 3 [--gpu 0]
+//   both:       scatter_test --mode both --buffer-size 4G --size 1G ...  (serves its own
+//               buffer and targets itself: the single-box memory-pool setup)
+// GB/s = bytes / 1e9 / wall seconds of the timed iterations (as the reference).
+// --gpu N puts the local (and served) buffers in HBM of GPU N (cudaMalloc).
+#include <cuda_runtime.h>
+#include <unistd.h>
+
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <random>
+#include <sstream>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "mpcomm.h"
+
+namespace {
+
+struct Target {
+    std::string id, addr;
+    int port = 0;
+};
+
+size_t parse_size(const std::string &s) {
+    char *end = nullptr;
+    double v = std::strtod(s.c_str(), &end);
+    size_t mul = 1;
+    if (end && *end) {
+        switch (*end) {
+            case 'K': case 'k': mul = 1ull << 10; break;
+            case 'M': case 'm': mul = 1ull << 20; break;
+            case 'G': case 'g': mul = 1ull << 30; break;
+            case 'T': case 't': mul = 1ull << 40; break;
+            default: break;
+        }
+    }
+    return static_cast<size_t>(v * static_cast<double>(mul));
+}
+
+std::vector<std::string> split(const std::string &s, char d) {
+    std::vector<std::string> out;
+    std::stringstream ss(s);
+    std::string p;
+    while (std::getline(ss, p, d))
+        if (!p.empty()) out.push_back(p);
+    return out;
+}
+
+void *alloc_buf(size_t n, int gpu) {
+    if (gpu >= 0) {
+        void *p = nullptr;
+        cudaSetDevice(gpu);
+        if (cudaMalloc(&p, n) != cudaSuccess) return nullptr;
+        cudaMemset(p, 0x5A, n);
+        cudaDeviceSynchronize();
+        return p;
+    }
+    void *p = nullptr;
+    if (posix_memalign(&p, 1 << 21, n)) return nullptr;
+    std::memset(p, 0x5A, n);
+    return p;
+}
+
+void usage(const char *prog) {
+    std::printf(
+        "Usage: %s [--mode initiator|target|both] [--host-id ID] [--device DEVS] [--tcp-port P]\n"
+        "          [--target ID:ADDR:PORT]... [--size S] [--buffer-size S] [--batch-size B]\n"
+        "          [--iterations N] [--warmup W] [--test-type put,get,scatter,gather,broadcast]\n"
+        "          [--gpu N] [--wait-go-file PATH] [--verbose]\n"
+        "Sizes take K/M/G/T suffixes. Fabric: MPCOMM_FABRIC (auto|nvl|ib|sock|lo).\n",
+        prog);
+}
+
+}  // namespace
+
+int main(int argc, char **argv) {
+    std::string mode = "initiator", host_id = "test:0", devices, tests = "put,get", go_file;
+    int tcp_port = 0, iters = 10, warmup = 3, gpu = -1;
+    size_t size = 1ull << 30, buf_size = 0, batch = 4;
+    bool verbose = false;
+    std::vector<Target> targets;
+    for (int i = 1; i < argc; ++i) {
+        std::string a = argv[i];
+        auto next = [&]() -> std::string { return i + 1 < argc ? argv[++i] : std::string(); };
+        if (a == "--mode") mode = next();
+        else if (a == "--host-id") host_id = next();
+        else if (a == "--device") devices = next();
+        else if (a == "--tcp-port") tcp_port = std::atoi(next().c_str());
+        else if (a == "--target") {
+            auto f = split(next(), ':');
+            if (f.size() < 3) return usage(argv[0]), 2;
+            targets.push_back(Target{f[0], f[1], std::atoi(f[2].c_str())});
+        } else if (a == "--size") size = parse_size(next());
+        else if (a == "--buffer-size") buf_size = parse_size(next());
+        else if (a == "--batch-size") batch = std::strtoul(next().c_str(), nullptr, 10);
+        else if (a == "--iterations") iters = std::atoi(next().c_str());
+        else if (a == "--warmup") warmup = std::atoi(next().c_str());
+        else if (a == "--test-type") tests = next();
+        else if (a == "--gpu") gpu = std::atoi(next().c_str());
+        else if (a == "--wait-go-file") go_file = next();
+        else if (a == "--verbose" || a == "-v") verbose = true;
+        else if (a == "--help" || a == "-h") return usage(argv[0]), 0;
+        else return usage(argv[0]), 2;
+    }
+    if (batch == 0) batch = 1;
+    if (gpu >= 0) cudaSetDevice(gpu);
+    mpcomm::MPComm comm;
+    if (comm.init(host_id, devices, tcp_port) != 0) return std::fprintf(stderr, "init failed\n"), 1;
+    std::printf("[scatter_test] host %s fabric %s rails %zu tcp %d\n", host_id.c_str(),
+                comm.getFabricName().c_str(), comm.getNumNics(), comm.getTcpPort());
+
+    void *served = nullptr;
+    if (mode == "target" || mode == "both") {
+        if (!buf_size) buf_size = size * batch;
+        served = alloc_buf(buf_size, gpu);
+        if (!served || comm.registerMemory(served, buf_size) || comm.publishBuffer(served, buf_size))
+            return std::fprintf(stderr, "serving buffer failed\n"), 1;
+        comm.startAcceptThread();
+        std::printf("[scatter_test] serving %zu bytes at %p (ready)\n", buf_size, served);
+        std::fflush(stdout);
+        if (mode == "target") {
+            for (;;) {
+                std::this_thread::sleep_for(std::chrono::seconds(verbose ? 5 : 60));
+                if (verbose) std::printf("[scatter_test] published=%zu\n", comm.getPublishedBufferCount());
+            }
+        }
+        targets.push_back(Target{"self", "127.0.0.1", comm.getTcpPort()});
+    }
+    if (targets.empty()) return usage(argv[0]), 2;
+    if (!go_file.empty())
+        while (access(go_file.c_str(), F_OK) != 0) std::this_thread::sleep_for(std::chrono::milliseconds(50));
+
+    std::vector<uintptr_t> remote;
+    for (auto &t : targets) {
+        int rc = -1;
+        for (int attempt = 0; attempt < 30 && rc != 0; ++attempt) {
+            rc = comm.connect(t.id, t.addr, t.port);
+            if (rc) std::this_thread::sleep_for(std::chrono::milliseconds(500));
+        }
+        mpcomm::RemoteBufferEntry e;
+        if (rc || comm.queryRemoteBufferByNuma(t.id, t.addr, t.port, -1, e))
+            return std::fprintf(stderr, "connect/query %s failed\n", t.id.c_str()), 1;
+        if (e.length < size * batch) return std::fprintf(stderr, "remote buffer too small\n"), 1;
+        remote.push_back(e.addr);
+    }
+    const size_t local_bytes = size * batch * targets.size();
+    void *local = alloc_buf(local_bytes, gpu);
+    if (!local || comm.registerMemory(local, local_bytes)) return std::fprintf(stderr, "local buffer failed\n"), 1;
+    const uintptr_t lp = reinterpret_cast<uintptr_t>(local);
+
+    for (const std::string &tt : split(tests, ',')) {
+        auto one_round = [&]() -> int {
+            std::vector<mpcomm::TransferHandle> hs;
+            for (size_t b = 0; b < batch; ++b) {
+                for (size_t t = 0; t < targets.size(); ++t) {
+                    const uintptr_t l = lp + (t * batch + b) * size;
+                    const uintptr_t r = remote[t] + b * size;
+                    mpcomm::TransferHandle h = mpcomm::INVALID_TRANSFER_HANDLE;
+                    if (tt == "put") h = comm.putAsync(l, targets[t].id, r, size);
+                    else if (tt == "get") h = comm.getAsync(l, targets[t].id, r, size);
+                    else if (tt == "scatter") h = comm.scatterAsync(l, {targets[t].id}, {r}, {size});
+                    else if (tt == "gather") h = comm.gatherAsync(l, {targets[t].id}, {r}, {size});
+                    else if (tt == "broadcast") h = comm.broadcastAsync(lp, size, {targets[t].id}, {r});
+                    if (h == mpcomm::INVALID_TRANSFER_HANDLE) return -1;
+                    hs.push_back(h);
+                }
+            }
+            int rc = 0;
+            for (auto h : hs) {
+                rc |= comm.waitTransfer(h, 600000);
+                comm.releaseTransfer(h);
+            }
+            return rc;
+        };
+        for (int w = 0; w < warmup; ++w)
+            if (one_round()) return std::fprintf(stderr, "%s warm-up failed\n", tt.c_str()), 1;
+        auto t0 = std::chrono::steady_clock::now();
+        for (int i = 0; i < iters; ++i)
+            if (one_round()) return std::fprintf(stderr, "%s failed\n", tt.c_str()), 1;
+        const double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        const double bytes = static_cast<double>(size) * batch * targets.size() * iters;
+        std::printf("--- %s Summary: size=%zu batch=%zu targets=%zu iters=%d  %.3f GB/s  (%.3f ms/round)\n",
+                    tt.c_str(), size, batch, targets.size(), iters, bytes / 1e9 / s, s * 1e3 / iters);
+        std::fflush(stdout);
+    }
+    comm.shutdown();
+    return 0;
+}

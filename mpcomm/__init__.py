@@ -64,8 +64,9 @@ def native_library_path() -> str:
 
 
 def get_include_dir() -> str:
-    """Directory holding mpcomm.h / mpcomm_log.h."""
-    return _os.path.join(_os.path.dirname(_PACKAGE_DIR), "include")
+    """Directory holding mpcomm.h / mpcomm_log.h (wheel: mpcomm/include; source tree: include/)."""
+    inside = _os.path.join(_PACKAGE_DIR, "include")
+    return inside if _os.path.isdir(inside) else _os.path.join(_os.path.dirname(_PACKAGE_DIR), "include")
 
 
 def get_lib_dir() -> str:
