@@ -479,8 +479,9 @@ void MPComm::Impl::maybeInjectFault() {
     if (cfg_.fault_after_sec < 0) return;
     const double t = std::chrono::duration<double>(Clock::now() - init_time_).count();
     if (!fault_injected_ && t >= cfg_.fault_after_sec) {
-        fault_injected_ = true;
         std::lock_guard<std::mutex> g(conn_mu_);
+        if (connections_.empty()) return;  // fire once there is something to break
+        fault_injected_ = true;
         for (auto &kv : connections_)
             for (auto &gp : kv.second->groups) {
                 const bool rail_hit = cfg_.fault_mode == "all_nic" ||

@@ -1,0 +1,60 @@
+"""Runs the "ib" fabric against the fake libibverbs provider (env
+MPCOMM_IBVERBS_LIB) in one process: handshake with suffix pairing (mlx5_0 ->
+mlx5_0 + cross-NUMA mlx5_4 is absent, so mlx5_0 <-> mlx5_0 and mlx5_1 <->
+mlx5_1), buffer query, PUT/GET/scatter with byte checks. With
+MPCOMM_FAULT_INJECT_* set, the QPs of rail 0 go to ERR and the transfer must
+still complete (completions flush, rail 0 is quarantined, chunks re-post on
+rail 1). Prints "ib fake ok" on success."""
+import ctypes
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import mpcomm  # noqa: E402
+
+
+def main():
+    n = 6 << 20
+    a, b = mpcomm.MPComm(), mpcomm.MPComm()
+    assert a.init("A") == 0 and b.init("B") == 0
+    assert a.get_fabric_name() == "ib", a.get_fabric_name()
+    assert a.get_active_devices() == ["mlx5_0", "mlx5_1"], a.get_active_devices()
+    gid = a.get_gid(0)
+    assert gid.startswith("fe:80:") and len(gid) == 47, gid
+    t = ctypes.create_string_buffer(n)
+    s = ctypes.create_string_buffer(os.urandom(n), n)
+    d = ctypes.create_string_buffer(n)
+    assert b.register_memory(ctypes.addressof(t), n) == 0
+    assert b.publish_buffer(ctypes.addressof(t), n) == 0
+    assert b.start_accept_thread() == 0
+    for x in (s, d):
+        assert a.register_memory(ctypes.addressof(x), n) == 0
+    rk = b.get_all_rkeys(ctypes.addressof(t))
+    assert len(rk) == 2 and all(rk), rk
+    port = b.get_tcp_port()
+    assert a.connect("B", "127.0.0.1", port) == 0
+    info = a.query_remote_buffers("B", "127.0.0.1", port)
+    assert info["buffers"][0]["rkeys"] == rk
+    h = a.put_async(ctypes.addressof(s), "B", ctypes.addressof(t), n)
+    assert a.wait_transfer(h, 20000) == 0, "PUT failed"
+    a.release_transfer(h)
+    assert t.raw == s.raw
+    h = a.get_async(ctypes.addressof(d), "B", ctypes.addressof(t), n)
+    assert a.wait_transfer(h, 20000) == 0, "GET failed"
+    a.release_transfer(h)
+    assert d.raw == s.raw
+    seg = n // 3
+    h = a.scatter_async(ctypes.addressof(s), ["B"] * 3, [ctypes.addressof(t) + (2 - i) * seg for i in range(3)],
+                        [seg] * 3)
+    assert a.wait_transfer(h, 20000) == 0
+    a.release_transfer(h)
+    for i in range(3):
+        assert t.raw[(2 - i) * seg:(3 - i) * seg] == s.raw[i * seg:(i + 1) * seg]
+    a.shutdown()
+    b.shutdown()
+    print("ib fake ok", flush=True)
+
+
+if __name__ == "__main__":
+    main()

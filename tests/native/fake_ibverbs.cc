@@ -1,0 +1,224 @@
+// In-process stand-in for libibverbs, loaded by the "ib" fabric through
+// MPCOMM_IBVERBS_LIB in CPU tests. Two devices (mlx5_0, mlx5_1), port 1
+// ACTIVE, one non-zero GID each. RC QPs follow the INIT/RTR/RTS/ERR state
+// machine; post_send (ops slot 25) executes RDMA WRITE/READ immediately with
+// rkey and bounds checks against the destination device's registrations and
+// queues one completion per WR on the send CQ, drained by poll_cq (slot 11).
+// A QP in ERR flushes WRs with status 5 (IBV_WC_WR_FLUSH_ERR).
+// Built as a shared library by CMake; it shares the ABI declarations of
+// csrc/transport/ib_verbs.h, so it checks the backend's logic, not the
+// system ABI.
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <mutex>
+#include <vector>
+
+#include "transport/ib_verbs.h"
+
+using namespace mpcomm::ibv;
+
+namespace {
+
+struct FakeDevice {
+    char name[32];
+    int index;
+};
+
+struct FakeCtx {
+    Context ctx;  // must be first: the backend sees Context*
+    FakeDevice *dev;
+};
+
+struct FakeCq {
+    Cq cq;
+    std::deque<Wc> wcs;
+};
+
+struct FakeQp {
+    Qp qp;
+    FakeCtx *owner;
+    uint32_t dest_qpn = 0;
+};
+
+struct FakeMr {
+    Mr mr;
+    FakeCtx *owner;
+};
+
+std::mutex g_mu;
+FakeDevice g_devs[2] = {{"mlx5_0", 0}, {"mlx5_1", 1}};
+std::map<uint32_t, FakeQp *> g_qps;
+std::map<uint32_t, FakeMr *> g_mrs;  // key -> region (lkey == rkey)
+uint32_t g_next_qpn = 0x300, g_next_key = 0x4000;
+
+bool mr_ok(uint32_t key, uint64_t addr, uint64_t len) {
+    auto it = g_mrs.find(key);
+    if (it == g_mrs.end()) return false;
+    const Mr &m = it->second->mr;
+    const uint64_t a = reinterpret_cast<uint64_t>(m.addr);
+    return addr >= a && addr + len <= a + m.length;
+}
+
+int fake_post_send(Qp *qp, SendWr *wr, SendWr **bad) {
+    std::lock_guard<std::mutex> g(g_mu);
+    FakeQp *q = reinterpret_cast<FakeQp *>(qp);
+    FakeCq *cq = reinterpret_cast<FakeCq *>(qp->send_cq);
+    for (SendWr *w = wr; w; w = w->next) {
+        Wc c;
+        std::memset(&c, 0, sizeof(c));
+        c.wr_id = w->wr_id;
+        c.qp_num = qp->qp_num;
+        c.opcode = w->opcode;
+        if (qp->state == kQpsErr) {
+            c.status = 5;
+        } else if (qp->state != kQpsRts || w->num_sge != 1) {
+            if (bad) *bad = w;
+            return 22;  // EINVAL, nothing queued from here on
+        } else {
+            const Sge &s = w->sg_list[0];
+            auto peer = g_qps.find(q->dest_qpn);
+            if (!mr_ok(s.lkey, s.addr, s.length)) {
+                c.status = 4;  // local protection error
+            } else if (peer == g_qps.end() || peer->second->qp.state == kQpsErr) {
+                c.status = 12;  // retry exceeded
+            } else if (!mr_ok(w->wr.rkey, w->wr.remote_addr, s.length)) {
+                c.status = 10;  // remote access error
+            } else {
+                void *local = reinterpret_cast<void *>(s.addr);
+                void *remote = reinterpret_cast<void *>(w->wr.remote_addr);
+                if (w->opcode == kWrRdmaWrite) std::memmove(remote, local, s.length);
+                else std::memmove(local, remote, s.length);
+                c.status = 0;
+                c.byte_len = s.length;
+            }
+        }
+        if (w->send_flags & kSendSignaled) cq->wcs.push_back(c);
+    }
+    return 0;
+}
+
+int fake_poll_cq(Cq *cq, int n, Wc *wc) {
+    std::lock_guard<std::mutex> g(g_mu);
+    FakeCq *f = reinterpret_cast<FakeCq *>(cq);
+    int k = 0;
+    while (k < n && !f->wcs.empty()) {
+        wc[k++] = f->wcs.front();
+        f->wcs.pop_front();
+    }
+    return k;
+}
+
+}  // namespace
+
+extern "C" {
+
+Device **ibv_get_device_list(int *n) {
+    Device **l = static_cast<Device **>(std::calloc(3, sizeof(Device *)));
+    l[0] = reinterpret_cast<Device *>(&g_devs[0]);
+    l[1] = reinterpret_cast<Device *>(&g_devs[1]);
+    if (n) *n = 2;
+    return l;
+}
+void ibv_free_device_list(Device **l) { std::free(l); }
+const char *ibv_get_device_name(Device *d) { return reinterpret_cast<FakeDevice *>(d)->name; }
+
+Context *ibv_open_device(Device *d) {
+    FakeCtx *c = new FakeCtx();
+    std::memset(&c->ctx, 0, sizeof(c->ctx));
+    c->ctx.device = d;
+    c->ctx.ops[11] = reinterpret_cast<void *>(&fake_poll_cq);
+    c->ctx.ops[25] = reinterpret_cast<void *>(&fake_post_send);
+    c->dev = reinterpret_cast<FakeDevice *>(d);
+    return &c->ctx;
+}
+int ibv_close_device(Context *c) {
+    delete reinterpret_cast<FakeCtx *>(c);
+    return 0;
+}
+int ibv_query_port(Context *c, uint8_t port, PortAttr *a) {
+    std::memset(a, 0, 64);
+    if (port != 1) return 22;
+    a->state = kPortActive;
+    a->gid_tbl_len = 4;
+    a->lid = static_cast<uint16_t>(reinterpret_cast<FakeCtx *>(c)->dev->index + 1);
+    return 0;
+}
+int ibv_query_gid(Context *c, uint8_t, int index, Gid *g) {
+    std::memset(g, 0, sizeof(*g));
+    if (index < 0 || index >= 4) return 22;
+    g->raw[0] = 0xfe;
+    g->raw[1] = 0x80;
+    g->raw[14] = static_cast<uint8_t>(index);
+    g->raw[15] = static_cast<uint8_t>(reinterpret_cast<FakeCtx *>(c)->dev->index + 1);
+    return 0;
+}
+Pd *ibv_alloc_pd(Context *c) { return reinterpret_cast<Pd *>(c); }
+int ibv_dealloc_pd(Pd *) { return 0; }
+Cq *ibv_create_cq(Context *c, int, void *, CompChannel *, int) {
+    FakeCq *f = new FakeCq();
+    f->cq.context = c;
+    return &f->cq;
+}
+int ibv_destroy_cq(Cq *cq) {
+    delete reinterpret_cast<FakeCq *>(cq);
+    return 0;
+}
+Mr *ibv_reg_mr(Pd *pd, void *addr, size_t len, int) {
+    std::lock_guard<std::mutex> g(g_mu);
+    FakeMr *m = new FakeMr();
+    m->owner = reinterpret_cast<FakeCtx *>(pd);
+    m->mr.context = &m->owner->ctx;
+    m->mr.pd = pd;
+    m->mr.addr = addr;
+    m->mr.length = len;
+    m->mr.lkey = m->mr.rkey = g_next_key++;
+    g_mrs[m->mr.lkey] = m;
+    return &m->mr;
+}
+int ibv_dereg_mr(Mr *mr) {
+    std::lock_guard<std::mutex> g(g_mu);
+    g_mrs.erase(mr->lkey);
+    delete reinterpret_cast<FakeMr *>(mr);
+    return 0;
+}
+Qp *ibv_create_qp(Pd *pd, QpInitAttr *a) {
+    std::lock_guard<std::mutex> g(g_mu);
+    FakeQp *q = new FakeQp();
+    std::memset(&q->qp, 0, sizeof(q->qp));
+    q->owner = reinterpret_cast<FakeCtx *>(pd);
+    q->qp.context = &q->owner->ctx;
+    q->qp.pd = pd;
+    q->qp.send_cq = a->send_cq;
+    q->qp.recv_cq = a->recv_cq;
+    q->qp.qp_num = g_next_qpn++;
+    q->qp.state = kQpsReset;
+    q->qp.qp_type = a->qp_type;
+    g_qps[q->qp.qp_num] = q;
+    return &q->qp;
+}
+int ibv_modify_qp(Qp *qp, QpAttr *a, int mask) {
+    std::lock_guard<std::mutex> g(g_mu);
+    FakeQp *q = reinterpret_cast<FakeQp *>(qp);
+    if (!(mask & kQpState)) return 22;
+    const uint32_t from = qp->state, to = a->qp_state;
+    const bool legal = to == kQpsErr || to == kQpsReset || (from == kQpsReset && to == kQpsInit) ||
+                       (from == kQpsInit && to == kQpsRtr) || (from == kQpsRtr && to == kQpsRts);
+    if (!legal) return 22;
+    if (to == kQpsRtr) {
+        if (!(mask & kQpDestQpn) || !(mask & kQpAv) || !a->ah_attr.is_global) return 22;
+        q->dest_qpn = a->dest_qp_num;
+    }
+    qp->state = to;
+    return 0;
+}
+int ibv_destroy_qp(Qp *qp) {
+    std::lock_guard<std::mutex> g(g_mu);
+    g_qps.erase(qp->qp_num);
+    delete reinterpret_cast<FakeQp *>(qp);
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,34 @@
+"""The ibverbs fabric on CPU, against tests/native/fake_ibverbs.cc."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB = os.path.join(ROOT, "tests", "native", "bin", "libfake_ibverbs.so")
+
+
+def _run(extra):
+    assert os.path.exists(LIB), "fake provider not built (run __graft_entry__.build())"
+    env = dict(os.environ, MPCOMM_FABRIC="ib", MPCOMM_IBVERBS_LIB=LIB, MPCOMM_GID_INDEX="-1",
+               MPCOMM_LOG_LEVEL="1", PYTHONPATH=ROOT, **extra)
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "ib_fake_case.py")], capture_output=True,
+                       text=True, env=env, timeout=120)
+    assert r.returncode == 0 and "ib fake ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+    return r
+
+
+def test_ib_fabric_put_get_scatter():
+    _run({})
+
+
+@pytest.mark.parametrize("mode", ["single_qp", "all_qp"])
+def test_ib_fault_injection_reposts_on_healthy_rail(mode):
+    r = _run({"MPCOMM_FAULT_INJECT_AFTER_SEC": "0", "MPCOMM_FAULT_INJECT_NIC": "0",
+              "MPCOMM_FAULT_INJECT_MODE": mode, "MPCOMM_MAX_RDMA_TRANSFER_SIZE": "65536"})
+    import re
+
+    moved = [int(x) for x in re.findall(r"fault injection \(\w+\) moved (\d+) QPs to ERR", r.stderr)]
+    assert moved and max(moved) > 0, r.stderr[-2000:]
+    assert "quarantined" in r.stderr
