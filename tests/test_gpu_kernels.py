@@ -217,6 +217,53 @@ def test_fabric_scatter_gather_hbm_to_hbm():
         comm.shutdown()
 
 
+def test_h2d_qos_pauses_read_posts_during_gather_windows(monkeypatch):
+    """A background GET (pool -> HBM) shares the PCIe link with tmaGather.
+    With QoS at rate 0 its chunk posts are deferred while a gather kernel's
+    window is open (PCIe-domain defer_count rises) and it still completes
+    bit-exact; posted == completed bytes at the end."""
+    monkeypatch.setenv("MPCOMM_PCIE_STAT_ENABLE", "1")
+    monkeypatch.setenv("MPCOMM_NVL_CHUNK_SIZE", str(1 << 20))
+    comm = mpcomm.MPComm()
+    assert comm.init("qos-test") == 0 and comm.start_accept_thread() == 0
+    try:
+        n = 512 << 20
+        pool = torch.randint(0, 256, (n,), dtype=torch.uint8).pin_memory()
+        dst = torch.zeros(n, dtype=torch.uint8, device="cuda")
+        for t in (pool, dst):
+            assert comm.register_memory(t.data_ptr(), n) == 0
+        assert comm.publish_buffer(pool.data_ptr(), n) == 0
+        port = comm.get_tcp_port()
+        assert comm.connect("pool", "127.0.0.1", port) == 0 and comm.query_remote_buffers("pool", "127.0.0.1", port)
+        pages, bs, m = 4096, 65536, 2048
+        kv = _pool(pages, bs, seed=4)
+        dram = comm.map_dram_to_gpu(kv.data_ptr(), kv.numel())
+        idx = torch.randperm(pages)[:m].cuda()
+        out = torch.empty(m * bs, dtype=torch.uint8, device="cuda")
+        comm.enable_h2d_qos(0, 0)
+        assert comm.is_pcie_domain_stat_enabled()
+        stream = torch.cuda.Stream()
+        h = comm.get_async(dst.data_ptr(), "pool", pool.data_ptr(), n)
+        while not comm.is_transfer_complete(h):
+            assert comm.tma_gather(dram, idx.data_ptr(), out.data_ptr(), m, bs, 0, 0, stream.cuda_stream) == 0
+            stream.synchronize()
+        assert comm.wait_transfer(h, 60000) == 0
+        comm.release_transfer(h)
+        torch.cuda.synchronize()
+        assert torch.equal(dst.cpu(), pool)
+        assert torch.equal(out.view(m, bs).cpu(), kv[idx.cpu()])
+        stats = {s["gpu"]: s for s in comm.get_pcie_domain_stats()}
+        s0 = stats[torch.cuda.current_device()]
+        assert s0["defer_count"] > 0, s0
+        assert s0["posted_bytes"] == s0["completed_bytes"] == n and s0["in_flight_bytes"] == 0
+        assert 0 < s0["in_flight_bytes_max"] <= n
+        comm.reset_pcie_domain_stats()
+        assert comm.get_pcie_domain_stats()[0]["post_count"] == 0
+        comm.unmap_dram_from_gpu(kv.data_ptr())
+    finally:
+        comm.shutdown()
+
+
 def test_tma_gather_api_with_mapping_and_qos_window():
     """tmaGather through MPComm with H2D QoS on: the kernel opens and closes its window."""
     comm = mpcomm.MPComm()
