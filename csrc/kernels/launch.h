@@ -52,8 +52,9 @@ struct CopyDesc {
 constexpr int kMaxCopyDescs = 64;
 // Copies up to kMaxCopyDescs spans in one launch (descriptors travel in the
 // kernel's parameter block, no staging buffer).
+// mode: kModeAuto/kModeTma = bulk pipeline, kModeSm = vector SM kernel.
 int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_t *status,
-               LaunchInfo *info);
+               LaunchInfo *info, int mode = kModeAuto);
 
 // CRC-32 (IEEE 802.3, reflected polynomial 0xEDB88320, init/xorout
 // 0xFFFFFFFF — the zlib/PNG variant) of n blocks of bs bytes each.

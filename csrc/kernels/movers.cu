@@ -444,24 +444,27 @@ int h2d_scatter(const void *srcp, const int64_t *idx, void *pool, int64_t pool_b
 }
 
 int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_t *status,
-               LaunchInfo *info) {
+               LaunchInfo *info, int mode) {
     if (n <= 0 || n > kMaxCopyDescs || !descs) return cudaErrorInvalidValue;
+    const bool vec = mode == kModeSm;
     BatchSrc src;
-    src.tile_bytes = kStageBytes;
+    src.tile_bytes = vec ? kVecTileBytes : kStageBytes;
     int k = 0;
     int64_t tiles = 0;
     for (int i = 0; i < n; ++i) {
         if (descs[i].bytes == 0) continue;
         src.d[k] = descs[i];
         src.start[k] = tiles;
-        tiles += static_cast<int64_t>((descs[i].bytes + kStageBytes - 1) / kStageBytes);
+        tiles += static_cast<int64_t>((descs[i].bytes + src.tile_bytes - 1) / src.tile_bytes);
         ++k;
     }
     if (k == 0) return cudaSuccess;
     src.start[k] = tiles;
     src.n = k;
-    return launch_bulk(src, tiles, max_ctas, static_cast<cudaStream_t>(stream), status,
-                       Epilogue{nullptr, nullptr, nullptr, 0}, info);
+    const Epilogue ep{nullptr, nullptr, nullptr, 0};
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return vec ? launch_vector(src, tiles, max_ctas, st, status, ep, info)
+               : launch_bulk(src, tiles, max_ctas, st, status, ep, info);
 }
 
 int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx, void *dst,

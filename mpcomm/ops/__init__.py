@@ -103,8 +103,10 @@ def crc32_host(data: bytes, crc: int = 0) -> int:
 
 
 def copy_spans(srcs: Sequence[int], dsts: Sequence[int], lengths: Sequence[int], max_ctas: int = 0,
-               stream: Optional[torch.cuda.Stream] = None) -> None:
-    _check(_native.copy_spans(list(srcs), list(dsts), list(lengths), max_ctas, _stream_ptr(stream)),
+               stream: Optional[torch.cuda.Stream] = None, mode: int = MODE_AUTO) -> None:
+    """Copies up to 64 spans in one launch (bulk pipeline, or the vector SM
+    kernel with ``mode=MODE_SM``); any device-reachable addresses."""
+    _check(_native.copy_spans(list(srcs), list(dsts), list(lengths), max_ctas, _stream_ptr(stream), mode),
            "copy_spans")
 
 

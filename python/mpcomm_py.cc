@@ -419,7 +419,7 @@ PYBIND11_MODULE(_mpcomm, m) {
           py::arg("block_size"), py::arg("mode") = 0, py::arg("max_ctas") = 0, py::arg("stream") = 0);
     m.def("copy_spans",
           [](const std::vector<uintptr_t> &src, const std::vector<uintptr_t> &dst, const std::vector<uint64_t> &len,
-             int max_ctas, uintptr_t stream) {
+             int max_ctas, uintptr_t stream, int mode) {
               if (src.size() != dst.size() || src.size() != len.size() || src.size() > kern::kMaxCopyDescs)
                   return static_cast<int>(MPCOMM_ERR_INVALID_ARG);
               std::vector<kern::CopyDesc> d(src.size());
@@ -427,9 +427,10 @@ PYBIND11_MODULE(_mpcomm, m) {
                   d[i] = kern::CopyDesc{reinterpret_cast<const void *>(src[i]), reinterpret_cast<void *>(dst[i]), len[i]};
               py::gil_scoped_release r;
               return kern::copy_batch(d.data(), static_cast<int>(d.size()), max_ctas,
-                                      reinterpret_cast<void *>(stream), nullptr, nullptr);
+                                      reinterpret_cast<void *>(stream), nullptr, nullptr, mode);
           },
-          py::arg("src"), py::arg("dst"), py::arg("lengths"), py::arg("max_ctas") = 0, py::arg("stream") = 0);
+          py::arg("src"), py::arg("dst"), py::arg("lengths"), py::arg("max_ctas") = 0, py::arg("stream") = 0,
+          py::arg("mode") = 0);
     m.def("pxn_gather_forward",
           [](uintptr_t pool, int64_t pool_blocks, uintptr_t idx, uintptr_t dst, int64_t n, int64_t bs, int max_ctas,
              uintptr_t stream, uintptr_t flag, uint64_t flag_value, uintptr_t ctr) {
@@ -495,6 +496,8 @@ PYBIND11_MODULE(_mpcomm, m) {
         return py::make_tuple(e, reinterpret_cast<uintptr_t>(d), pinned);
     });
     m.def("host_unregister", [](uintptr_t ptr) { return gpu::host_unpin(reinterpret_cast<void *>(ptr)); });
+    m.def("enable_peer_access", &gpu::enable_peer_access, py::arg("device"), py::arg("peer"),
+          "Lets kernels on `device` access memory of `peer` (0 or a CUDA error).");
     m.def("multicast_supported", &vmm::multicast_supported, py::arg("device"));
     m.def("multicast_granularity", [](size_t size, int ndev) {
         size_t g = 0;

@@ -294,8 +294,14 @@ def test_handle_recycling(pair):
     assert len(seen) <= 2  # released handles are reused
 
 
-def test_native_core_binary():
-    exe = os.path.join(ROOT, "tests", "native", "bin", "test_core")
+@pytest.mark.parametrize("name", ["test_core", "test_engine", "test_engine_san"])
+def test_native_binaries(name):
+    """Core unit tests, the multi-threaded engine stress, and the same stress
+    built with AddressSanitizer (memory errors in the engine's lifetime and
+    completion protocol abort with a report)."""
+    exe = os.path.join(ROOT, "tests", "native", "bin", name)
     assert os.path.exists(exe), "native tests not built (run __graft_entry__.build())"
-    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
-    assert r.returncode == 0, r.stderr
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=0:abort_on_error=1", MPCOMM_LOG_LEVEL="1")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    assert "ERROR: AddressSanitizer" not in r.stderr
