@@ -210,6 +210,15 @@ void *stream_create(int dev) {
     return s;
 }
 
+int stream_device(void *s) {
+    int d = -1;
+    if (cudaStreamGetDevice(static_cast<cudaStream_t>(s), &d) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return d;
+}
+
 void stream_destroy(void *s) {
     if (s) cudaStreamDestroy(static_cast<cudaStream_t>(s));
 }

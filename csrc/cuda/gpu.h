@@ -57,6 +57,8 @@ int enable_peer_access(int dev, int peer);
 
 // Streams and events (opaque handles).
 void *stream_create(int dev);
+// Device ordinal a stream belongs to (-1 on error).
+int stream_device(void *s);
 void stream_destroy(void *s);
 int stream_sync(void *s);
 void *event_create(int dev);

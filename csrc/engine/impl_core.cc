@@ -72,9 +72,10 @@ int MPComm::Impl::init(const std::string &host_id, const std::string &device_nam
 
     // MPCOMM_NIC_FILTER overrides the init() device list (reference :1942-1959).
     std::vector<std::string> filter = split_csv(cfg_.nic_filter.empty() ? device_names : cfg_.nic_filter);
-    if (filter.empty() && fab == "nvl") {
+    if (filter.empty() && fab == "nvl" && !cfg_.pxn_enable) {
         // One rail for the calling thread's current GPU: opening a rail (a
         // CUDA context + streams) on every GPU from every rank is wasteful.
+        // With PXN every visible GPU becomes a rail (proxy egress/ingress).
         int dev = gpu::current_device();
         filter.push_back("nvl_" + std::to_string(dev < 0 ? 0 : dev));
     }

@@ -94,6 +94,20 @@ TransferHandle MPComm::Impl::submit(uintptr_t local, const std::vector<std::stri
     // Candidate rails: PCIe-affine to the local GPU buffer, else NUMA-local,
     // else all; quarantined rails dropped unless that empties the set.
     std::vector<size_t> cand = region.affine_rails;
+    // PXN (NVLink proxy rails): a GPU buffer moving to or from host memory
+    // is striped over every GPU's rail — peers read/write the buffer over
+    // NVLink and cross their own PCIe links — instead of only its own link
+    // (the reference routes SCATTERs through a proxy GPU's NIC the same way,
+    // src/mpcomm.cpp:5135-5403).
+    if (cfg_.pxn_enable && region.gpu >= 0 && !cand.empty()) {
+        bool host_side = true;
+        for (size_t i = 0; i < hosts.size(); ++i) host_side &= t->conns[i]->remote_gpu_for(raddrs[i]) < 0;
+        if (host_side) {
+            cand.clear();
+            for (size_t i = 0; i < rails_.size(); ++i)
+                if (rails_[i]->gpu >= 0) cand.push_back(i);
+        }
+    }
     if (cand.empty()) cand = localNicsForNuma(region.numa);
     if (cand.empty())
         for (size_t i = 0; i < rails_.size(); ++i) cand.push_back(i);

@@ -436,6 +436,8 @@ class NvlRail final : public Rail {
         return cfg.max_outstanding_set ? cfg.max_outstanding_per_qp : cfg.nvl_outstanding_per_qp;
     }
     int set_stream(void *stream) override {
+        // A stream belongs to one device: only that device's rail adopts it.
+        if (stream && gpu::stream_device(stream) != dev_) return 0;
         std::lock_guard<std::mutex> g(mu_);
         override_stream_ = stream;
         return 0;

@@ -43,6 +43,7 @@ def main(argv=None):
     ap.add_argument("--qos-rate", type=float, default=0.0, help="bytes/s during H2D windows (0 = pause)")
     ap.add_argument("--bg-mb", type=int, default=1024)
     ap.add_argument("--no-qos", action="store_true")
+    ap.add_argument("--sweep-ctas", default="", help="comma list: time the broadcast alone per grid size")
     a = ap.parse_args(argv)
     rank, world, local = parallel.init_from_env("nccl")
     dev = torch.device("cuda", local)
@@ -133,6 +134,18 @@ def main(argv=None):
     # NVLink roofline of the broadcast (after the gather): NVLS sends the
     # bytes once through the switch; fan-out sends them world-1 times.
     res["roofline_note"] = "NVLink 770 GB/s per direction per GPU (measured peer copy)"
+
+    if a.sweep_ctas and world > 1:
+        rows = []
+        for ctas in [int(x) for x in a.sweep_ctas.split(",")]:
+            row = {"ctas": ctas}
+            if grp is not None:
+                row["nvls_ms"] = round(timed(lambda: rank == 0 and ops.nvls_broadcast(
+                    staged, grp.mc_ptr, nbytes, max_ctas=ctas, stream=stream)), 4)
+            row["fanout_ms"] = round(timed(lambda: rank == 0 and ops.p2p_fanout(
+                staged, [peers.ptrs[r] for r in range(1, world)], nbytes, max_ctas=ctas, stream=stream)), 4)
+            rows.append(row)
+        res["broadcast_only_sweep"] = rows
 
     if rank == 0 and not a.no_qos:
         res["qos"] = qos_experiment(comm, host, dram, idx, staged, pages, stream, a)
