@@ -54,6 +54,7 @@ struct RailSlot {
     std::string pci_path;
     std::atomic<bool> quarantined{false};
     std::atomic<uint64_t> quarantine_since_ns{0};
+    std::atomic<uint64_t> completed_bytes{0};
 };
 
 struct Region {
@@ -188,6 +189,11 @@ class MPComm::Impl {
     bool isH2DQoSEnabled() const { return h2d_qos_enabled_.load(std::memory_order_acquire); }
     void disableH2DQoS();
     uint64_t getNicCompletedBytes() const { return nic_completed_bytes_.load(); }
+    std::vector<uint64_t> railCompletedBytes() const {
+        std::vector<uint64_t> v;
+        for (const auto &r : rails_) v.push_back(r->completed_bytes.load(std::memory_order_relaxed));
+        return v;
+    }
     std::vector<MPComm::PcieDomainStats> getPcieDomainStats() const;
     void resetPcieDomainStats();
     bool isPcieDomainStatEnabled() const { return cfg_.pcie_stat_enable; }

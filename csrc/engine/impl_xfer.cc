@@ -422,6 +422,7 @@ void MPComm::Impl::handleCompletion(Worker *w, const fabric::WorkCompletion &wc)
         t->rail_bytes[rail].fetch_add(c.length, std::memory_order_relaxed);
         t->done_chunks.fetch_add(1, std::memory_order_relaxed);
         nic_completed_bytes_.fetch_add(c.length, std::memory_order_relaxed);
+        rails_[rail]->completed_bytes.fetch_add(c.length, std::memory_order_relaxed);
         return;
     }
     MPCOMM_LOG_WARN("MPComm: WC error %d on %s (handle %lu chunk %zu)\n", wc.status,

@@ -81,6 +81,7 @@ void MPComm::setH2DQoSPolicy(uint64_t r, uint64_t b) { impl_->setH2DQoSPolicy(r,
 bool MPComm::isH2DQoSEnabled() const { return impl_->isH2DQoSEnabled(); }
 void MPComm::disableH2DQoS() { impl_->disableH2DQoS(); }
 uint64_t MPComm::getNicCompletedBytes() const { return impl_->getNicCompletedBytes(); }
+std::vector<uint64_t> MPComm::getRailCompletedBytes() const { return impl_->railCompletedBytes(); }
 std::vector<MPComm::PcieDomainStats> MPComm::getPcieDomainStats() const { return impl_->getPcieDomainStats(); }
 void MPComm::resetPcieDomainStats() { impl_->resetPcieDomainStats(); }
 bool MPComm::isPcieDomainStatEnabled() const { return impl_->isPcieDomainStatEnabled(); }

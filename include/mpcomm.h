@@ -213,6 +213,9 @@ class MPComm {
     bool isH2DQoSEnabled() const;
     void disableH2DQoS();
     uint64_t getNicCompletedBytes() const;
+    // Extension: completed bytes per rail, in getActiveDevices() order (how
+    // striping spread the traffic, e.g. over the PXN proxy rails).
+    std::vector<uint64_t> getRailCompletedBytes() const;
 
     struct PcieDomainStats {
         int gpu_device_id;

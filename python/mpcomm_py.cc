@@ -104,6 +104,7 @@ class PyMPComm {
     bool is_h2d_qos_enabled() const { return c_.isH2DQoSEnabled(); }
     void disable_h2d_qos() { c_.disableH2DQoS(); }
     uint64_t get_nic_completed_bytes() const { return c_.getNicCompletedBytes(); }
+    std::vector<uint64_t> get_rail_completed_bytes() const { return c_.getRailCompletedBytes(); }
     py::list get_pcie_domain_stats() const {
         py::list out;
         for (auto &s : c_.getPcieDomainStats()) {
@@ -326,6 +327,7 @@ PYBIND11_MODULE(_mpcomm, m) {
         .def("is_h2d_qos_enabled", &C::is_h2d_qos_enabled)
         .def("disable_h2d_qos", &C::disable_h2d_qos)
         .def("get_nic_completed_bytes", &C::get_nic_completed_bytes)
+        .def("get_rail_completed_bytes", &C::get_rail_completed_bytes)
         .def("get_pcie_domain_stats", &C::get_pcie_domain_stats)
         .def("reset_pcie_domain_stats", &C::reset_pcie_domain_stats)
         .def("is_pcie_domain_stat_enabled", &C::is_pcie_domain_stat_enabled)

@@ -70,7 +70,7 @@ def test_module_surface():
               "get_num_nics", "get_local_host_id", "get_tcp_port", "get_gid", "get_device_name",
               "get_active_devices", "get_qps_per_connection", "set_nic_throttle", "clear_nic_throttle",
               "enable_h2d_qos", "set_h2d_qos_policy", "is_h2d_qos_enabled", "disable_h2d_qos",
-              "get_nic_completed_bytes", "get_pcie_domain_stats", "reset_pcie_domain_stats",
+              "get_nic_completed_bytes", "get_rail_completed_bytes", "get_pcie_domain_stats", "reset_pcie_domain_stats",
               "is_pcie_domain_stat_enabled", "get_throttle_latency", "write_bytes_to_buffer",
               "read_bytes_from_buffer", "publish_buffer", "unpublish_buffer", "unpublish_all_buffers",
               "get_published_buffer_count", "query_remote_buffers", "query_remote_buffer_by_numa",
@@ -108,6 +108,8 @@ def test_put_get_roundtrip(pair):
     a.release_transfer(h)
     assert d.bytes() == s.bytes()
     assert a.get_nic_completed_bytes() == 2 * n
+    per_rail = a.get_rail_completed_bytes()
+    assert len(per_rail) == a.get_num_nics() and sum(per_rail) == 2 * n
 
 
 def test_scatter_gather_broadcast(pair):
