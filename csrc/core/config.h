@@ -30,6 +30,9 @@ struct Config {
     bool h2d_qos_enable = false;             // MPCOMM_H2D_QOS_ENABLE
     uint64_t h2d_qos_rate_bps = 0;           // MPCOMM_H2D_QOS_RATE_BPS
     uint64_t h2d_qos_burst_bytes = 0;        // MPCOMM_H2D_QOS_BURST_BYTES
+    // Device-side pause of background GPU-fabric H2D copies while an H2D
+    // window is open (rate 0 only): total pause per copy pipeline, us.
+    uint64_t qos_device_pause_us = 2000;     // MPCOMM_QOS_DEVICE_PAUSE_US (0 = host gating only)
     size_t nic_probe_interval = 10000;       // MPCOMM_NIC_PROBE_INTERVAL (loops)
     double nic_quarantine_sec = 5.0;         // MPCOMM_NIC_QUARANTINE_SEC
     // ---- fault injection (host side only) ----

@@ -256,6 +256,8 @@ int event_query(void *e) {
     return -static_cast<int>(r);
 }
 
+int event_sync(void *e) { return cudaEventSynchronize(static_cast<cudaEvent_t>(e)); }
+
 int device_sync() { return cudaDeviceSynchronize(); }
 
 const char *error_string(int err) { return cudaGetErrorString(static_cast<cudaError_t>(err)); }

@@ -66,6 +66,7 @@ void event_destroy(void *e);
 int event_record(void *e, void *stream);
 // 1 = complete, 0 = pending, <0 = error.
 int event_query(void *e);
+int event_sync(void *e);
 int device_sync();
 const char *error_string(int err);
 int last_error_clear();

@@ -200,9 +200,13 @@ class MPComm::Impl {
     bool getThrottleLatency(uint64_t *set, uint64_t *seen, uint64_t *drained, size_t *snap) const;
     // True while an H2D kernel window is open on GPU `gpu` (device-written).
     bool h2dWindowOpen(int gpu) const;
+    bool lastH2DWindow(int gpu, uint64_t *begin_ns, uint64_t *end_ns) const;
     // Arms a window slot for one H2D launch on `gpu`; returns device-visible
     // pointers (nullptr when QoS is off).
     bool acquireH2DWindow(int gpu, kern::H2DWindow **win, uint32_t **ctr);
+    bool ensureWindowPoolLocked();
+    uint32_t *deviceGateLocked(int gpu);
+    void applyDeviceGates();
 
     // ---- H2D (impl_h2d.cc) ----
     uintptr_t mapDRAMtoGPU(void *host, size_t len);
@@ -317,6 +321,7 @@ class MPComm::Impl {
 
     // H2D QoS
     std::atomic<bool> h2d_qos_enabled_{false};
+    std::atomic<bool> device_gates_on_{false};
     TokenBucket qos_bucket_;
     struct WindowPool;
     std::unique_ptr<WindowPool> windows_;
@@ -351,6 +356,7 @@ constexpr int kSlotsPerGpu = 64;
 struct MPComm::Impl::WindowPool {
     kern::H2DWindow *slots = nullptr;  // [kMaxGpuDomains][kSlotsPerGpu], host-mapped
     uint32_t *ctrs[kMaxGpuDomains] = {nullptr};  // device counters per GPU
+    uint32_t *gates[kMaxGpuDomains] = {nullptr};  // open-window count per GPU (device memory)
     ~WindowPool();
 };
 

@@ -21,6 +21,7 @@ namespace mpcomm {
 MPComm::Impl::WindowPool::~WindowPool() {
     gpu::host_free(slots);
     for (auto *c : ctrs) gpu::device_free(c);
+    for (auto *g : gates) gpu::device_free(g);
 }
 
 void MPComm::Impl::setNicThrottle(size_t outstanding, size_t chunk) {
@@ -55,34 +56,71 @@ bool MPComm::Impl::getThrottleLatency(uint64_t *set, uint64_t *seen, uint64_t *d
 }
 
 void MPComm::Impl::enableH2DQoS(uint64_t rate, uint64_t burst) {
-    setH2DQoSPolicy(rate, burst);
     h2d_qos_enabled_.store(true, std::memory_order_release);
-    MPCOMM_LOG_INFO("MPComm: H2D QoS enabled (rate=%lu B/s, burst=%lu B)\n",
-                    static_cast<unsigned long>(rate), static_cast<unsigned long>(qos_bucket_.burst()));
+    setH2DQoSPolicy(rate, burst);
+    MPCOMM_LOG_INFO("MPComm: H2D QoS enabled (rate=%lu B/s, burst=%lu B, device pause %s)\n",
+                    static_cast<unsigned long>(rate), static_cast<unsigned long>(qos_bucket_.burst()),
+                    device_gates_on_.load() ? "on" : "off");
 }
 
 void MPComm::Impl::setH2DQoSPolicy(uint64_t rate, uint64_t burst) {
     if (burst == 0 && rate != 0) burst = default_qos_burst(rate);
     qos_bucket_.configure(rate, burst);
+    applyDeviceGates();
 }
 
-void MPComm::Impl::disableH2DQoS() { h2d_qos_enabled_.store(false, std::memory_order_release); }
+void MPComm::Impl::disableH2DQoS() {
+    h2d_qos_enabled_.store(false, std::memory_order_release);
+    applyDeviceGates();
+}
+
+// Device gating: with QoS on and rate 0 (pause), every GPU rail's H2D copy
+// kernels watch their GPU's open-window counter and yield within one tile
+// (host gating alone stops new posts but cannot recall launched chunks).
+// A paced rate (> 0) stays host-side: the token bucket meters chunks.
+void MPComm::Impl::applyDeviceGates() {
+    const bool on = isH2DQoSEnabled() && qos_bucket_.rate() == 0 && cfg_.qos_device_pause_us > 0;
+    std::lock_guard<std::mutex> lk(map_mu_);
+    for (auto &r : rails_) {
+        const int g = r->gpu;
+        uint32_t *gate = (on && g >= 0 && ensureWindowPoolLocked()) ? deviceGateLocked(g) : nullptr;
+        r->rail->set_qos_gate(gate, gate ? cfg_.qos_device_pause_us * 1000ull : 0);
+    }
+    device_gates_on_.store(on, std::memory_order_release);
+}
+
+bool MPComm::Impl::ensureWindowPoolLocked() {
+    if (windows_) return true;
+    windows_ = std::make_unique<WindowPool>();
+    windows_->slots = static_cast<kern::H2DWindow *>(
+        gpu::host_alloc_mapped(sizeof(kern::H2DWindow) * kMaxGpuDomains * kSlotsPerGpu));
+    if (!windows_->slots) {
+        windows_.reset();
+        return false;
+    }
+    windows_live_.store(windows_.get(), std::memory_order_release);
+    return true;
+}
+
+uint32_t *MPComm::Impl::deviceGateLocked(int g) {
+    if (g < 0 || g >= static_cast<int>(kMaxGpuDomains)) return nullptr;
+    WindowPool &p = *windows_;
+    if (!p.gates[g]) {
+        int prev = gpu::current_device();
+        gpu::set_device(g);
+        p.gates[g] = static_cast<uint32_t *>(gpu::device_alloc(128));
+        if (p.gates[g]) gpu::memset_device(p.gates[g], 0, 128);
+        if (prev >= 0) gpu::set_device(prev);
+    }
+    return p.gates[g];
+}
 
 bool MPComm::Impl::acquireH2DWindow(int g, kern::H2DWindow **win, uint32_t **ctr) {
     *win = nullptr;
     *ctr = nullptr;
     if (!isH2DQoSEnabled() || g < 0 || g >= static_cast<int>(kMaxGpuDomains)) return false;
     std::lock_guard<std::mutex> lk(map_mu_);
-    if (!windows_) {
-        windows_ = std::make_unique<WindowPool>();
-        windows_->slots = static_cast<kern::H2DWindow *>(
-            gpu::host_alloc_mapped(sizeof(kern::H2DWindow) * kMaxGpuDomains * kSlotsPerGpu));
-        if (!windows_->slots) {
-            windows_.reset();
-            return false;
-        }
-        windows_live_.store(windows_.get(), std::memory_order_release);
-    }
+    if (!ensureWindowPoolLocked()) return false;
     WindowPool &p = *windows_;
     if (!p.ctrs[g]) {
         int prev = gpu::current_device();
@@ -100,6 +138,7 @@ bool MPComm::Impl::acquireH2DWindow(int g, kern::H2DWindow **win, uint32_t **ctr
         __atomic_store_n(&s->begin_ns, 0ull, __ATOMIC_RELAXED);
         __atomic_store_n(&s->end_ns, 0ull, __ATOMIC_RELAXED);
         s->gpu = g;
+        s->gate = device_gates_on_.load(std::memory_order_acquire) ? deviceGateLocked(g) : nullptr;
         __atomic_store_n(&s->armed, 1u, __ATOMIC_RELEASE);
         *win = s;
         *ctr = p.ctrs[g] + i;
@@ -120,6 +159,25 @@ bool MPComm::Impl::h2dWindowOpen(int g) const {
             return true;
     }
     return false;
+}
+
+bool MPComm::Impl::lastH2DWindow(int g, uint64_t *begin_ns, uint64_t *end_ns) const {
+    const WindowPool *wp = windows_live_.load(std::memory_order_acquire);
+    if (g < 0 || g >= static_cast<int>(kMaxGpuDomains) || !wp) return false;
+    uint64_t best_b = 0, best_e = 0;
+    for (int i = 0; i < kSlotsPerGpu; ++i) {
+        const kern::H2DWindow *s = &wp->slots[g * kSlotsPerGpu + i];
+        const uint64_t e = __atomic_load_n(&s->end_ns, __ATOMIC_ACQUIRE);
+        const uint64_t b = __atomic_load_n(&s->begin_ns, __ATOMIC_ACQUIRE);
+        if (e > best_e && b != 0) {
+            best_e = e;
+            best_b = b;
+        }
+    }
+    if (!best_e) return false;
+    *begin_ns = best_b;
+    *end_ns = best_e;
+    return true;
 }
 
 bool MPComm::Impl::qosAllowPost(const Transfer &t, size_t rail, size_t bytes) {

@@ -73,7 +73,26 @@ __device__ __forceinline__ void warp_copy_any(char *d, const char *s, uint64_t b
 
 // H2D QoS window helpers (see H2DWindow in launch.h).
 __device__ __forceinline__ void window_open(H2DWindow *win) {
-    if (win && blockIdx.x == 0 && threadIdx.x == 0) st_release_sys_u64(&win->begin_ns, globaltimer_ns() | 1ull);
+    if (win && blockIdx.x == 0 && threadIdx.x == 0) {
+        st_release_sys_u64(&win->begin_ns, globaltimer_ns() | 1ull);
+        uint32_t *gate = *reinterpret_cast<uint32_t *volatile *>(&win->gate);
+        if (gate) atomicAdd(gate, 1u);
+    }
+}
+
+// Device QoS gate of a background copy: returns at once when the gate is
+// closed (0) or this pipeline's pause budget is spent; otherwise sleeps
+// until the gate closes or the budget runs out. `paused` accumulates the
+// time spent here across calls (one per tile).
+__device__ __forceinline__ void qos_gate_wait(const uint32_t *gate, uint64_t &paused, uint64_t budget) {
+    if (!gate || paused >= budget || ld_acquire_gpu_u32(gate) == 0) return;
+    const uint64_t t0 = globaltimer_ns();
+    uint64_t now = t0;
+    while (ld_acquire_gpu_u32(gate) != 0 && paused + (now - t0) < budget) {
+        __nanosleep(256);
+        now = globaltimer_ns();
+    }
+    paused += now - t0;
 }
 
 }  // namespace kern

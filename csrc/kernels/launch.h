@@ -14,12 +14,17 @@ namespace kern {
 // kernel writes begin_ns when its first CTA starts and end_ns (release,
 // system scope) when its last CTA has finished all stores. The host QoS
 // engine treats begin != 0 && end == 0 as "window open".
+// `gate` (device memory of the same GPU, may be null) counts the open
+// windows of that GPU on the device: the first CTA adds 1, the last CTA
+// subtracts 1. GPU-fabric copies given the same gate pause their next tile
+// while it is non-zero (bounded), so background traffic yields within one
+// tile instead of after its launched chunks drain.
 struct H2DWindow {
     uint64_t begin_ns;
     uint64_t end_ns;
     int32_t gpu;
     uint32_t armed;
-    uint64_t pad;
+    uint32_t *gate;
 };
 
 struct LaunchInfo {
@@ -53,8 +58,17 @@ constexpr int kMaxCopyDescs = 64;
 // Copies up to kMaxCopyDescs spans in one launch (descriptors travel in the
 // kernel's parameter block, no staging buffer).
 // mode: kModeAuto/kModeTma = bulk pipeline, kModeSm = vector SM kernel.
+// gate (device memory, may be null): while *gate != 0 every pipeline waits
+// before issuing its next tile, for at most gate_budget_ns in total per
+// pipeline (then it runs ungated: fail-open, never a hang).
+// done_flag (may be host-mapped memory): after every store of the launch has
+// completed, the last CTA stores done_value there (system-scope release);
+// done_ctr is its last-CTA counter (device memory, zero, self-resetting;
+// launches sharing one must be stream-ordered).
 int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_t *status,
-               LaunchInfo *info, int mode = kModeAuto);
+               LaunchInfo *info, int mode = kModeAuto, const uint32_t *gate = nullptr,
+               uint64_t gate_budget_ns = 0, uint64_t *done_flag = nullptr, uint64_t done_value = 0,
+               uint32_t *done_ctr = nullptr);
 
 // CRC-32 (IEEE 802.3, reflected polynomial 0xEDB88320, init/xorout
 // 0xFFFFFFFF — the zlib/PNG variant) of n blocks of bs bytes each.

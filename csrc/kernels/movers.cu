@@ -96,6 +96,8 @@ struct GatherSrc {
     char *out;
     int64_t n, bs, pool_blocks, tpb;
     uint32_t tile_bytes;
+    const uint32_t *gate = nullptr;  // QoS gate: only fabric batches use one
+    uint64_t gate_budget = 0;
     __device__ __forceinline__ int64_t count() const { return n * tpb; }
     __device__ __forceinline__ Tile tile(int64_t t) const {
         const int64_t b = t / tpb;
@@ -116,6 +118,8 @@ struct ScatterSrc {
     char *pool;
     int64_t n, bs, pool_blocks, tpb;
     uint32_t tile_bytes;
+    const uint32_t *gate = nullptr;
+    uint64_t gate_budget = 0;
     __device__ __forceinline__ int64_t count() const { return n * tpb; }
     __device__ __forceinline__ Tile tile(int64_t t) const {
         const int64_t b = t / tpb;
@@ -135,6 +139,8 @@ struct BatchSrc {
     int64_t start[kMaxCopyDescs + 1];
     int n;
     uint32_t tile_bytes;
+    const uint32_t *gate;  // device QoS gate (null = ungated)
+    uint64_t gate_budget;  // total pause per pipeline, ns
     __device__ __forceinline__ int64_t count() const { return start[n]; }
     __device__ __forceinline__ Tile tile(int64_t t) const {
         int lo = 0, hi = n;
@@ -177,6 +183,7 @@ __device__ __forceinline__ void warp_bulk_pipeline(const Src &src, int64_t first
     uint32_t st_bytes[STAGES];
     uint32_t st_kind[STAGES];
     int64_t issued = 0;
+    uint64_t paused = 0;  // lane 0: QoS pause spent so far
 
     auto issue = [&](int64_t t, int s) {  // warp-collective
         const int64_t w = t >> 5;
@@ -198,6 +205,7 @@ __device__ __forceinline__ void warp_bulk_pipeline(const Src &src, int64_t first
             st_bytes[s] = tb;
             st_kind[s] = tk;
             const bool bulk = tk == kBulk;
+            qos_gate_wait(src.gate, paused, src.gate_budget);
             mbar_arrive_expect_tx(&bars[s], bulk ? tb : 0u);
             if (bulk) bulk_load(stage_mem + static_cast<size_t>(s) * STAGE_BYTES, ts, tb, &bars[s]);
         }
@@ -292,7 +300,11 @@ __device__ __forceinline__ void run_epilogue(const Epilogue &ep) {
             *ep.ctr = 0u;
             __threadfence_system();
             if (ep.flag) st_release_sys_u64(ep.flag, ep.flag_value);
-            if (ep.win) st_release_sys_u64(&ep.win->end_ns, globaltimer_ns() | 1ull);
+            if (ep.win) {
+                uint32_t *gate = *reinterpret_cast<uint32_t *volatile *>(&ep.win->gate);
+                if (gate) atomicSub(gate, 1u);
+                st_release_sys_u64(&ep.win->end_ns, globaltimer_ns() | 1ull);
+            }
         }
     }
 }
@@ -321,9 +333,14 @@ __global__ void __launch_bounds__(kVecWarps * 32)
     const int lane = threadIdx.x & 31;
     const int64_t total = src.count();
     const int64_t nw = static_cast<int64_t>(gridDim.x) * kVecWarps;
+    uint64_t paused = 0;
     window_open(ep.win);
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * kVecWarps + (threadIdx.x >> 5); t < total;
          t += nw) {
+        if (src.gate) {
+            if (lane == 0) qos_gate_wait(src.gate, paused, src.gate_budget);
+            __syncwarp();
+        }
         const Tile tl = src.tile(t);
         if (tl.kind == kBad) {
             if (lane == 0) atomicOr(status, kStatusBadIndex);
@@ -444,11 +461,15 @@ int h2d_scatter(const void *srcp, const int64_t *idx, void *pool, int64_t pool_b
 }
 
 int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_t *status,
-               LaunchInfo *info, int mode) {
+               LaunchInfo *info, int mode, const uint32_t *gate, uint64_t gate_budget_ns, uint64_t *done_flag,
+               uint64_t done_value, uint32_t *done_ctr) {
     if (n <= 0 || n > kMaxCopyDescs || !descs) return cudaErrorInvalidValue;
+    if (done_flag && !done_ctr) return cudaErrorInvalidValue;
     const bool vec = mode == kModeSm;
     BatchSrc src;
     src.tile_bytes = vec ? kVecTileBytes : kStageBytes;
+    src.gate = gate_budget_ns ? gate : nullptr;
+    src.gate_budget = gate_budget_ns;
     int k = 0;
     int64_t tiles = 0;
     for (int i = 0; i < n; ++i) {
@@ -458,10 +479,16 @@ int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_
         tiles += static_cast<int64_t>((descs[i].bytes + src.tile_bytes - 1) / src.tile_bytes);
         ++k;
     }
-    if (k == 0) return cudaSuccess;
+    if (k == 0) {
+        // Nothing to copy: still publish completion, in stream order.
+        if (!done_flag) return cudaSuccess;
+        src.d[0] = CopyDesc{descs[0].src, descs[0].dst, 0};
+        src.start[0] = 0;
+        k = 0;
+    }
     src.start[k] = tiles;
     src.n = k;
-    const Epilogue ep{nullptr, nullptr, nullptr, 0};
+    const Epilogue ep{nullptr, done_ctr, done_flag, done_value};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     return vec ? launch_vector(src, tiles, max_ctas, st, status, ep, info)
                : launch_bulk(src, tiles, max_ctas, st, status, ep, info);

@@ -79,6 +79,7 @@ void MPComm::clearNicThrottle() { impl_->clearNicThrottle(); }
 void MPComm::enableH2DQoS(uint64_t r, uint64_t b) { impl_->enableH2DQoS(r, b); }
 void MPComm::setH2DQoSPolicy(uint64_t r, uint64_t b) { impl_->setH2DQoSPolicy(r, b); }
 bool MPComm::isH2DQoSEnabled() const { return impl_->isH2DQoSEnabled(); }
+bool MPComm::getLastH2DWindow(int gpu, uint64_t *b, uint64_t *e) const { return impl_->lastH2DWindow(gpu, b, e); }
 void MPComm::disableH2DQoS() { impl_->disableH2DQoS(); }
 uint64_t MPComm::getNicCompletedBytes() const { return impl_->getNicCompletedBytes(); }
 std::vector<uint64_t> MPComm::getRailCompletedBytes() const { return impl_->railCompletedBytes(); }

@@ -114,6 +114,10 @@ class Rail {
     }
     // Routes kernel launches (nvl) into a caller stream; others ignore it.
     virtual int set_stream(void * /*stream*/) { return 0; }
+    // Device QoS gate for H2D copies (nvl): while *gate != 0 the rail's copy
+    // kernels pause before each tile, at most budget_ns per pipeline.
+    // Null disables it. Other fabrics ignore it.
+    virtual void set_qos_gate(const uint32_t * /*gate*/, uint64_t /*budget_ns*/) {}
 };
 
 class Backend {

@@ -287,13 +287,6 @@ class LoBackend final : public Backend {
     }
 };
 
-LoRail *find_rail_by_name_locked(const std::string &name, int ordinal) {
-    int seen = 0;
-    for (auto &kv : Directory::get().rails)
-        if (kv.second->name() == name && seen++ == ordinal) return kv.second;
-    return nullptr;
-}
-
 }  // namespace
 
 std::unique_ptr<Backend> make_loopback_backend() { return std::make_unique<LoBackend>(); }

@@ -4,15 +4,24 @@
 // posted WR is resolved to a (src, dst) device-address pair and queued; the
 // doorbell (flush) turns every queued WR into one descriptor of a single
 // copy_batch launch — the sm_100a bulk-copy kernel — followed by an event.
-// poll() retires launches whose event completed and emits one completion
-// per WR, so the engine sees RC-verbs semantics.
+// The last CTA of every launch stores the launch's sequence number into a
+// host-mapped completion word of its QP; poll() reads that word (no driver
+// call on the hot path, so polling never contends for the CUDA driver's
+// locks with other launches) and emits one completion per WR, so the
+// engine sees RC-verbs semantics. An event per launch remains for error
+// detection: it is queried only for a launch pending longer than a while.
 //
 // Reachable memory:
 //   * this process's device memory on any GPU (peer access enabled),
 //   * this process's host memory (pinned + mapped at registration; UVA),
 //   * another process's device memory on the same host: registrations are
 //     published in /dev/shm/mpcomm-nvl.<boot>.<pid> (key, range, CUDA IPC
-//     handle) and opened with cudaIpcOpenMemHandle on first use.
+//     handle) and opened with cudaIpcOpenMemHandle on first use,
+//   * another process's host memory when it is a shared file mapping
+//     (/dev/shm, hugetlbfs, any MAP_SHARED file): the record carries the
+//     file path and offset; the peer maps the same pages, pins them and
+//     reaches them through its own UVA address. Private anonymous memory of
+//     another process is unreachable (WC remote-access error).
 // This replaces the reference's NVLink proxy copies (cuMemcpyPeerAsync +
 // host callbacks, src/mpcomm_pxn.cpp:638-814) with in-kernel stores.
 #include <fcntl.h>
@@ -26,6 +35,7 @@
 #include <deque>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <unordered_map>
 
 #include "core/core.h"
@@ -40,7 +50,7 @@ namespace mpcomm {
 namespace fabric {
 namespace {
 
-constexpr uint32_t kDirMagic = 0x4E564C44;  // "NVLD"
+constexpr uint32_t kDirMagic = 0x4E564C45;  // "NVLE": layout with file-backed host records
 constexpr size_t kDirSlots = 4096;
 
 struct DirRecord {
@@ -53,7 +63,36 @@ struct DirRecord {
     int32_t device;
     int32_t kind;  // 0 device memory, 1 host memory
     unsigned char ipc[gpu::kIpcHandleBytes];
+    uint64_t file_off;  // host memory: offset of `addr` in the backing file
+    char path[160];     // host memory: backing file ("" = private, unreachable)
 };
+
+// Backing file of a host range that lies inside one shared file mapping of
+// this process (from /proc/self/maps): path and the file offset of `addr`.
+bool shared_backing(uintptr_t addr, size_t len, std::string *path, uint64_t *off) {
+    FILE *f = fopen("/proc/self/maps", "r");
+    if (!f) return false;
+    char line[512];
+    bool found = false;
+    while (fgets(line, sizeof(line), f)) {
+        unsigned long lo = 0, hi = 0, foff = 0;
+        char perms[8] = {0};
+        int pos = 0;
+        if (sscanf(line, "%lx-%lx %7s %lx %*s %*s %n", &lo, &hi, perms, &foff, &pos) < 4) continue;
+        if (addr < lo || addr >= hi) continue;
+        if (addr + len > hi || perms[3] != 's' || pos <= 0) break;
+        std::string p(line + pos);
+        while (!p.empty() && (p.back() == '\n' || p.back() == ' ')) p.pop_back();
+        // Only a path another process can open (not "/memfd:... (deleted)").
+        if (p.empty() || p[0] != '/' || p.find(" (deleted)") != std::string::npos) break;
+        *path = p;
+        *off = foff + (addr - lo);
+        found = true;
+        break;
+    }
+    fclose(f);
+    return found;
+}
 
 struct DirHeader {
     uint32_t magic;
@@ -92,6 +131,8 @@ struct Region {
     bool pinned_by_us;
     int refs;
     size_t slot;
+    std::string path;   // host memory: shared backing file ("" if private)
+    uint64_t file_off;
 };
 
 // Process-wide registry of nvl registrations + the shared directory.
@@ -147,6 +188,7 @@ class Registry {
             r.base = r.addr;
             r.alloc_size = len;
             r.pinned_by_us = pinned;
+            if (!shared_backing(r.addr, len, &r.path, &r.file_off)) r.path.clear();
         }
         r.key = next_key_++;
         r.refs = 1;
@@ -225,6 +267,9 @@ class Registry {
             recs[i].device = r.dev;
             recs[i].kind = r.device ? 0 : 1;
             std::memcpy(recs[i].ipc, ipc, gpu::kIpcHandleBytes);
+            recs[i].file_off = r.file_off;
+            std::memset(recs[i].path, 0, sizeof(recs[i].path));
+            if (r.path.size() < sizeof(recs[i].path)) std::memcpy(recs[i].path, r.path.data(), r.path.size());
             __atomic_store_n(&recs[i].state, 1u, __ATOMIC_RELEASE);
             return i;
         }
@@ -247,8 +292,12 @@ class RemoteMaps {
         return m;
     }
     // Resolves [addr, addr+len) of process `pid`'s registration `key` to a
-    // pointer usable by kernels of this process. 0 on success.
-    int resolve(long pid, uint32_t key, uintptr_t addr, size_t len, uintptr_t *out) {
+    // pointer usable by kernels of this process on device `dev`. 0 on
+    // success. Sets *host when the memory is host DRAM (a PCIe-bound copy).
+    // IPC mappings belong to the context current when they are opened, so
+    // they are opened with `dev` current and cached per (pid, base, dev).
+    int resolve(long pid, uint32_t key, uintptr_t addr, size_t len, int dev, uintptr_t *out, bool *host) {
+        *host = false;
         std::lock_guard<std::mutex> g(mu_);
         const DirRecord *dir = open_dir(pid);
         if (!dir) return kWcRemAccessErr;
@@ -257,28 +306,20 @@ class RemoteMaps {
             DirRecord rec;
             std::memcpy(&rec, &dir[i], sizeof(rec));
             if (addr < rec.addr || addr + len > rec.addr + rec.len) return kWcRemAccessErr;
-            if (rec.kind != 0) return kWcRemAccessErr;  // remote host memory: not mappable
-            auto mk = std::make_pair(pid, rec.base);
-            auto it = opened_.find(mk);
-            if (it == opened_.end()) {
-                bool any = false;
-                for (size_t b = 0; b < gpu::kIpcHandleBytes; ++b) any |= rec.ipc[b] != 0;
-                if (!any) return kWcRemAccessErr;
-                void *p = nullptr;
-                int e = gpu::ipc_open_handle(rec.ipc, &p);
-                if (e != 0) {
-                    MPCOMM_LOG_ERROR("MPComm[nvl]: cudaIpcOpenMemHandle(pid %ld) failed: %s\n", pid,
-                                     gpu::error_string(e));
-                    return kWcRemAccessErr;
-                }
-                it = opened_.emplace(mk, reinterpret_cast<uintptr_t>(p)).first;
+            const int prev = gpu::current_device();
+            if (prev != dev) gpu::set_device(dev);
+            int st;
+            if (rec.kind != 0) {
+                *host = true;
+                st = resolve_host(pid, rec, addr, out);
+            } else {
+                st = resolve_device(pid, rec, addr, dev, out);
             }
-            *out = it->second + (addr - rec.base);
-            return 0;
+            if (prev >= 0 && prev != dev) gpu::set_device(prev);
+            return st;
         }
         return kWcRemAccessErr;
     }
-
  private:
     const DirRecord *open_dir(long pid) {
         auto it = dirs_.find(pid);
@@ -300,9 +341,67 @@ class RemoteMaps {
         return recs;
     }
 
+ public:
+    // Another process's shared host mapping: map the same file range here,
+    // pin it (mapped, portable) and cache the local base per (pid, key).
+    int resolve_host(long pid, const DirRecord &rec, uintptr_t addr, uintptr_t *out) {
+        auto mk = std::make_pair(pid, rec.key);
+        auto it = host_ranges_.find(mk);
+        if (it == host_ranges_.end()) {
+            if (rec.path[0] != '/') {
+                MPCOMM_LOG_WARN("MPComm[nvl]: pid %ld's host buffer 0x%lx is private memory; publish a "
+                                "shared mapping (e.g. /dev/shm) to reach it from another process\n",
+                                pid, static_cast<unsigned long>(rec.addr));
+                return kWcRemAccessErr;
+            }
+            std::string path(rec.path, strnlen(rec.path, sizeof(rec.path)));
+            const uint64_t page = static_cast<uint64_t>(sysconf(_SC_PAGESIZE));
+            const uint64_t off0 = rec.file_off & ~(page - 1);
+            const size_t span = static_cast<size_t>(rec.file_off - off0 + rec.len);
+            int fd = open(path.c_str(), O_RDWR);
+            if (fd < 0) return kWcRemAccessErr;
+            void *m = mmap(nullptr, span, PROT_READ | PROT_WRITE, MAP_SHARED, fd, static_cast<off_t>(off0));
+            close(fd);
+            if (m == MAP_FAILED) return kWcRemAccessErr;
+            char *base = static_cast<char *>(m) + (rec.file_off - off0);
+            void *dptr = nullptr;
+            bool pinned = false;
+            if (gpu::host_pin_mapped(base, rec.len, &dptr, &pinned) != 0 || dptr != base) {
+                if (pinned) gpu::host_unpin(base);
+                munmap(m, span);
+                MPCOMM_LOG_ERROR("MPComm[nvl]: cannot pin %s (pid %ld) for device access\n", path.c_str(), pid);
+                return kWcRemAccessErr;
+            }
+            it = host_ranges_.emplace(mk, reinterpret_cast<uintptr_t>(base)).first;
+        }
+        *out = it->second + (addr - rec.addr);
+        return 0;
+    }
+
+    int resolve_device(long pid, const DirRecord &rec, uintptr_t addr, int dev, uintptr_t *out) {
+        auto mk = std::make_tuple(pid, rec.base, dev);
+        auto it = opened_.find(mk);
+        if (it == opened_.end()) {
+            bool any = false;
+            for (size_t b = 0; b < gpu::kIpcHandleBytes; ++b) any |= rec.ipc[b] != 0;
+            if (!any) return kWcRemAccessErr;
+            void *p = nullptr;
+            int e = gpu::ipc_open_handle(rec.ipc, &p);
+            if (e != 0) {
+                MPCOMM_LOG_ERROR("MPComm[nvl]: cudaIpcOpenMemHandle(pid %ld) failed: %s\n", pid,
+                                 gpu::error_string(e));
+                return kWcRemAccessErr;
+            }
+            it = opened_.emplace(mk, reinterpret_cast<uintptr_t>(p)).first;
+        }
+        *out = it->second + (addr - rec.base);
+        return 0;
+    }
+
     std::mutex mu_;
     std::unordered_map<long, const DirRecord *> dirs_;
-    std::map<std::pair<long, uintptr_t>, uintptr_t> opened_;
+    std::map<std::tuple<long, uintptr_t, int>, uintptr_t> opened_;  // (pid, base, local dev)
+    std::map<std::pair<long, uint32_t>, uintptr_t> host_ranges_;  // portable pinned: any device
 };
 
 // gid = "nvl:<boot8>:<pid>:<dev>"
@@ -322,11 +421,16 @@ class NvlRail;
 
 struct Inflight {
     void *event;
+    uint64_t seq;  // value the launch's last CTA stores into the QP's done word
     std::vector<uint64_t> wr_ids;
     std::vector<uint32_t> lens;
     std::chrono::steady_clock::time_point launched;
     bool failed;
 };
+
+// A launch not retired through its done word after this long is checked
+// through its event (errors, lost context); later checks are spaced as much.
+constexpr auto kEventCheckAfter = std::chrono::microseconds(500);
 
 class NvlQp final : public QueuePair {
  public:
@@ -366,11 +470,15 @@ class NvlQp final : public QueuePair {
     long remote_pid_ = -1;
     int remote_dev_ = -1;
     void *stream_ = nullptr;
-    uint32_t *status_ = nullptr;
+    uint32_t *status_ = nullptr;     // device: [0] status word, [4] last-CTA counter
+    uint64_t *done_word_ = nullptr;  // host-mapped: sequence of the last finished launch
+    uint64_t seq_ = 0;
+    std::chrono::steady_clock::time_point next_check_{};
     std::vector<kern::CopyDesc> pending_;
     std::vector<uint64_t> pending_ids_;
     std::vector<uint32_t> pending_lens_;
     bool pending_host_ = false;
+    bool pending_h2d_ = false;  // a READ from host memory into this GPU's HBM
     std::deque<Inflight> inflight_;
 };
 
@@ -417,10 +525,8 @@ class NvlRail final : public Rail {
 
     int poll(WorkCompletion *out, int max) override {
         std::lock_guard<std::mutex> g(mu_);
-        if (cq_.size() < static_cast<size_t>(max)) {
-            gpu::set_device(dev_);
+        if (cq_.size() < static_cast<size_t>(max))
             for (NvlQp *qp : qps_) qp->reap(&cq_);
-        }
         int n = 0;
         while (n < max && !cq_.empty()) {
             out[n++] = cq_.front();
@@ -442,13 +548,21 @@ class NvlRail final : public Rail {
         override_stream_ = stream;
         return 0;
     }
+    void set_qos_gate(const uint32_t *gate, uint64_t budget_ns) override {
+        std::lock_guard<std::mutex> g(mu_);
+        qos_gate_ = gate;
+        qos_budget_ns_ = gate ? budget_ns : 0;
+    }
 
-    // Launch geometry: a copy touching host memory is PCIe-bound and gets a
-    // small grid (leaves SMs free for H2D kernels); device-to-device copies
-    // share the GPU among the QPs (or take all of it on one caller stream).
+    // Launch geometry: a copy touching host memory is PCIe-bound: 2 CTAs
+    // per QP already saturate a Gen5 x16 link (measured: 4 x 1 GiB PUT/GET
+    // at 51.6-51.9 GB/s for 2..32 CTAs), so it gets 4 — fewer SMs held and
+    // fewer loads queued ahead of a concurrent H2D gather. Device-to-device
+    // copies share the GPU among the QPs (or take all of it on one caller
+    // stream).
     int ctas_for(bool host) const {
         if (cfg_.nvl_ctas_per_qp > 0) return cfg_.nvl_ctas_per_qp;
-        if (host) return sms_ < 32 ? sms_ : 32;
+        if (host) return sms_ < 4 ? sms_ : 4;
         if (override_stream_) return sms_;
         int q = static_cast<int>(cfg_.qps_per_connection);
         int c = q > 0 ? sms_ / q : sms_;
@@ -467,6 +581,8 @@ class NvlRail final : public Rail {
     std::mutex mu_;
     int dev_;
     void *override_stream_ = nullptr;
+    const uint32_t *qos_gate_ = nullptr;  // device QoS gate for H2D copies
+    uint64_t qos_budget_ns_ = 0;
     std::deque<WorkCompletion> cq_;
 
  private:
@@ -485,19 +601,26 @@ NvlQp::NvlQp(NvlRail *rail, uint32_t qpn) : rail_(rail), qpn_(qpn) {
     gpu::set_device(rail_->dev_);
     status_ = static_cast<uint32_t *>(gpu::device_alloc(64));
     if (status_) gpu::memset_device(status_, 0, 64);
+    done_word_ = static_cast<uint64_t *>(gpu::host_alloc_mapped(64));
     if (prev >= 0) gpu::set_device(prev);
 }
 
 NvlQp::~NvlQp() {
     if (stream_) gpu::stream_sync(stream_);
     {
+        // Launches may sit on a caller stream: wait for each (they are
+        // bounded) before the words they write are freed.
         std::lock_guard<std::mutex> g(rail_->mu_);
-        for (auto &f : inflight_) rail_->give_event(f.event);
+        for (auto &f : inflight_) {
+            gpu::event_sync(f.event);
+            rail_->give_event(f.event);
+        }
         inflight_.clear();
     }
     rail_->forget(this);
     gpu::stream_destroy(stream_);
     gpu::device_free(status_);
+    gpu::host_free(done_word_);
 }
 
 int NvlQp::to_rtr(const EndpointInfo &remote) {
@@ -563,7 +686,8 @@ int NvlQp::post(const WorkRequest *wrs, size_t n) {
             rptr = wr.remote_addr;
             remote_host = !rr.device;
         } else {
-            int st = RemoteMaps::get().resolve(remote_pid_, wr.rkey, wr.remote_addr, wr.length, &rptr);
+            int st = RemoteMaps::get().resolve(remote_pid_, wr.rkey, wr.remote_addr, wr.length, rail_->dev_, &rptr,
+                                               &remote_host);
             if (st != 0) {
                 rail_->cq_.push_back(WorkCompletion{wr.wr_id, st, 0});
                 continue;
@@ -583,6 +707,7 @@ int NvlQp::post(const WorkRequest *wrs, size_t n) {
         pending_ids_.push_back(wr.wr_id);
         pending_lens_.push_back(wr.length);
         pending_host_ |= remote_host || !lr.device;
+        pending_h2d_ |= wr.op == Opcode::kRead && remote_host && lr.device;
     }
     return 0;
 }
@@ -600,9 +725,15 @@ void NvlQp::flush() {
         Inflight f;
         f.event = nullptr;
         f.failed = false;
+        f.seq = ++seq_;
         f.wr_ids.assign(pending_ids_.begin() + i, pending_ids_.begin() + i + n);
         f.lens.assign(pending_lens_.begin() + i, pending_lens_.begin() + i + n);
-        int e = kern::copy_batch(pending_.data() + i, static_cast<int>(n), ctas, stream, status_, nullptr);
+        const bool gated = pending_h2d_ && rail_->qos_gate_;
+        int e = done_word_ ? 0 : -1;
+        if (e == 0)
+            e = kern::copy_batch(pending_.data() + i, static_cast<int>(n), ctas, stream, status_, nullptr,
+                                 kern::kModeAuto, gated ? rail_->qos_gate_ : nullptr,
+                                 gated ? rail_->qos_budget_ns_ : 0, done_word_, f.seq, status_ + 4);
         if (e == 0) {
             f.event = rail_->take_event();
             if (!f.event || gpu::event_record(f.event, stream) != 0) e = -1;
@@ -623,13 +754,40 @@ void NvlQp::flush() {
     pending_ids_.clear();
     pending_lens_.clear();
     pending_host_ = false;
+    pending_h2d_ = false;
 }
 
 void NvlQp::reap(std::deque<WorkCompletion> *cq) {
+    if (inflight_.empty()) return;
+    uint64_t done = __atomic_load_n(done_word_, __ATOMIC_ACQUIRE);
     while (!inflight_.empty()) {
         Inflight &f = inflight_.front();
-        int q = gpu::event_query(f.event);
-        if (q == 0) return;
+        int q = 1;
+        if (f.seq > done && !f.failed) {
+            // Not signalled yet: consult the event only now and then.
+            const auto now = std::chrono::steady_clock::now();
+            if (now - f.launched < kEventCheckAfter || now < next_check_) return;
+            next_check_ = now + kEventCheckAfter;
+            gpu::set_device(rail_->dev_);  // the event belongs to this rail's device
+            q = gpu::event_query(f.event);
+            if (q < 0)
+                MPCOMM_LOG_WARN("MPComm[nvl]: launch %lu on %s failed: %s\n", static_cast<unsigned long>(f.seq),
+                                rail_->name().c_str(), gpu::error_string(-q));
+            if (q == 0) return;
+            // The event completed, so the kernel's last store (the done
+            // word) has been issued: allow it a moment to land, then treat
+            // a missing word as a failed launch.
+            for (int spin = 0; q > 0 && spin < 1000; ++spin) {
+                done = __atomic_load_n(done_word_, __ATOMIC_ACQUIRE);
+                if (f.seq <= done) break;
+                cpu_relax();
+            }
+            if (q > 0 && f.seq > done) {
+                MPCOMM_LOG_WARN("MPComm[nvl]: launch %lu on %s completed without its done word\n",
+                                static_cast<unsigned long>(f.seq), rail_->name().c_str());
+                q = -1;
+            }
+        }
         bool bad = f.failed || q < 0;
         if (!bad) {
             // A kernel can only have timed out if it ran at least the wait
@@ -637,6 +795,7 @@ void NvlQp::reap(std::deque<WorkCompletion> *cq) {
             double ran = std::chrono::duration<double>(std::chrono::steady_clock::now() - f.launched).count();
             if (ran * 1e9 >= 0.9 * static_cast<double>(kern::wait_budget_ns())) {
                 uint32_t st = 0;
+                gpu::set_device(rail_->dev_);
                 gpu::copy_d2h_sync(&st, status_, sizeof(st));
                 if (st) {
                     bad = true;

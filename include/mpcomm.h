@@ -211,6 +211,10 @@ class MPComm {
     void enableH2DQoS(uint64_t rate_bytes_per_sec = 0, uint64_t burst_bytes = 0);
     void setH2DQoSPolicy(uint64_t rate_bytes_per_sec, uint64_t burst_bytes = 0);
     bool isH2DQoSEnabled() const;
+    // Extension: device timestamps (%globaltimer, ns) of the most recently
+    // closed H2D window on GPU `gpu`: first CTA start and last CTA end of a
+    // tmaGather/tmaScatter launched while QoS was enabled. False if none.
+    bool getLastH2DWindow(int gpu, uint64_t *begin_ns, uint64_t *end_ns) const;
     void disableH2DQoS();
     uint64_t getNicCompletedBytes() const;
     // Extension: completed bytes per rail, in getActiveDevices() order (how

@@ -128,18 +128,40 @@ def node_cpus(node: int) -> Optional[set]:
 
 class LocalBuffer:
     """A registered-ready byte buffer: host DRAM placed on `numa` by first
-    touch from that node's CPUs, or HBM of `gpu` (torch allocation)."""
+    touch from that node's CPUs, or HBM of `gpu` (torch allocation).
+
+    Host buffers are shared file mappings under /dev/shm (removed on close),
+    so the GPU fabric of another process on this host can map and reach
+    them; private anonymous memory is the fallback where /dev/shm is absent.
+    """
+
+    _count = 0
 
     def __init__(self, nbytes: int, numa: int = -1, gpu: int = -1):
         self.nbytes, self.numa, self.gpu = nbytes, numa, gpu
+        self.path = None
         if gpu >= 0:
             import torch
             self.tensor = torch.zeros(nbytes, dtype=torch.uint8, device=f"cuda:{gpu}")
             self.ptr = self.tensor.data_ptr()
             self._mm = None
             return
-        self._mm = mmap.mmap(-1, max(nbytes, 1), mmap.MAP_PRIVATE | mmap.MAP_ANONYMOUS,
-                             mmap.PROT_READ | mmap.PROT_WRITE)
+        LocalBuffer._count += 1
+        path = f"/dev/shm/mpcomm-harness.{os.getpid()}.{LocalBuffer._count}"
+        try:
+            fd = os.open(path, os.O_RDWR | os.O_CREAT | os.O_EXCL, 0o600)
+        except OSError:
+            fd = -1
+        if fd >= 0:
+            try:
+                os.ftruncate(fd, max(nbytes, 1))
+                self._mm = mmap.mmap(fd, max(nbytes, 1), mmap.MAP_SHARED, mmap.PROT_READ | mmap.PROT_WRITE)
+                self.path = path
+            finally:
+                os.close(fd)
+        else:
+            self._mm = mmap.mmap(-1, max(nbytes, 1), mmap.MAP_PRIVATE | mmap.MAP_ANONYMOUS,
+                                 mmap.PROT_READ | mmap.PROT_WRITE)
         self._cbuf = (ctypes.c_char * max(nbytes, 1)).from_buffer(self._mm)
         self.ptr = ctypes.addressof(self._cbuf)
         saved = os.sched_getaffinity(0)
@@ -180,6 +202,12 @@ class LocalBuffer:
             del self._cbuf
             self._mm.close()
             self._mm = None
+        if self.path:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+            self.path = None
         self.tensor = None
 
 

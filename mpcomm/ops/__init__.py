@@ -103,11 +103,15 @@ def crc32_host(data: bytes, crc: int = 0) -> int:
 
 
 def copy_spans(srcs: Sequence[int], dsts: Sequence[int], lengths: Sequence[int], max_ctas: int = 0,
-               stream: Optional[torch.cuda.Stream] = None, mode: int = MODE_AUTO) -> None:
+               stream: Optional[torch.cuda.Stream] = None, mode: int = MODE_AUTO, gate: int = 0,
+               gate_budget_ns: int = 0) -> None:
     """Copies up to 64 spans in one launch (bulk pipeline, or the vector SM
-    kernel with ``mode=MODE_SM``); any device-reachable addresses."""
-    _check(_native.copy_spans(list(srcs), list(dsts), list(lengths), max_ctas, _stream_ptr(stream), mode),
-           "copy_spans")
+    kernel with ``mode=MODE_SM``); any device-reachable addresses. ``gate``
+    (a device uint32 address) makes every pipeline pause before its next
+    tile while the word is non-zero, for at most ``gate_budget_ns`` in total
+    per pipeline (the QoS yield of background copies)."""
+    _check(_native.copy_spans(list(srcs), list(dsts), list(lengths), max_ctas, _stream_ptr(stream), mode,
+                              gate, gate_budget_ns), "copy_spans")
 
 
 def pxn_gather_forward(pool_ptr: int, pool_blocks: int, indices: torch.Tensor, dst_ptr: int,

@@ -102,6 +102,15 @@ class PyMPComm {
     void enable_h2d_qos(uint64_t r, uint64_t b) { c_.enableH2DQoS(r, b); }
     void set_h2d_qos_policy(uint64_t r, uint64_t b) { c_.setH2DQoSPolicy(r, b); }
     bool is_h2d_qos_enabled() const { return c_.isH2DQoSEnabled(); }
+    py::object get_last_h2d_window(int gpu) const {
+        uint64_t b = 0, e = 0;
+        if (!c_.getLastH2DWindow(gpu, &b, &e)) return py::none();
+        py::dict d;
+        d["begin_ns"] = b;
+        d["end_ns"] = e;
+        d["duration_us"] = e > b ? (e - b) / 1000.0 : 0.0;
+        return d;
+    }
     void disable_h2d_qos() { c_.disableH2DQoS(); }
     uint64_t get_nic_completed_bytes() const { return c_.getNicCompletedBytes(); }
     std::vector<uint64_t> get_rail_completed_bytes() const { return c_.getRailCompletedBytes(); }
@@ -325,6 +334,7 @@ PYBIND11_MODULE(_mpcomm, m) {
         .def("enable_h2d_qos", &C::enable_h2d_qos, py::arg("rate_bytes_per_sec") = 0, py::arg("burst_bytes") = 0)
         .def("set_h2d_qos_policy", &C::set_h2d_qos_policy, py::arg("rate_bytes_per_sec"), py::arg("burst_bytes") = 0)
         .def("is_h2d_qos_enabled", &C::is_h2d_qos_enabled)
+        .def("get_last_h2d_window", &C::get_last_h2d_window, py::arg("gpu") = 0)
         .def("disable_h2d_qos", &C::disable_h2d_qos)
         .def("get_nic_completed_bytes", &C::get_nic_completed_bytes)
         .def("get_rail_completed_bytes", &C::get_rail_completed_bytes)
@@ -421,7 +431,7 @@ PYBIND11_MODULE(_mpcomm, m) {
           py::arg("block_size"), py::arg("mode") = 0, py::arg("max_ctas") = 0, py::arg("stream") = 0);
     m.def("copy_spans",
           [](const std::vector<uintptr_t> &src, const std::vector<uintptr_t> &dst, const std::vector<uint64_t> &len,
-             int max_ctas, uintptr_t stream, int mode) {
+             int max_ctas, uintptr_t stream, int mode, uintptr_t gate, uint64_t gate_budget_ns) {
               if (src.size() != dst.size() || src.size() != len.size() || src.size() > kern::kMaxCopyDescs)
                   return static_cast<int>(MPCOMM_ERR_INVALID_ARG);
               std::vector<kern::CopyDesc> d(src.size());
@@ -429,10 +439,11 @@ PYBIND11_MODULE(_mpcomm, m) {
                   d[i] = kern::CopyDesc{reinterpret_cast<const void *>(src[i]), reinterpret_cast<void *>(dst[i]), len[i]};
               py::gil_scoped_release r;
               return kern::copy_batch(d.data(), static_cast<int>(d.size()), max_ctas,
-                                      reinterpret_cast<void *>(stream), nullptr, nullptr, mode);
+                                      reinterpret_cast<void *>(stream), nullptr, nullptr, mode,
+                                      reinterpret_cast<const uint32_t *>(gate), gate_budget_ns);
           },
           py::arg("src"), py::arg("dst"), py::arg("lengths"), py::arg("max_ctas") = 0, py::arg("stream") = 0,
-          py::arg("mode") = 0);
+          py::arg("mode") = 0, py::arg("gate") = 0, py::arg("gate_budget_ns") = 0);
     m.def("pxn_gather_forward",
           [](uintptr_t pool, int64_t pool_blocks, uintptr_t idx, uintptr_t dst, int64_t n, int64_t bs, int max_ctas,
              uintptr_t stream, uintptr_t flag, uint64_t flag_value, uintptr_t ctr) {

@@ -117,6 +117,35 @@ def test_copy_spans_mixed_alignment():
         assert torch.equal(dst[b:b + n], src[a:a + n])
 
 
+@pytest.mark.parametrize("mode", [ops.MODE_AUTO, ops.MODE_SM])
+def test_copy_gate_pauses_then_fails_open(mode):
+    """A copy given a QoS gate pauses before each tile while the gate word
+    is non-zero, for at most gate_budget_ns per pipeline, then finishes the
+    copy anyway (bit-exact); with the gate at zero it does not pause."""
+    src = torch.randint(0, 256, (8 << 20,), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros_like(src)
+    gate = torch.zeros(32, dtype=torch.int32, device="cuda")
+    budget = 40_000_000  # 40 ms
+
+    def timed():
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops.copy_spans([src.data_ptr()], [dst.data_ptr()], [src.numel()], max_ctas=8, mode=mode,
+                       gate=gate.data_ptr(), gate_budget_ns=budget)
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    timed()  # warm-up
+    open_ms = timed()
+    assert open_ms < 20, open_ms
+    gate[0] = 1
+    dst.zero_()
+    held_ms = timed()
+    assert torch.equal(dst, src)
+    assert 0.9 * budget / 1e6 <= held_ms < 20 * budget / 1e6, held_ms
+
+
 def test_bounded_flag_wait_times_out_and_context_survives():
     """A wait on a flag nothing sets ends with a status bit, not a hang."""
     flag = torch.zeros(1, dtype=torch.int64, device="cuda")
