@@ -6,7 +6,14 @@
 //   initiator:  scatter_test --target T:10.0.0.2:5000 --size 1G --batch-size 4 \
 //                            --test-type put,get --iterations 10 --warmup 3 [--gpu 0]
 //   both:       scatter_test --mode both --buffer-size 4G --size 1G ...  (serves its own
-//               buffer and targets itself: the single-box memory-pool setup)
+//               buffer and targets itself: the single-box memory-pool setup; with
+//               --target options it serves AND initiates to those targets, the
+//               multi-initiator setup where every host runs one process)
+// Orchestration: --ready-file P is written once the buffer is served,
+// --wait-go-file P delays the tests until P exists, --hold-file P keeps a
+// "both" process serving after its tests until P exists (at most
+// --hold-timeout s), --done-file P is written when its tests are finished,
+// --json prints one JSON line per test.
 // GB/s = bytes / 1e9 / wall seconds of the timed iterations (as the reference).
 // --gpu N puts the local (and served) buffers in HBM of GPU N (cudaMalloc).
 #include <cuda_runtime.h>
@@ -77,7 +84,8 @@ void usage(const char *prog) {
         "Usage: %s [--mode initiator|target|both] [--host-id ID] [--device DEVS] [--tcp-port P]\n"
         "          [--target ID:ADDR:PORT]... [--size S] [--buffer-size S] [--batch-size B]\n"
         "          [--iterations N] [--warmup W] [--test-type put,get,scatter,gather,broadcast]\n"
-        "          [--gpu N] [--wait-go-file PATH] [--verbose]\n"
+        "          [--gpu N] [--wait-go-file PATH] [--ready-file PATH] [--hold-file PATH]\n"
+        "          [--hold-timeout S] [--done-file PATH] [--json] [--verbose]\n"
         "Sizes take K/M/G/T suffixes. Fabric: MPCOMM_FABRIC (auto|nvl|ib|sock|lo).\n",
         prog);
 }
@@ -85,10 +93,10 @@ void usage(const char *prog) {
 }  // namespace
 
 int main(int argc, char **argv) {
-    std::string mode = "initiator", host_id = "test:0", devices, tests = "put,get", go_file;
-    int tcp_port = 0, iters = 10, warmup = 3, gpu = -1;
+    std::string mode = "initiator", host_id = "test:0", devices, tests = "put,get", go_file, ready_file, hold_file, done_file;
+    int tcp_port = 0, iters = 10, warmup = 3, gpu = -1, hold_timeout = 600;
     size_t size = 1ull << 30, buf_size = 0, batch = 4;
-    bool verbose = false;
+    bool verbose = false, json = false;
     std::vector<Target> targets;
     for (int i = 1; i < argc; ++i) {
         std::string a = argv[i];
@@ -109,6 +117,11 @@ int main(int argc, char **argv) {
         else if (a == "--test-type") tests = next();
         else if (a == "--gpu") gpu = std::atoi(next().c_str());
         else if (a == "--wait-go-file") go_file = next();
+        else if (a == "--ready-file") ready_file = next();
+        else if (a == "--hold-file") hold_file = next();
+        else if (a == "--done-file") done_file = next();
+        else if (a == "--hold-timeout") hold_timeout = std::atoi(next().c_str());
+        else if (a == "--json") json = true;
         else if (a == "--verbose" || a == "-v") verbose = true;
         else if (a == "--help" || a == "-h") return usage(argv[0]), 0;
         else return usage(argv[0]), 2;
@@ -129,17 +142,31 @@ int main(int argc, char **argv) {
         comm.startAcceptThread();
         std::printf("[scatter_test] serving %zu bytes at %p (ready)\n", buf_size, served);
         std::fflush(stdout);
+        if (!ready_file.empty()) {
+            const std::string tmp = ready_file + ".tmp";
+            if (FILE *f = std::fopen(tmp.c_str(), "w")) {
+                std::fprintf(f, "%d\n", comm.getTcpPort());
+                std::fclose(f);
+                std::rename(tmp.c_str(), ready_file.c_str());
+            }
+        }
         if (mode == "target") {
             for (;;) {
                 std::this_thread::sleep_for(std::chrono::seconds(verbose ? 5 : 60));
                 if (verbose) std::printf("[scatter_test] published=%zu\n", comm.getPublishedBufferCount());
             }
         }
-        targets.push_back(Target{"self", "127.0.0.1", comm.getTcpPort()});
+        if (targets.empty()) targets.push_back(Target{"self", "127.0.0.1", comm.getTcpPort()});
     }
     if (targets.empty()) return usage(argv[0]), 2;
-    if (!go_file.empty())
-        while (access(go_file.c_str(), F_OK) != 0) std::this_thread::sleep_for(std::chrono::milliseconds(50));
+    if (!go_file.empty()) {
+        const auto until = std::chrono::steady_clock::now() + std::chrono::seconds(hold_timeout);
+        while (access(go_file.c_str(), F_OK) != 0) {
+            if (std::chrono::steady_clock::now() >= until)
+                return std::fprintf(stderr, "no go file %s after %d s\n", go_file.c_str(), hold_timeout), 1;
+            std::this_thread::sleep_for(std::chrono::milliseconds(50));
+        }
+    }
 
     std::vector<uintptr_t> remote;
     for (auto &t : targets) {
@@ -192,7 +219,20 @@ int main(int argc, char **argv) {
         const double bytes = static_cast<double>(size) * batch * targets.size() * iters;
         std::printf("--- %s Summary: size=%zu batch=%zu targets=%zu iters=%d  %.3f GB/s  (%.3f ms/round)\n",
                     tt.c_str(), size, batch, targets.size(), iters, bytes / 1e9 / s, s * 1e3 / iters);
+        if (json)
+            std::printf("{\"tool\": \"scatter_test\", \"host\": \"%s\", \"test\": \"%s\", \"size\": %zu, "
+                        "\"batch\": %zu, \"targets\": %zu, \"iters\": %d, \"gbps\": %.4f, \"ms_per_round\": %.4f}\n",
+                        host_id.c_str(), tt.c_str(), size, batch, targets.size(), iters, bytes / 1e9 / s,
+                        s * 1e3 / iters);
         std::fflush(stdout);
+    }
+    if (!done_file.empty())
+        if (FILE *f = std::fopen(done_file.c_str(), "w")) std::fclose(f);
+    if (!hold_file.empty() && served) {
+        // Keep serving for the other initiators until released (bounded).
+        const auto until = std::chrono::steady_clock::now() + std::chrono::seconds(hold_timeout);
+        while (access(hold_file.c_str(), F_OK) != 0 && std::chrono::steady_clock::now() < until)
+            std::this_thread::sleep_for(std::chrono::milliseconds(50));
     }
     comm.shutdown();
     return 0;

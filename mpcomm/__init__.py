@@ -14,6 +14,9 @@ Subpackages:
   * ``mpcomm.models``   workload shapes the benchmarks use (Llama-3-8B paged
                         KV pool, RL rollout / expert-ID batches).
   * ``mpcomm.utils``    timing, clock sampling, seeds.
+  * ``mpcomm.harness``  target / initiator command-line harness.
+  * ``mpcomm.deploy``   multi-host orchestration (hosts.txt / jobs.txt over
+                        SSH), environment profiles, link monitor.
 """
 import glob as _glob
 import os as _os
@@ -45,7 +48,7 @@ except ImportError as _e:  # pragma: no cover - exercised only on broken install
     ) from _e
 
 
-_SUBPACKAGES = ("ops", "parallel", "models", "utils", "bench")
+_SUBPACKAGES = ("ops", "parallel", "models", "utils", "bench", "harness", "deploy")
 
 
 def __getattr__(name):
@@ -67,6 +70,16 @@ def get_include_dir() -> str:
     """Directory holding mpcomm.h / mpcomm_log.h (wheel: mpcomm/include; source tree: include/)."""
     inside = _os.path.join(_PACKAGE_DIR, "include")
     return inside if _os.path.isdir(inside) else _os.path.join(_os.path.dirname(_PACKAGE_DIR), "include")
+
+
+def tool_path(name: str) -> str:
+    """Path of a bundled command-line tool (``scatter_test``, ``hello_mpcomm``):
+    mpcomm/bin in a wheel, examples/bin in a source-tree build."""
+    for d in (_os.path.join(_PACKAGE_DIR, "bin"), _os.path.join(_os.path.dirname(_PACKAGE_DIR), "examples", "bin")):
+        p = _os.path.join(d, name)
+        if _os.path.isfile(p) and _os.access(p, _os.X_OK):
+            return p
+    raise FileNotFoundError(f"mpcomm tool '{name}' is not built (looked in mpcomm/bin and examples/bin)")
 
 
 def get_lib_dir() -> str:
