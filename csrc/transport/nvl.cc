@@ -25,11 +25,13 @@
 // This replaces the reference's NVLink proxy copies (cuMemcpyPeerAsync +
 // host callbacks, src/mpcomm_pxn.cpp:638-814) with in-kernel stores.
 #include <fcntl.h>
+#include <signal.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
 
 #include <atomic>
+#include <cerrno>
 #include <chrono>
 #include <cstring>
 #include <deque>
@@ -661,6 +663,17 @@ int NvlQp::post(const WorkRequest *wrs, size_t n) {
     QpState s = state_.load();
     if (s != QpState::kRts && s != QpState::kErr) return MPCOMM_ERR_CONNECTION;
     std::lock_guard<std::mutex> g(rail_->mu_);
+    // Peer liveness, checked on the host before anything is launched at the
+    // peer's memory: once its process is gone, WRs complete with
+    // retry-exceeded and the QP enters the error state (RC semantics).
+    if (s == QpState::kRts && remote_pid_ > 0 && remote_pid_ != getpid() &&
+        kill(static_cast<pid_t>(remote_pid_), 0) != 0 && errno == ESRCH) {
+        MPCOMM_LOG_WARN("MPComm[nvl]: peer process %ld is gone; QP %u on %s -> error\n", remote_pid_, qpn_,
+                        rail_->name().c_str());
+        for (size_t i = 0; i < n; ++i) rail_->cq_.push_back(WorkCompletion{wrs[i].wr_id, kWcRetryExcErr, 0});
+        state_ = QpState::kErr;
+        return 0;
+    }
     for (size_t i = 0; i < n; ++i) {
         const WorkRequest &wr = wrs[i];
         if (s == QpState::kErr) {

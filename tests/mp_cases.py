@@ -9,10 +9,14 @@ non-zero on any mismatch.
           lands in rank r's memory.
   nvls    NVLS multicast broadcast from rank 0 (falls back to P2P fan-out
           where multicast is unavailable) of a rollout-style batch.
+  peer_exit  (2 ranks) rank 1 leaves between steps; rank 0's next PUT to it
+          fails on the host, fast, and its engine keeps working.
 """
 import argparse
+import datetime
 import os
 import sys
+import time
 import zlib
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -132,11 +136,76 @@ def case_nvls(rank, world):
         print(f"nvls case used: {used}", flush=True)
 
 
+def case_peer_exit(rank, world):
+    """Rank 1 leaves between steps (its MPComm shut down, nothing in flight)
+    and tells rank 0 through the store. Rank 0's next PUT to it must fail
+    fast on the host (peer liveness check, no launch at the dead peer's
+    memory) and rank 0's engine must stay usable."""
+    n = 8 << 20
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    inbox = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    comm = mpcomm.MPComm()
+    assert comm.init(f"r{rank}") == 0 and comm.start_accept_thread() == 0
+    for t in (src, inbox):
+        assert comm.register_memory(t.data_ptr(), n) == 0
+    assert comm.publish_buffer(inbox.data_ptr(), n) == 0
+    info = [None] * world
+    dist.all_gather_object(info, (comm.get_tcp_port(), os.getpid()))
+    peer = rank ^ 1
+    assert comm.connect("peer", "127.0.0.1", info[peer][0]) == 0
+    remote = comm.query_remote_buffers("peer", "127.0.0.1", info[peer][0])["buffers"][0]["addr"]
+    h = comm.put_async(src.data_ptr(), "peer", remote, n)
+    assert comm.wait_transfer(h, 60000) == 0
+    comm.release_transfer(h)
+    torch.cuda.synchronize()
+    dist.barrier()  # step 1 done on both sides
+    store = dist.distributed_c10d._get_default_store()
+    if rank == 1:
+        comm.shutdown()
+        store.set("r1_left", "1")
+        return True
+    store.wait(["r1_left"], datetime.timedelta(seconds=60))
+    deadline = time.time() + 60
+    while time.time() < deadline:
+        try:
+            os.kill(info[1][1], 0)
+        except ProcessLookupError:
+            break
+        time.sleep(0.05)
+    else:
+        raise AssertionError("rank 1 did not exit")
+    t0 = time.time()
+    h = comm.put_async(src.data_ptr(), "peer", remote, n)
+    rc = comm.wait_transfer(h, 20000) if h else -1
+    if h:
+        comm.release_transfer(h)
+    assert rc != 0 and rc != int(mpcomm.MPCommError.ERR_TIMEOUT), rc
+    assert time.time() - t0 < 10, "failure took too long to surface"
+    # The engine is still usable: PUT into a pinned host pool of our own.
+    pool = torch.zeros(n, dtype=torch.uint8, pin_memory=True)
+    assert comm.register_memory(pool.data_ptr(), n) == 0 and comm.publish_buffer(pool.data_ptr(), n) == 0
+    port = comm.get_tcp_port()
+    assert comm.connect("self", "127.0.0.1", port) == 0 and comm.query_remote_buffers("self", "127.0.0.1", port)
+    h = comm.put_async(src.data_ptr(), "self", pool.data_ptr(), n)
+    assert comm.wait_transfer(h, 60000) == 0
+    comm.release_transfer(h)
+    assert torch.equal(pool, src.cpu())
+    comm.shutdown()
+    return True
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["putget", "pxn", "nvls", "all"])
+    p.add_argument("case", choices=["putget", "pxn", "nvls", "peer_exit", "all"])
     a = p.parse_args()
     rank, world, _ = parallel.init_from_env("gloo")
+    if a.case == "peer_exit":
+        # Ranks leave independently: no final collective.
+        if rank < 2:
+            case_peer_exit(rank, world)
+        if rank == 0:
+            print("case peer_exit ok", flush=True)
+        os._exit(0)
     cases = ["putget", "pxn", "nvls"] if a.case == "all" else [a.case]
     for c in cases:
         globals()[f"case_{c}"](rank, world)

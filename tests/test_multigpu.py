@@ -18,12 +18,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("case", ["putget", "pxn", "nvls"])
+@pytest.mark.parametrize("case", ["putget", "pxn", "nvls", "peer_exit"])
 def test_multigpu_case(case):
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs >= 2 GPUs")
-    n = min(n, 8)
+    n = 2 if case == "peer_exit" else min(n, 8)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(ROOT, "tests", "mp_cases.py"), case]
