@@ -91,6 +91,7 @@ struct Connection {
 
 struct Transfer {
     uint64_t handle = 0;
+    uint64_t nvtx = 0;  // NVTX range of the transfer's lifetime (0 = none)
     Direction dir = Direction::kScatter;
     fabric::Opcode op = fabric::Opcode::kWrite;
     uintptr_t local_addr = 0;

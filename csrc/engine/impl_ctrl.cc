@@ -10,6 +10,7 @@
 #include <cstring>
 #include <set>
 
+#include "core/nvtx.h"
 #include "cuda/gpu.h"
 #include "engine/impl.h"
 #include "mpcomm_log.h"
@@ -131,6 +132,7 @@ fabric::EndpointInfo to_ep(const RemoteEndpointInfo &r) {
 }  // namespace
 
 int MPComm::Impl::connect(const std::string &id, const std::string &addr, int port) {
+    nvtx::Range range("mpcomm::connect");
     if (!initialized_) return MPCOMM_ERR_CONTEXT;
     int fd = net::connect_tcp(addr, port, net::ctrl_timeout_ms());
     if (fd < 0) return MPCOMM_ERR_CONNECTION;

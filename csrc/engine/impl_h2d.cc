@@ -5,6 +5,7 @@
 // pool, SM counts cached per device, no printf, AUTO picks by alignment.
 #include <cstring>
 
+#include "core/nvtx.h"
 #include "cuda/gpu.h"
 #include "engine/impl.h"
 #include "mpcomm_log.h"
@@ -69,6 +70,7 @@ int MPComm::Impl::h2dMove(bool gather, uintptr_t dram, const int64_t *idx, void 
             }
         }
     }
+    nvtx::Range range(gather ? "mpcomm::tmaGather" : "mpcomm::tmaScatter");
     kern::H2DWindow *win = nullptr;
     uint32_t *ctr = nullptr;
     if (isH2DQoSEnabled()) acquireH2DWindow(gpu::device_of(gpu_buf), &win, &ctr);

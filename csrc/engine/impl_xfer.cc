@@ -7,6 +7,7 @@
 #include <limits>
 #include <thread>
 
+#include "core/nvtx.h"
 #include "cuda/gpu.h"
 #include "engine/impl.h"
 #include "engine/staging.h"
@@ -87,6 +88,14 @@ TransferHandle MPComm::Impl::submit(uintptr_t local, const std::vector<std::stri
         return INVALID_TRANSFER_HANDLE;
     }
     t->local_gpu = region.gpu;
+    if (nvtx::enabled()) {
+        size_t total = 0;
+        for (size_t l : lens) total += l;
+        char msg[96];
+        std::snprintf(msg, sizeof(msg), "mpcomm %s %zu B x%zu #%lu", op, total, hosts.size(),
+                      static_cast<unsigned long>(t->handle));
+        t->nvtx = nvtx::start(msg);
+    }
     if (cfg_.pcie_stat_enable && dir != Direction::kGather) {
         t->remote_gpu.resize(hosts.size(), -1);
         for (size_t i = 0; i < hosts.size(); ++i) t->remote_gpu[i] = t->conns[i]->remote_gpu_for(raddrs[i]);
@@ -599,6 +608,7 @@ void MPComm::Impl::releaseTransfer(TransferHandle h) {
 
 void MPComm::Impl::finishTransfer(Transfer *t) {
     t->t_end = Clock::now();
+    nvtx::end(t->nvtx);
     t->finished.store(true, std::memory_order_release);
     if (t->life.fetch_or(1) & 2) {
         handle_table_[t->handle].store(nullptr, std::memory_order_release);

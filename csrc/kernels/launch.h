@@ -6,6 +6,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <vector>
 
 namespace mpcomm {
 namespace kern {
@@ -101,6 +102,28 @@ int p2p_fanout(const void *src, void *const *dsts, int ndst, uint64_t bytes, int
 // until *flag >= value or budget_ns elapses (then sets kStatusFlagTimeout).
 int wait_flag(const uint64_t *flag, uint64_t value, uint64_t budget_ns, void *stream,
               uint32_t *status);
+
+// Kernel trace (MPCOMM_KERNEL_TRACE=<slots per device>; 0/unset = off). The
+// data movers (gather, scatter, fabric batches, PXN forward) stamp their
+// device start (CTA 0) and end (last CTA to exit) with %globaltimer into a
+// device-memory ring; kernel_trace() reads the rings back (synchronous
+// copies: not for hot paths) and returns the launches still in them.
+struct KernelStamp {
+    uint64_t begin_ns;
+    uint64_t end_ns;
+};
+struct TraceRecord {
+    uint64_t seq;      // launch order across devices
+    int dev;
+    const char *kind;  // "h2d_gather", "h2d_scatter", "copy_batch", "pxn_gather_forward"
+    uint64_t bytes;
+    uint64_t begin_ns, end_ns;
+};
+// Slot for the next launch on the current device (nullptr when off).
+KernelStamp *trace_acquire(const char *kind, uint64_t bytes);
+int kernel_trace(std::vector<TraceRecord> *out);
+void kernel_trace_reset();
+size_t kernel_trace_slots();
 
 // Kernels launched by this library since load (all devices).
 uint64_t launch_count();

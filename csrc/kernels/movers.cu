@@ -21,9 +21,11 @@
 // 32-bit indices and a div/mod per 16 bytes).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "kernels/common.cuh"
 
@@ -86,6 +88,96 @@ uint32_t *default_status_word(int dev) {
     }
     return words[dev];
 }
+
+// ---------------------------------------------------------------------------
+// Kernel trace ring (MPCOMM_KERNEL_TRACE=<slots>, 0 = off): per device, a
+// device-memory ring of start/end stamps that launches write themselves;
+// the host keeps what each slot was used for and reads the ring back only
+// when asked (kernel_trace()).
+// ---------------------------------------------------------------------------
+namespace {
+
+struct TraceMeta {
+    uint64_t seq = 0;
+    const char *kind = nullptr;
+    uint64_t bytes = 0;
+};
+
+struct TraceState {
+    std::mutex mu;
+    size_t slots = 0;
+    uint64_t seq = 0;
+    KernelStamp *ring[64] = {nullptr};
+    std::vector<TraceMeta> meta[64];
+};
+
+TraceState &trace_state() {
+    static TraceState *t = [] {
+        auto *s = new TraceState();
+        const char *e = std::getenv("MPCOMM_KERNEL_TRACE");
+        long long v = e ? std::atoll(e) : 0;
+        s->slots = v > 0 ? static_cast<size_t>(v < 1048576 ? v : 1048576) : 0;
+        return s;
+    }();
+    return *t;
+}
+
+}  // namespace
+
+KernelStamp *trace_acquire(const char *kind, uint64_t bytes) {
+    TraceState &t = trace_state();
+    if (!t.slots) return nullptr;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> g(t.mu);
+    if (!t.ring[dev]) {
+        void *p = nullptr;
+        if (cudaMalloc(&p, t.slots * sizeof(KernelStamp)) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        cudaMemset(p, 0, t.slots * sizeof(KernelStamp));
+        t.ring[dev] = static_cast<KernelStamp *>(p);
+        t.meta[dev].assign(t.slots, TraceMeta{});
+    }
+    const uint64_t seq = ++t.seq;
+    const size_t slot = static_cast<size_t>(seq % t.slots);
+    t.meta[dev][slot] = TraceMeta{seq, kind, bytes};
+    return t.ring[dev] + slot;
+}
+
+int kernel_trace(std::vector<TraceRecord> *out) {
+    out->clear();
+    TraceState &t = trace_state();
+    std::lock_guard<std::mutex> g(t.mu);
+    if (!t.slots) return 0;
+    std::vector<KernelStamp> host(t.slots);
+    for (int dev = 0; dev < 64; ++dev) {
+        if (!t.ring[dev]) continue;
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(dev);
+        cudaError_t e = cudaMemcpy(host.data(), t.ring[dev], t.slots * sizeof(KernelStamp), cudaMemcpyDeviceToHost);
+        cudaSetDevice(prev);
+        if (e != cudaSuccess) return e;
+        for (size_t i = 0; i < t.slots; ++i) {
+            const TraceMeta &m = t.meta[dev][i];
+            if (!m.seq || !host[i].begin_ns || host[i].end_ns < host[i].begin_ns) continue;
+            out->push_back(TraceRecord{m.seq, dev, m.kind, m.bytes, host[i].begin_ns, host[i].end_ns});
+        }
+    }
+    std::sort(out->begin(), out->end(), [](const TraceRecord &a, const TraceRecord &b) { return a.seq < b.seq; });
+    return 0;
+}
+
+void kernel_trace_reset() {
+    TraceState &t = trace_state();
+    std::lock_guard<std::mutex> g(t.mu);
+    for (int dev = 0; dev < 64; ++dev)
+        if (t.ring[dev]) t.meta[dev].assign(t.slots, TraceMeta{});
+}
+
+size_t kernel_trace_slots() { return trace_state().slots; }
 
 // ---------------------------------------------------------------------------
 // Tile sources
@@ -282,13 +374,29 @@ __device__ __forceinline__ void warp_bulk_pipeline(const Src &src, int64_t first
 }
 
 // Kernel epilogue: closes an H2D QoS window and/or publishes a completion
-// flag once the last CTA has drained all of its stores.
+// flag once the last CTA has drained all of its stores; records the
+// launch's device start/end in its trace slot (device memory, optional).
 struct Epilogue {
     H2DWindow *win;
     uint32_t *ctr;      // last-CTA detector (self-resetting), required if win or flag
     uint64_t *flag;     // may point into a peer GPU's memory
     uint64_t flag_value;
+    KernelStamp *stamp = nullptr;
 };
+
+// Trace stamps: CTA 0 writes the start time; every CTA raises the end time
+// to its own exit time (atomicMax), so a reused slot needs no reset.
+__device__ __forceinline__ void trace_begin(KernelStamp *st) {
+    if (st && blockIdx.x == 0 && threadIdx.x == 0)
+        *reinterpret_cast<volatile unsigned long long *>(&st->begin_ns) = globaltimer_ns();
+}
+__device__ __forceinline__ void trace_end(KernelStamp *st) {
+    if (!st) return;
+    __syncthreads();
+    if (threadIdx.x == 0)
+        atomicMax(reinterpret_cast<unsigned long long *>(&st->end_ns),
+                  static_cast<unsigned long long>(globaltimer_ns()));
+}
 
 __device__ __forceinline__ void run_epilogue(const Epilogue &ep) {
     if (!ep.win && !ep.flag) return;
@@ -320,10 +428,12 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(
                          smem_raw + static_cast<size_t>(WARPS) * STAGES * STAGE_BYTES) +
                      warp * STAGES;
+    trace_begin(ep.stamp);
     window_open(ep.win);
     warp_bulk_pipeline<STAGES, STAGE_BYTES>(src, static_cast<int64_t>(blockIdx.x) * WARPS + warp,
                                             static_cast<int64_t>(gridDim.x) * WARPS, stage_mem,
                                             bars, status, budget);
+    trace_end(ep.stamp);
     run_epilogue(ep);
 }
 
@@ -334,6 +444,7 @@ __global__ void __launch_bounds__(kVecWarps * 32)
     const int64_t total = src.count();
     const int64_t nw = static_cast<int64_t>(gridDim.x) * kVecWarps;
     uint64_t paused = 0;
+    trace_begin(ep.stamp);
     window_open(ep.win);
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * kVecWarps + (threadIdx.x >> 5); t < total;
          t += nw) {
@@ -348,6 +459,7 @@ __global__ void __launch_bounds__(kVecWarps * 32)
         }
         warp_copy_any(tl.dst, tl.src, tl.bytes);
     }
+    trace_end(ep.stamp);
     run_epilogue(ep);
 }
 
@@ -433,7 +545,7 @@ int h2d_gather(const void *pool, int64_t pool_blocks, const int64_t *idx, void *
     src.pool_blocks = pool_blocks;
     src.tile_bytes = path == 1 ? kStageBytes : kVecTileBytes;
     src.tpb = (bs + src.tile_bytes - 1) / src.tile_bytes;
-    const Epilogue ep{window, window_ctr, nullptr, 0};
+    const Epilogue ep{window, window_ctr, nullptr, 0, trace_acquire("h2d_gather", static_cast<uint64_t>(n * bs))};
     return path == 1 ? launch_bulk(src, src.n * src.tpb, max_ctas, st, status, ep, info)
                      : launch_vector(src, src.n * src.tpb, max_ctas, st, status, ep, info);
 }
@@ -455,7 +567,7 @@ int h2d_scatter(const void *srcp, const int64_t *idx, void *pool, int64_t pool_b
     src.pool_blocks = pool_blocks;
     src.tile_bytes = path == 1 ? kStageBytes : kVecTileBytes;
     src.tpb = (bs + src.tile_bytes - 1) / src.tile_bytes;
-    const Epilogue ep{window, window_ctr, nullptr, 0};
+    const Epilogue ep{window, window_ctr, nullptr, 0, trace_acquire("h2d_scatter", static_cast<uint64_t>(n * bs))};
     return path == 1 ? launch_bulk(src, src.n * src.tpb, max_ctas, st, status, ep, info)
                      : launch_vector(src, src.n * src.tpb, max_ctas, st, status, ep, info);
 }
@@ -488,7 +600,9 @@ int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_
     }
     src.start[k] = tiles;
     src.n = k;
-    const Epilogue ep{nullptr, done_ctr, done_flag, done_value};
+    uint64_t total = 0;
+    for (int i = 0; i < n; ++i) total += descs[i].bytes;
+    const Epilogue ep{nullptr, done_ctr, done_flag, done_value, trace_acquire("copy_batch", total)};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     return vec ? launch_vector(src, tiles, max_ctas, st, status, ep, info)
                : launch_bulk(src, tiles, max_ctas, st, status, ep, info);
@@ -509,7 +623,8 @@ int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx
     src.pool_blocks = pool_blocks;
     src.tile_bytes = path == 1 ? kStageBytes : kVecTileBytes;
     src.tpb = (bs + src.tile_bytes - 1) / src.tile_bytes;
-    const Epilogue ep{nullptr, ctr, done_flag, flag_value};
+    const Epilogue ep{nullptr, ctr, done_flag, flag_value,
+                      trace_acquire("pxn_gather_forward", static_cast<uint64_t>(n * bs))};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     return path == 1 ? launch_bulk(src, src.n * src.tpb, max_ctas, st, status, ep, info)
                      : launch_vector(src, src.n * src.tpb, max_ctas, st, status, ep, info);

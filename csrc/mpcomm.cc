@@ -118,6 +118,13 @@ int MPComm::tmaScatterOnStream(void *src, const int64_t *idx, uintptr_t dram, in
 }
 int MPComm::setFabricStream(void *stream) { return impl_->setFabricStream(stream); }
 uint64_t MPComm::getKernelLaunchCount() { return kern::launch_count(); }
+std::vector<MPComm::KernelTraceRecord> MPComm::getKernelTrace() {
+    std::vector<kern::TraceRecord> raw;
+    std::vector<KernelTraceRecord> out;
+    if (kern::kernel_trace(&raw) != 0) return out;
+    for (const auto &r : raw) out.push_back(KernelTraceRecord{r.seq, r.dev, r.kind ? r.kind : "", r.bytes, r.begin_ns, r.end_ns});
+    return out;
+}
 std::string MPComm::getFabricName() const { return impl_->fabricName(); }
 
 }  // namespace mpcomm

@@ -41,6 +41,7 @@
 #include <unordered_map>
 
 #include "core/core.h"
+#include "core/nvtx.h"
 #include "cuda/gpu.h"
 #include "kernels/launch.h"
 #include "mpcomm.h"
@@ -728,6 +729,7 @@ int NvlQp::post(const WorkRequest *wrs, size_t n) {
 void NvlQp::flush() {
     std::lock_guard<std::mutex> g(rail_->mu_);
     if (pending_.empty()) return;
+    nvtx::Range range("mpcomm::nvl_doorbell");
     gpu::set_device(rail_->dev_);
     void *stream = rail_->override_stream_ ? rail_->override_stream_ : stream_;
     const int ctas = rail_->ctas_for(pending_host_);

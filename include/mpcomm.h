@@ -275,6 +275,17 @@ class MPComm {
     int setFabricStream(void *stream);
     // Number of this library's GPU kernels launched so far (all objects).
     static uint64_t getKernelLaunchCount();
+    // Extension: device start/end of recent data-mover launches, from the
+    // kernel trace ring (enable with MPCOMM_KERNEL_TRACE=<slots per device>;
+    // empty when off). Reading it synchronises with the devices.
+    struct KernelTraceRecord {
+        uint64_t seq;
+        int device;
+        std::string kind;
+        uint64_t bytes;
+        uint64_t begin_ns, end_ns;  // %globaltimer of the device
+    };
+    static std::vector<KernelTraceRecord> getKernelTrace();
     // Name of the fabric backend in use ("nvl", "lo", "sock", "ib").
     std::string getFabricName() const;
 

@@ -481,6 +481,30 @@ PYBIND11_MODULE(_mpcomm, m) {
           },
           py::arg("flag"), py::arg("value"), py::arg("budget_ns"), py::arg("stream") = 0, py::arg("status") = 0);
     m.def("kernel_launch_count", [] { return kern::launch_count(); });
+    m.def("kernel_trace", [] {
+        std::vector<kern::TraceRecord> raw;
+        int e;
+        {
+            py::gil_scoped_release r;
+            e = kern::kernel_trace(&raw);
+        }
+        if (e != 0) throw std::runtime_error(std::string("kernel_trace: ") + gpu::error_string(e));
+        py::list out;
+        for (const auto &t : raw) {
+            py::dict d;
+            d["seq"] = t.seq;
+            d["device"] = t.dev;
+            d["kind"] = t.kind ? t.kind : "";
+            d["bytes"] = t.bytes;
+            d["begin_ns"] = t.begin_ns;
+            d["end_ns"] = t.end_ns;
+            d["duration_us"] = (t.end_ns - t.begin_ns) / 1000.0;
+            out.append(d);
+        }
+        return out;
+    });
+    m.def("kernel_trace_reset", [] { kern::kernel_trace_reset(); });
+    m.def("kernel_trace_slots", [] { return kern::kernel_trace_slots(); });
     m.def("kernel_wait_budget_ns", [] { return kern::wait_budget_ns(); });
 
     // ---- cross-process GPU memory (mpcomm.parallel) ----

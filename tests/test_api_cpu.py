@@ -296,6 +296,12 @@ def test_handle_recycling(pair):
     assert len(seen) <= 2  # released handles are reused
 
 
+def test_kernel_trace_off_by_default():
+    assert mpcomm._native.kernel_trace_slots() == 0
+    assert mpcomm._native.kernel_trace() == []
+    assert mpcomm.MPComm.get_kernel_launch_count() >= 0
+
+
 @pytest.mark.parametrize("name", ["test_core", "test_engine", "test_engine_san"])
 def test_native_binaries(name):
     """Core unit tests, the multi-threaded engine stress, and the same stress

@@ -311,3 +311,45 @@ def test_tma_gather_api_with_mapping_and_qos_window():
         assert comm.unmap_dram_from_gpu(kv.data_ptr()) == 0
     finally:
         comm.shutdown()
+
+
+def test_kernel_trace_ring_records_launches():
+    """MPCOMM_KERNEL_TRACE=<slots>: gather, scatter and fabric copies stamp
+    their device start/end into the ring; durations agree with CUDA events
+    and the ring wraps without a reset."""
+    import os
+    import subprocess
+    import sys
+    code = r"""
+import torch, mpcomm
+from mpcomm import ops
+n_pages, bs = 512, 65536
+pool = torch.randint(0, 256, (n_pages, bs), dtype=torch.uint8).pin_memory()
+idx = torch.randperm(n_pages)[:256].cuda()
+out = torch.empty(256 * bs, dtype=torch.uint8, device="cuda")
+e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+e0.record(); ops.paged_gather(pool, idx, out); e1.record(); torch.cuda.synchronize()
+ev_us = e0.elapsed_time(e1) * 1e3
+ops.paged_scatter(out, idx, pool)
+src = torch.randint(0, 256, (64 << 20,), dtype=torch.uint8, device="cuda"); dst = torch.empty_like(src)
+ops.copy_spans([src.data_ptr()], [dst.data_ptr()], [src.numel()])
+torch.cuda.synchronize()
+tr = mpcomm._native.kernel_trace()
+kinds = [r["kind"] for r in tr]
+assert kinds[-3:] == ["h2d_gather", "h2d_scatter", "copy_batch"], kinds
+g = tr[-3]
+assert g["bytes"] == 256 * bs and 0 < g["duration_us"] <= ev_us * 1.05 + 5, (g, ev_us)
+assert tr[-1]["bytes"] == 64 << 20 and tr[-1]["duration_us"] > 0
+for _ in range(10):  # wrap the 8-slot ring
+    ops.copy_spans([src.data_ptr()], [dst.data_ptr()], [1 << 20])
+torch.cuda.synchronize()
+tr = mpcomm._native.kernel_trace()
+assert len(tr) == 8 and all(r["kind"] == "copy_batch" and r["bytes"] == 1 << 20 and r["duration_us"] > 0 for r in tr)
+assert [r["seq"] for r in tr] == sorted(r["seq"] for r in tr)
+mpcomm._native.kernel_trace_reset()
+assert mpcomm._native.kernel_trace() == []
+print("trace ok", round(g["duration_us"], 1), round(ev_us, 1))
+"""
+    env = dict(os.environ, MPCOMM_KERNEL_TRACE="8")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
+    assert r.returncode == 0 and "trace ok" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]
