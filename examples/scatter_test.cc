@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -169,11 +170,19 @@ int main(int argc, char **argv) {
     }
 
     std::vector<uintptr_t> remote;
+    // Connect retries while targets come up (MPCOMM_CONNECT_RETRIES,
+    // MPCOMM_CONNECT_RETRY_INTERVAL_MS; the reference tool's variables).
+    auto env_int = [](const char *name, int def) {
+        const char *v = std::getenv(name);
+        return v && *v ? std::atoi(v) : def;
+    };
+    const int retries = std::max(1, env_int("MPCOMM_CONNECT_RETRIES", 30));
+    const int retry_ms = std::max(1, env_int("MPCOMM_CONNECT_RETRY_INTERVAL_MS", 500));
     for (auto &t : targets) {
         int rc = -1;
-        for (int attempt = 0; attempt < 30 && rc != 0; ++attempt) {
+        for (int attempt = 0; attempt < retries && rc != 0; ++attempt) {
             rc = comm.connect(t.id, t.addr, t.port);
-            if (rc) std::this_thread::sleep_for(std::chrono::milliseconds(500));
+            if (rc) std::this_thread::sleep_for(std::chrono::milliseconds(retry_ms));
         }
         mpcomm::RemoteBufferEntry e;
         if (rc || comm.queryRemoteBufferByNuma(t.id, t.addr, t.port, -1, e))

@@ -19,7 +19,6 @@ staging code).
 from __future__ import annotations
 
 import argparse
-import ctypes
 import json
 import mmap
 import os
