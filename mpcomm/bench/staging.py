@@ -54,7 +54,7 @@ def _run(comm, op, local_ptr, remote_ptr, nblocks, bs, batch):
     return time.perf_counter() - t0
 
 
-def measure(nblocks, bs, iters, batch, zero_copy, seed=0):
+def measure(nblocks, bs, iters, batch, zero_copy, seed=0, warmup=1):
     n = nblocks * bs
     a, b = mpcomm.MPComm(), mpcomm.MPComm()
     assert a.init("initiator") == 0 and b.init("pool-host") == 0 and b.start_accept_thread() == 0
@@ -69,8 +69,9 @@ def measure(nblocks, bs, iters, batch, zero_copy, seed=0):
         assert a.connect("pool", "127.0.0.1", port) == 0 and a.query_remote_buffers("pool", "127.0.0.1", port)
         if zero_copy:
             assert a.register_memory(ptr(src), n) == 0 and a.register_memory(ptr(back), n) == 0
-        _run(a, "put", ptr(src), ptr(pool), nblocks, bs, batch)  # warm-up
-        _run(a, "get", ptr(back), ptr(pool), nblocks, bs, batch)
+        for _ in range(warmup):
+            _run(a, "put", ptr(src), ptr(pool), nblocks, bs, batch)
+            _run(a, "get", ptr(back), ptr(pool), nblocks, bs, batch)
         tp = sum(_run(a, "put", ptr(src), ptr(pool), nblocks, bs, batch) for _ in range(iters))
         back[:] = 0
         tg = sum(_run(a, "get", ptr(back), ptr(pool), nblocks, bs, batch) for _ in range(iters))
@@ -110,7 +111,9 @@ def main(argv=None):
     if a.sweep:
         rows = []
         for size in [512 << 10, 1 << 20, 4 << 20, 16 << 20, 64 << 20, 256 << 20, 1 << 30]:
-            r = measure(4, size, max(1, min(a.iters, (1 << 30) // size)), 4, zero_copy=False)
+            # Enough rounds of 4 blocks to move ~1 GiB (at least --iters, at most 256).
+            rounds = max(a.iters, min(256, (1 << 30) // (4 * size)))
+            r = measure(4, size, rounds, 4, zero_copy=False, warmup=3)
             rows.append({"block": size, "put_gbs": r["put_gbs"], "get_gbs": r["get_gbs"], "ok": r["crc32_verified"]})
             print(json.dumps(rows[-1]), flush=True)
         res["sweep_batch4"] = rows
