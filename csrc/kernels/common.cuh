@@ -71,6 +71,20 @@ __device__ __forceinline__ void warp_copy_any(char *d, const char *s, uint64_t b
     for (uint64_t i = lane; i < bytes; i += 32) d[i] = s[i];
 }
 
+// Trace stamps: CTA 0 writes the start time; every CTA raises the end time
+// to its own exit time (atomicMax), so a reused slot needs no reset.
+__device__ __forceinline__ void trace_begin(KernelStamp *st) {
+    if (st && blockIdx.x == 0 && threadIdx.x == 0)
+        *reinterpret_cast<volatile unsigned long long *>(&st->begin_ns) = globaltimer_ns();
+}
+__device__ __forceinline__ void trace_end(KernelStamp *st) {
+    if (!st) return;
+    __syncthreads();
+    if (threadIdx.x == 0)
+        atomicMax(reinterpret_cast<unsigned long long *>(&st->end_ns),
+                  static_cast<unsigned long long>(globaltimer_ns()));
+}
+
 // H2D QoS window helpers (see H2DWindow in launch.h).
 __device__ __forceinline__ void window_open(H2DWindow *win) {
     if (win && blockIdx.x == 0 && threadIdx.x == 0) {

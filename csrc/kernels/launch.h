@@ -95,6 +95,8 @@ int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx
 // (every GPU bound to the multicast object receives the bytes).
 int nvls_broadcast(const void *src, void *mc_dst, uint64_t bytes, int max_ctas, void *stream,
                    LaunchInfo *info);
+// Tuning knob of nvls_broadcast's store flavour and depth (0..3; see bcast.cu).
+void set_nvls_variant(int v);
 // Fallback fan-out: the same bytes stored to up to 8 peer pointers.
 int p2p_fanout(const void *src, void *const *dsts, int ndst, uint64_t bytes, int max_ctas,
                void *stream, LaunchInfo *info);

@@ -384,19 +384,6 @@ struct Epilogue {
     KernelStamp *stamp = nullptr;
 };
 
-// Trace stamps: CTA 0 writes the start time; every CTA raises the end time
-// to its own exit time (atomicMax), so a reused slot needs no reset.
-__device__ __forceinline__ void trace_begin(KernelStamp *st) {
-    if (st && blockIdx.x == 0 && threadIdx.x == 0)
-        *reinterpret_cast<volatile unsigned long long *>(&st->begin_ns) = globaltimer_ns();
-}
-__device__ __forceinline__ void trace_end(KernelStamp *st) {
-    if (!st) return;
-    __syncthreads();
-    if (threadIdx.x == 0)
-        atomicMax(reinterpret_cast<unsigned long long *>(&st->end_ns),
-                  static_cast<unsigned long long>(globaltimer_ns()));
-}
 
 __device__ __forceinline__ void run_epilogue(const Epilogue &ep) {
     if (!ep.win && !ep.flag) return;

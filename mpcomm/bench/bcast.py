@@ -44,7 +44,10 @@ def main(argv=None):
     ap.add_argument("--bg-mb", type=int, default=1024)
     ap.add_argument("--no-qos", action="store_true")
     ap.add_argument("--sweep-ctas", default="", help="comma list: time the broadcast alone per grid size")
+    ap.add_argument("--variants", default="", help="comma list of NVLS store variants (0-3) to time alone")
     a = ap.parse_args(argv)
+    # Device start/end of every broadcast launch (kernel trace ring).
+    os.environ.setdefault("MPCOMM_KERNEL_TRACE", "4096")
     rank, world, local = parallel.init_from_env("nccl")
     dev = torch.device("cuda", local)
     raw, ids, lens = RolloutBatch().make(seed=4)
@@ -146,6 +149,29 @@ def main(argv=None):
                 staged, [peers.ptrs[r] for r in range(1, world)], nbytes, max_ctas=ctas, stream=stream)), 4)
             rows.append(row)
         res["broadcast_only_sweep"] = rows
+
+    def kernel_us(kind):
+        """Median device duration of the `kind` launches since the last reset (rank 0)."""
+        if rank != 0:
+            return None
+        d = sorted(r["duration_us"] for r in mpcomm._native.kernel_trace() if r["kind"] == kind)
+        return round(d[len(d) // 2], 2) if d else None
+
+    if a.variants and world > 1 and grp is not None:
+        rows = []
+        for v in [int(x) for x in a.variants.split(",")]:
+            mpcomm._native._set_nvls_variant(v)
+            if rank == 0:
+                mpcomm._native.kernel_trace_reset()
+            ms = timed(lambda: rank == 0 and ops.nvls_broadcast(staged, grp.mc_ptr, nbytes, stream=stream))
+            ok_v = torch.tensor([1 if rank == 0 or torch.equal(grp.uc[:nbytes].cpu(), raw) else 0], device=dev)
+            dist.all_reduce(ok_v, op=dist.ReduceOp.MIN)
+            ok_v = bool(ok_v.item())
+            k = kernel_us("nvls_broadcast")
+            rows.append({"variant": v, "with_barrier_ms": round(ms, 4), "kernel_us": k,
+                         "kernel_gbs": round(nbytes / (k * 1e-6) / 1e9, 1) if k else None, "ok": ok_v})
+        mpcomm._native._set_nvls_variant(0)
+        res["nvls_variants"] = rows
 
     if rank == 0 and not a.no_qos:
         res["qos"] = qos_experiment(comm, host, dram, idx, staged, pages, stream, a)

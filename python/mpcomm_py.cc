@@ -504,6 +504,7 @@ PYBIND11_MODULE(_mpcomm, m) {
         return out;
     });
     m.def("kernel_trace_reset", [] { kern::kernel_trace_reset(); });
+    m.def("_set_nvls_variant", [](int v) { kern::set_nvls_variant(v); });
     m.def("kernel_trace_slots", [] { return kern::kernel_trace_slots(); });
     m.def("kernel_wait_budget_ns", [] { return kern::wait_budget_ns(); });
 
