@@ -93,6 +93,7 @@ Config Config::from_env() {
     read_u64("MPCOMM_H2D_QOS_RATE_BPS", &c.h2d_qos_rate_bps);
     read_u64("MPCOMM_H2D_QOS_BURST_BYTES", &c.h2d_qos_burst_bytes);
     read_u64("MPCOMM_QOS_DEVICE_PAUSE_US", &c.qos_device_pause_us);
+    read_flag("MPCOMM_QOS_REMOTE", &c.qos_remote);
     read_int("MPCOMM_NIC_PROBE_INTERVAL", 1, 1ll << 40, &c.nic_probe_interval);
     read_double("MPCOMM_NIC_QUARANTINE_SEC", 0.0, 1e6, &c.nic_quarantine_sec);
     read_double("MPCOMM_FAULT_INJECT_AFTER_SEC", 0.0, 1e9, &c.fault_after_sec);

@@ -33,6 +33,9 @@ struct Config {
     // Device-side pause of background GPU-fabric H2D copies while an H2D
     // window is open (rate 0 only): total pause per copy pipeline, us.
     uint64_t qos_device_pause_us = 2000;     // MPCOMM_QOS_DEVICE_PAUSE_US (0 = host gating only)
+    // Send pause/clear frames to every peer with an open QoS control channel
+    // around each QoS-windowed tmaGather/tmaScatter.
+    bool qos_remote = false;                 // MPCOMM_QOS_REMOTE
     size_t nic_probe_interval = 10000;       // MPCOMM_NIC_PROBE_INTERVAL (loops)
     double nic_quarantine_sec = 5.0;         // MPCOMM_NIC_QUARANTINE_SEC
     // ---- fault injection (host side only) ----

@@ -74,6 +74,7 @@ struct QpGroup {
 
 struct Connection {
     std::string host_id;
+    std::string tcp_addr;  // control-plane address (active side; empty when accepted)
     int tcp_port = 0;
     std::vector<RemoteEndpointInfo> nic_endpoints;  // indexed by remote rail
     std::vector<int> remote_nic_numa;
@@ -209,6 +210,19 @@ class MPComm::Impl {
     uint32_t *deviceGateLocked(int gpu);
     void applyDeviceGates();
 
+    // ---- QoS control channel (impl_qos_channel.cc) ----
+    int openQosChannel(const std::string &host_id);
+    int closeQosChannel(const std::string &host_id);
+    int sendQosPolicy(const std::string &host_id, int gpu, uint64_t rate, uint64_t burst, bool clear);
+    struct RemoteQosView {
+        std::string peer;
+        int gpu;
+        uint64_t rate, burst, generation;
+    };
+    std::vector<RemoteQosView> remoteQosPolicies() const;
+    uint64_t remoteQosDefers() const { return remote_qos_defers_.load(std::memory_order_relaxed); }
+    size_t qosChannelCount() const;
+
     // ---- H2D (impl_h2d.cc) ----
     uintptr_t mapDRAMtoGPU(void *host, size_t len);
     int unmapDRAMfromGPU(void *host);
@@ -269,6 +283,43 @@ class MPComm::Impl {
     void pcieOnPosted(int gpu, uint64_t bytes);
     void pcieOnCompleted(int gpu, uint64_t bytes);
     bool qosAllowPost(const Transfer &t, size_t rail, size_t bytes);
+
+    // impl_qos_channel.cc
+    struct QosOutChannel;
+    struct RemoteQosPolicy {
+        std::string peer, peer_ip;
+        int gpu = -1;
+        uint64_t rate = 0, burst = 0, generation = 0;
+        TokenBucket bucket;
+    };
+    struct QosRestoreItem {
+        int gpu;
+        const kern::H2DWindow *win;
+        std::chrono::steady_clock::time_point deadline;
+    };
+    void qosRxLoop(int fd, std::string peer, std::string peer_ip);
+    bool qosAllowRemoteWrite(const Connection &conn, uint64_t raddr, size_t bytes);
+    void broadcastQos(int gpu, uint64_t rate, uint64_t burst, bool clear);
+    void stopQosChannels();
+    void remotePauseForWindow(int gpu, const kern::H2DWindow *win);
+    void qosRestoreLoop();
+
+    mutable std::mutex qos_out_mu_;
+    std::map<std::string, std::shared_ptr<QosOutChannel>> qos_out_;  // channels we opened
+    mutable std::mutex qos_in_mu_;
+    std::vector<std::unique_ptr<RemoteQosPolicy>> qos_in_;  // policies peers sent us
+    std::atomic<int> qos_in_active_{0};
+    std::atomic<uint64_t> remote_qos_defers_{0};
+    std::atomic<uint64_t> qos_generation_{0};
+    std::mutex qos_rx_mu_;
+    std::atomic<bool> qos_rx_running_{true};
+    std::vector<std::thread> qos_rx_threads_;
+    std::vector<int> qos_rx_fds_;
+    std::mutex qos_restore_mu_;
+    std::condition_variable qos_restore_cv_;
+    std::deque<QosRestoreItem> qos_restore_q_;
+    bool qos_restore_running_ = false;
+    std::thread qos_restore_thread_;
 
     Config cfg_;
     bool initialized_ = false;

@@ -52,6 +52,7 @@ int MPComm::Impl::init(const std::string &host_id, const std::string &device_nam
         return MPCOMM_SUCCESS;
     }
     host_id_ = host_id;
+    qos_rx_running_.store(true, std::memory_order_release);
 
     // Backend selection.
     std::string fab = cfg_.fabric;
@@ -144,6 +145,7 @@ int MPComm::Impl::init(const std::string &host_id, const std::string &device_nam
 void MPComm::Impl::shutdown() {
     if (!initialized_ && workers_.empty() && rails_.empty()) return;
     stopAcceptThread();
+    stopQosChannels();
     if (staging_) staging_.reset();
     running_ = false;
     for (auto &w : workers_)

@@ -143,6 +143,7 @@ int MPComm::Impl::connect(const std::string &id, const std::string &addr, int po
     };
     auto conn = std::make_shared<Connection>();
     conn->host_id = id;
+    conn->tcp_addr = addr;
     conn->tcp_port = port;
 
     const uint32_t nn = static_cast<uint32_t>(rails_.size());
@@ -267,17 +268,6 @@ void MPComm::Impl::acceptLoop() {
             MPCOMM_LOG_WARN("MPComm: unknown control message 0x%08x\n", msg);
         }
         ::close(fd);
-    }
-}
-
-void MPComm::Impl::handleQosChannel(int fd) {
-    // The reference build rejects QoS control channels as well
-    // (src/mpcomm.cpp:4524-4531); the H2D QoS here is driven locally by
-    // device-written window flags and needs no peer channel.
-    QosControlHello hello;
-    if (net::recv_pod(fd, &hello)) {
-        hello.host_id[sizeof(hello.host_id) - 1] = 0;
-        MPCOMM_LOG_WARN("MPComm: QoS control channel from %s not supported; closing\n", hello.host_id);
     }
 }
 

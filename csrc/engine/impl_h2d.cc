@@ -73,7 +73,11 @@ int MPComm::Impl::h2dMove(bool gather, uintptr_t dram, const int64_t *idx, void 
     nvtx::Range range(gather ? "mpcomm::tmaGather" : "mpcomm::tmaScatter");
     kern::H2DWindow *win = nullptr;
     uint32_t *ctr = nullptr;
-    if (isH2DQoSEnabled()) acquireH2DWindow(gpu::device_of(gpu_buf), &win, &ctr);
+    const int wgpu = isH2DQoSEnabled() ? gpu::device_of(gpu_buf) : -1;
+    if (wgpu >= 0) acquireH2DWindow(wgpu, &win, &ctr);
+    // Remote writers into this GPU pause (or pace) before the kernel starts.
+    const bool remote = win && cfg_.qos_remote && qosChannelCount() > 0;
+    if (remote) broadcastQos(wgpu, qos_bucket_.rate(), qos_bucket_.burst(), false);
     int e;
     if (gather) {
         e = kern::h2d_gather(reinterpret_cast<const void *>(dram), pool_blocks, idx, gpu_buf, n, bs, mode,
@@ -81,6 +85,12 @@ int MPComm::Impl::h2dMove(bool gather, uintptr_t dram, const int64_t *idx, void 
     } else {
         e = kern::h2d_scatter(gpu_buf, idx, reinterpret_cast<void *>(dram), pool_blocks, n, bs, mode,
                               max_sm, stream, nullptr, win, ctr, nullptr);
+    }
+    if (remote) {
+        if (e == 0)
+            remotePauseForWindow(wgpu, win);  // clear once the window closes
+        else
+            broadcastQos(wgpu, 0, 0, true);
     }
     if (e != 0) {
         if (win) __atomic_store_n(&win->armed, 0u, __ATOMIC_RELEASE);

@@ -341,6 +341,7 @@ void MPComm::Impl::postChunks(Worker *w, Transfer *t, std::vector<fabric::QueueP
             }
         }
         if (q == SIZE_MAX) break;
+        if (t->op == fabric::Opcode::kWrite && !qosAllowRemoteWrite(*conn, c.remote_addr, c.length)) break;
         if (!qosAllowPost(*t, best, c.length)) {
             const int dom = t->local_gpu;
             if (cfg_.pcie_stat_enable && dom >= 0 && dom < static_cast<int>(kMaxGpuDomains))

@@ -80,6 +80,18 @@ void MPComm::enableH2DQoS(uint64_t r, uint64_t b) { impl_->enableH2DQoS(r, b); }
 void MPComm::setH2DQoSPolicy(uint64_t r, uint64_t b) { impl_->setH2DQoSPolicy(r, b); }
 bool MPComm::isH2DQoSEnabled() const { return impl_->isH2DQoSEnabled(); }
 bool MPComm::getLastH2DWindow(int gpu, uint64_t *b, uint64_t *e) const { return impl_->lastH2DWindow(gpu, b, e); }
+int MPComm::openQosChannel(const std::string &h) { return impl_->openQosChannel(h); }
+int MPComm::closeQosChannel(const std::string &h) { return impl_->closeQosChannel(h); }
+int MPComm::sendQosPolicy(const std::string &h, int gpu, uint64_t rate, uint64_t burst) {
+    return impl_->sendQosPolicy(h, gpu, rate, burst, false);
+}
+int MPComm::clearQosPolicy(const std::string &h, int gpu) { return impl_->sendQosPolicy(h, gpu, 0, 0, true); }
+std::vector<MPComm::RemoteQosPolicy> MPComm::getRemoteQosPolicies() const {
+    std::vector<RemoteQosPolicy> out;
+    for (auto &v : impl_->remoteQosPolicies()) out.push_back(RemoteQosPolicy{v.peer, v.gpu, v.rate, v.burst, v.generation});
+    return out;
+}
+uint64_t MPComm::getRemoteQosDeferCount() const { return impl_->remoteQosDefers(); }
 void MPComm::disableH2DQoS() { impl_->disableH2DQoS(); }
 uint64_t MPComm::getNicCompletedBytes() const { return impl_->getNicCompletedBytes(); }
 std::vector<uint64_t> MPComm::getRailCompletedBytes() const { return impl_->railCompletedBytes(); }

@@ -215,6 +215,30 @@ class MPComm {
     // closed H2D window on GPU `gpu`: first CTA start and last CTA end of a
     // tmaGather/tmaScatter launched while QoS was enabled. False if none.
     bool getLastH2DWindow(int gpu, uint64_t *begin_ns, uint64_t *end_ns) const;
+
+    // QoS control channel (extension; the reference's wire format, which it
+    // declares but never opens). openQosChannel(host) connects to a host
+    // this object connect()ed to; policies sent over it make that host
+    // defer (rate 0) or pace its RDMA WRITEs into this host's GPU `gpu`
+    // (-1 = any) until cleared or until the channel closes (fail-open).
+    // With MPCOMM_QOS_REMOTE=1 each QoS-windowed tmaGather/tmaScatter sends
+    // the enableH2DQoS rate to every open channel and clears it when its
+    // H2D window closes.
+    int openQosChannel(const std::string &host_id);
+    int closeQosChannel(const std::string &host_id);
+    int sendQosPolicy(const std::string &host_id, int gpu, uint64_t rate_bytes_per_sec, uint64_t burst_bytes = 0);
+    int clearQosPolicy(const std::string &host_id, int gpu = -1);
+    struct RemoteQosPolicy {
+        std::string peer_host_id;
+        int gpu_device_id;
+        uint64_t rate_bytes_per_sec;
+        uint64_t burst_bytes;
+        uint64_t generation;
+    };
+    // Policies peers have sent to this object, and how many WRITE chunk
+    // posts they deferred so far.
+    std::vector<RemoteQosPolicy> getRemoteQosPolicies() const;
+    uint64_t getRemoteQosDeferCount() const;
     void disableH2DQoS();
     uint64_t getNicCompletedBytes() const;
     // Extension: completed bytes per rail, in getActiveDevices() order (how

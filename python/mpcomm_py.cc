@@ -102,6 +102,26 @@ class PyMPComm {
     void enable_h2d_qos(uint64_t r, uint64_t b) { c_.enableH2DQoS(r, b); }
     void set_h2d_qos_policy(uint64_t r, uint64_t b) { c_.setH2DQoSPolicy(r, b); }
     bool is_h2d_qos_enabled() const { return c_.isH2DQoSEnabled(); }
+    int open_qos_channel(const std::string &h) { return c_.openQosChannel(h); }
+    int close_qos_channel(const std::string &h) { return c_.closeQosChannel(h); }
+    int send_qos_policy(const std::string &h, int gpu, uint64_t rate, uint64_t burst) {
+        return c_.sendQosPolicy(h, gpu, rate, burst);
+    }
+    int clear_qos_policy(const std::string &h, int gpu) { return c_.clearQosPolicy(h, gpu); }
+    py::list get_remote_qos_policies() const {
+        py::list out;
+        for (auto &p : c_.getRemoteQosPolicies()) {
+            py::dict d;
+            d["peer_host_id"] = p.peer_host_id;
+            d["gpu_device_id"] = p.gpu_device_id;
+            d["rate_bytes_per_sec"] = p.rate_bytes_per_sec;
+            d["burst_bytes"] = p.burst_bytes;
+            d["generation"] = p.generation;
+            out.append(d);
+        }
+        return out;
+    }
+    uint64_t get_remote_qos_defer_count() const { return c_.getRemoteQosDeferCount(); }
     py::object get_last_h2d_window(int gpu) const {
         uint64_t b = 0, e = 0;
         if (!c_.getLastH2DWindow(gpu, &b, &e)) return py::none();
@@ -334,6 +354,13 @@ PYBIND11_MODULE(_mpcomm, m) {
         .def("enable_h2d_qos", &C::enable_h2d_qos, py::arg("rate_bytes_per_sec") = 0, py::arg("burst_bytes") = 0)
         .def("set_h2d_qos_policy", &C::set_h2d_qos_policy, py::arg("rate_bytes_per_sec"), py::arg("burst_bytes") = 0)
         .def("is_h2d_qos_enabled", &C::is_h2d_qos_enabled)
+        .def("open_qos_channel", &C::open_qos_channel, py::arg("host_id"))
+        .def("close_qos_channel", &C::close_qos_channel, py::arg("host_id"))
+        .def("send_qos_policy", &C::send_qos_policy, py::arg("host_id"), py::arg("gpu") = -1,
+             py::arg("rate_bytes_per_sec") = 0, py::arg("burst_bytes") = 0)
+        .def("clear_qos_policy", &C::clear_qos_policy, py::arg("host_id"), py::arg("gpu") = -1)
+        .def("get_remote_qos_policies", &C::get_remote_qos_policies)
+        .def("get_remote_qos_defer_count", &C::get_remote_qos_defer_count)
         .def("get_last_h2d_window", &C::get_last_h2d_window, py::arg("gpu") = 0)
         .def("disable_h2d_qos", &C::disable_h2d_qos)
         .def("get_nic_completed_bytes", &C::get_nic_completed_bytes)

@@ -6,6 +6,7 @@ trip, alignment sweep 16..1024 B) plus the B200 additions (64 KiB pages,
 index bound check, bounded waits, CRC-32, fabric copies).
 """
 import random
+import time
 import zlib
 
 import pytest
@@ -353,3 +354,52 @@ print("trace ok", round(g["duration_us"], 1), round(ev_us, 1))
     env = dict(os.environ, MPCOMM_KERNEL_TRACE="8")
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=300)
     assert r.returncode == 0 and "trace ok" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]
+
+
+def test_qos_remote_pause_around_gather_windows(monkeypatch):
+    """MPCOMM_QOS_REMOTE=1: B's QoS-windowed tma_gather on its GPU sends a
+    pause to A over B's control channel before the kernel starts and the
+    clear once the window closes; A's PUTs into B's GPU are deferred
+    meanwhile and complete bit-exact, and no policy is left behind."""
+    monkeypatch.setenv("MPCOMM_QOS_REMOTE", "1")
+    monkeypatch.setenv("MPCOMM_NVL_CHUNK_SIZE", str(1 << 20))
+    a, b = mpcomm.MPComm(), mpcomm.MPComm()
+    assert a.init("A") == 0 and b.init("B") == 0
+    try:
+        assert a.start_accept_thread() == 0 and b.start_accept_thread() == 0
+        n = 256 << 20
+        inbox = torch.zeros(n, dtype=torch.uint8, device="cuda")
+        src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+        assert b.register_memory(inbox.data_ptr(), n) == 0 and b.publish_buffer(inbox.data_ptr(), n) == 0
+        assert a.register_memory(src.data_ptr(), n) == 0
+        assert a.connect("B", "127.0.0.1", b.get_tcp_port()) == 0
+        assert a.query_remote_buffers("B", "127.0.0.1", b.get_tcp_port())
+        assert b.connect("A", "127.0.0.1", a.get_tcp_port()) == 0
+        assert b.open_qos_channel("A") == 0
+        b.enable_h2d_qos(0, 0)
+        pages, bs, m = 4096, 65536, 2048
+        kv = _pool(pages, bs, seed=9)
+        dram = b.map_dram_to_gpu(kv.data_ptr(), kv.numel())
+        idx = torch.randperm(pages)[:m].cuda()
+        out = torch.empty(m * bs, dtype=torch.uint8, device="cuda")
+        stream = torch.cuda.Stream()
+        h = a.put_async(src.data_ptr(), "B", inbox.data_ptr(), n)
+        gathers = 0
+        while not a.is_transfer_complete(h) and gathers < 200:
+            assert b.tma_gather(dram, idx.data_ptr(), out.data_ptr(), m, bs, 0, 0, stream.cuda_stream) == 0
+            stream.synchronize()
+            gathers += 1
+        assert a.wait_transfer(h, 60000) == 0
+        a.release_transfer(h)
+        torch.cuda.synchronize()
+        assert torch.equal(inbox, src)
+        assert torch.equal(out.view(m, bs).cpu(), kv[idx.cpu()])
+        assert a.get_remote_qos_defer_count() > 0, gathers
+        t0 = time.time()
+        while a.get_remote_qos_policies() and time.time() - t0 < 2:
+            time.sleep(0.01)
+        assert a.get_remote_qos_policies() == []
+        b.unmap_dram_from_gpu(kv.data_ptr())
+    finally:
+        b.shutdown()
+        a.shutdown()
