@@ -100,6 +100,23 @@ void set_nvls_variant(int v);
 // Fallback fan-out: the same bytes stored to up to 8 peer pointers.
 int p2p_fanout(const void *src, void *const *dsts, int ndst, uint64_t bytes, int max_ctas,
                void *stream, LaunchInfo *info);
+// Fused H2D gather + broadcast of a batch of host pages to several GPUs in
+// one launch (no staging of the batch in local HBM): tile k of page i,
+// read from pool[idx[i]*bs ..] (mapped host DRAM) into shared memory, is
+// delivered to offset i*bs of every consumer's buffer, either by multimem
+// stores to `mc_dst` (an NVLS multicast address: every bound GPU receives
+// it) or, when mc_dst is null, by bulk stores to each of the `ndst` (<= 8)
+// device pointers in `dsts` (IPC-mapped peer HBM and/or local HBM).
+// Completion (optional; `ctr` is a zeroed device word, self-resetting,
+// launches sharing it must be stream-ordered): with mc_dst, the last CTA
+// adds 1 to the 64-bit flag at multicast address `mc_flag` (release,
+// system scope), so every bound GPU's copy of the flag counts broadcasts;
+// without, it stores `flag_value` to each of the `nflag` flag pointers.
+// Requires 16-byte aligned pool/destinations and bs % 16 == 0.
+int gather_bcast(const void *pool, int64_t pool_blocks, const int64_t *idx, int64_t n, int64_t bs, void *mc_dst,
+                 void *const *dsts, int ndst, uint64_t *mc_flag, uint64_t *const *flags, int nflag,
+                 uint64_t flag_value, uint32_t *ctr, int max_ctas, void *stream, uint32_t *status,
+                 LaunchInfo *info);
 // Bounded wait on a 64-bit flag written by another GPU or the host: waits
 // until *flag >= value or budget_ns elapses (then sets kStatusFlagTimeout).
 int wait_flag(const uint64_t *flag, uint64_t value, uint64_t budget_ns, void *stream,
@@ -117,7 +134,7 @@ struct KernelStamp {
 struct TraceRecord {
     uint64_t seq;      // launch order across devices
     int dev;
-    const char *kind;  // "h2d_gather", "h2d_scatter", "copy_batch", "pxn_gather_forward"
+    const char *kind;  // "h2d_gather", "h2d_scatter", "copy_batch", "pxn_gather_forward", ...
     uint64_t bytes;
     uint64_t begin_ns, end_ns;
 };

@@ -7,6 +7,10 @@ Batch (seed 4): 1,048,576 tokens x top_k=8 int32 expert IDs in [0, 256) plus
   nvls    multimem.st into an NVLS multicast object bound on all GPUs
   fanout  the same bytes stored to each peer's IPC-mapped buffer
   nccl    torch.distributed.broadcast (library baseline)
+  fused_nvls / fused_p2p  ONE kernel (gather_bcast) that reads the pages from
+          host DRAM into shared memory and stores each tile straight to the
+          multicast address (multimem.st) or to every GPU's buffer (bulk
+          stores): no staging in HBM, PCIe read and NVLink fan-out overlap.
 Times: CUDA events on rank 0's stream for gather+broadcast, then a device
 barrier (NCCL all-reduce) so the max over ranks covers delivery.
 
@@ -105,10 +109,25 @@ def main(argv=None):
         if rank == 0:
             ops.p2p_fanout(staged, [peers.ptrs[r] for r in range(1, world)], nbytes, stream=stream)
 
+    def step_fused_nvls():
+        if rank == 0:
+            ops.gather_bcast(dram, pages, idx, PAGE, mc_ptr=grp.mc_ptr, stream=stream)
+
+    def step_fused_p2p():
+        if rank == 0:
+            ops.gather_bcast(dram, pages, idx, PAGE, dst_ptrs=peers.ptrs, stream=stream)
+
     def step_nccl():
         gather()
         with torch.cuda.stream(stream):
             dist.broadcast(staged if rank == 0 else recv, src=0)
+
+    def kernel_us(kind):
+        """Median device duration of the `kind` launches since the last reset (rank 0)."""
+        if rank != 0:
+            return None
+        d = sorted(r["duration_us"] for r in mpcomm._native.kernel_trace() if r["kind"] == kind)
+        return round(d[len(d) // 2], 2) if d else None
 
     res = {"metric": "rollout batch H2D gather + broadcast", "n_gpus": world, "bytes": nbytes,
            "tokens": ids.shape[0], "top_k": ids.shape[1], "sequences": int(lens.numel()),
@@ -116,6 +135,32 @@ def main(argv=None):
     launches0 = mpcomm.MPComm.get_kernel_launch_count()
     g_ms = timed(gather)
     res["gather_ms"] = round(g_ms, 4)
+    # Copy-engine H2D of the same bytes (contiguous pinned -> HBM) on rank 0:
+    # the PCIe side of every path's roofline.
+    if rank == 0:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                staged.copy_(host, non_blocking=True)
+            e0.record(stream)
+            for _ in range(5):
+                staged.copy_(host, non_blocking=True)
+            e1.record(stream)
+        stream.synchronize()
+        ce_ms = e0.elapsed_time(e1) / 5
+    else:
+        ce_ms = 0.0
+    t = torch.tensor([ce_ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ce_ms = t.item()
+    res["ce_h2d_ms"] = round(ce_ms, 4)
+    res["ce_h2d_gbs"] = round(nbytes / (ce_ms * 1e-3) / 1e9, 3)
+    # Roofline of gather + broadcast: the slower of the PCIe read (copy-engine
+    # rate) and the NVLink side (NVLS: the bytes leave rank 0 once; P2P:
+    # world-1 times) at 770 GB/s per direction.
+    nvl_gbs = 770.0
+    res["roofline_ms"] = {"nvls": round(max(ce_ms, nbytes / nvl_gbs / 1e6), 4),
+                          "p2p": round(max(ce_ms, nbytes * max(world - 1, 1) / nvl_gbs / 1e6), 4)}
     if grp is not None and world > 1:
         res["nvls_ms"] = round(timed(step_nvls), 4)
         ok = torch.equal(grp.uc[:nbytes].cpu(), raw)
@@ -127,11 +172,29 @@ def main(argv=None):
         if rank != 0:
             ok = ok and torch.equal(peers.local.cpu(), raw)
         res["nccl_ms"] = round(timed(step_nccl), 4)
+        if grp is not None:
+            grp.uc.zero_()
+            torch.cuda.synchronize()
+            if rank == 0:
+                mpcomm._native.kernel_trace_reset()
+            res["fused_nvls_ms"] = round(timed(step_fused_nvls), 4)
+            ok = ok and torch.equal(grp.uc[:nbytes].cpu(), raw)
+            res["fused_nvls_kernel_us"] = kernel_us("gather_bcast_nvls")
+        peers.local.zero_()
+        torch.cuda.synchronize()
+        if rank == 0:
+            mpcomm._native.kernel_trace_reset()
+        res["fused_p2p_ms"] = round(timed(step_fused_p2p), 4)
+        ok = ok and torch.equal(peers.local.cpu(), raw)
+        res["fused_p2p_kernel_us"] = kernel_us("gather_bcast_p2p")
+        for k, roof in (("fused_nvls", "nvls"), ("fused_p2p", "p2p"), ("nvls", "nvls"), ("fanout", "p2p")):
+            if f"{k}_ms" in res:
+                res[f"{k}_roofline_frac"] = round(res["roofline_ms"][roof] / res[f"{k}_ms"], 4)
     okt = torch.tensor([1 if ok else 0], device=dev)
     dist.all_reduce(okt, op=dist.ReduceOp.MIN)
     res["bitexact"] = bool(okt.item())
     res["gpu_launches"] = int(mpcomm.MPComm.get_kernel_launch_count() - launches0)
-    for k in ("nvls", "fanout", "nccl"):
+    for k in ("nvls", "fanout", "nccl", "fused_nvls", "fused_p2p"):
         if f"{k}_ms" in res:
             res[f"{k}_delivered_gbs"] = round(nbytes * (world - 1) / (res[f"{k}_ms"] * 1e-3) / 1e9, 3)
     # NVLink roofline of the broadcast (after the gather): NVLS sends the
@@ -149,13 +212,6 @@ def main(argv=None):
                 staged, [peers.ptrs[r] for r in range(1, world)], nbytes, max_ctas=ctas, stream=stream)), 4)
             rows.append(row)
         res["broadcast_only_sweep"] = rows
-
-    def kernel_us(kind):
-        """Median device duration of the `kind` launches since the last reset (rank 0)."""
-        if rank != 0:
-            return None
-        d = sorted(r["duration_us"] for r in mpcomm._native.kernel_trace() if r["kind"] == kind)
-        return round(d[len(d) // 2], 2) if d else None
 
     if a.variants and world > 1 and grp is not None:
         rows = []

@@ -10,6 +10,8 @@ a host without the native module or a GPU these functions raise.
   crc32_blocks(tensor, num_blocks)        zlib CRC-32 of each block
   copy_spans(srcs, dsts, lengths)         raw device copy of up to 64 spans
   pxn_gather_forward(...)                 fused gather + forward (peer dst)
+  gather_bcast(...)                       fused host-page gather + broadcast
+                                          (NVLS multimem or P2P bulk stores)
   nvls_broadcast(src, mc_ptr)             multimem.st broadcast
   p2p_fanout(src, dst_ptrs)               store the same bytes to peers
 
@@ -28,7 +30,7 @@ MODE_AUTO, MODE_SM, MODE_TMA = 0, 1, 2
 
 __all__ = [
     "MODE_AUTO", "MODE_SM", "MODE_TMA", "paged_gather", "paged_scatter", "crc32_blocks",
-    "copy_spans", "pxn_gather_forward", "nvls_broadcast", "p2p_fanout", "wait_flag",
+    "copy_spans", "pxn_gather_forward", "gather_bcast", "nvls_broadcast", "p2p_fanout", "wait_flag",
     "crc32_host",
 ]
 
@@ -120,6 +122,30 @@ def pxn_gather_forward(pool_ptr: int, pool_blocks: int, indices: torch.Tensor, d
     _check(_native.pxn_gather_forward(pool_ptr, pool_blocks, indices.data_ptr(), dst_ptr,
                                       indices.numel(), block_size, max_ctas, _stream_ptr(stream),
                                       done_flag, flag_value, counter), "pxn_gather_forward")
+
+
+def gather_bcast(pool_ptr: int, pool_blocks: int, indices: torch.Tensor, block_size: int, mc_ptr: int = 0,
+                 dst_ptrs: Sequence[int] = (), mc_flag: int = 0, flags: Sequence[int] = (), flag_value: int = 1,
+                 counter: int = 0, max_ctas: int = 0, stream: Optional[torch.cuda.Stream] = None,
+                 status_ptr: int = 0) -> None:
+    """One launch that gathers ``indices`` pages of ``block_size`` bytes from
+    a host pool (device-visible pointer) and delivers page i to byte offset
+    ``i * block_size`` of every consumer GPU, without staging the batch in
+    local HBM: ``multimem.st`` to ``mc_ptr`` (NVLS multicast address; every
+    bound GPU receives it) or, with ``mc_ptr == 0``, bulk stores to each of
+    ``dst_ptrs`` (<= 8 local or IPC-mapped peer buffers).
+
+    Completion: with ``mc_ptr`` and ``mc_flag`` (multicast address of a
+    64-bit word), every bound GPU's copy of that word is incremented once the
+    whole batch has been stored; without multicast, ``flag_value`` is stored
+    to each address in ``flags``. ``counter`` is a zeroed int32 device word
+    (required with a flag). Consumers wait with :func:`wait_flag`.
+    """
+    if indices.dtype != torch.int64 or not indices.is_cuda:
+        raise ValueError("indices must be an int64 CUDA tensor")
+    _check(_native.gather_bcast(pool_ptr, pool_blocks, indices.data_ptr(), indices.numel(), block_size, mc_ptr,
+                                list(dst_ptrs), mc_flag, list(flags), flag_value, counter, max_ctas,
+                                _stream_ptr(stream), status_ptr), "gather_bcast")
 
 
 def nvls_broadcast(src: torch.Tensor, mc_ptr: int, nbytes: Optional[int] = None, max_ctas: int = 0,

@@ -484,6 +484,26 @@ PYBIND11_MODULE(_mpcomm, m) {
           py::arg("pool"), py::arg("pool_blocks"), py::arg("indices"), py::arg("dst"), py::arg("num_blocks"),
           py::arg("block_size"), py::arg("max_ctas") = 0, py::arg("stream") = 0, py::arg("done_flag") = 0,
           py::arg("flag_value") = 1, py::arg("counter") = 0);
+    m.def("gather_bcast",
+          [](uintptr_t pool, int64_t pool_blocks, uintptr_t idx, int64_t n, int64_t bs, uintptr_t mc,
+             const std::vector<uintptr_t> &dsts, uintptr_t mc_flag, const std::vector<uintptr_t> &flags,
+             uint64_t flag_value, uintptr_t ctr, int max_ctas, uintptr_t stream, uintptr_t status) {
+              std::vector<void *> d;
+              for (auto p : dsts) d.push_back(reinterpret_cast<void *>(p));
+              std::vector<uint64_t *> f;
+              for (auto p : flags) f.push_back(reinterpret_cast<uint64_t *>(p));
+              py::gil_scoped_release r;
+              return kern::gather_bcast(reinterpret_cast<const void *>(pool), pool_blocks,
+                                        reinterpret_cast<const int64_t *>(idx), n, bs, reinterpret_cast<void *>(mc),
+                                        d.data(), static_cast<int>(d.size()), reinterpret_cast<uint64_t *>(mc_flag),
+                                        f.data(), static_cast<int>(f.size()), flag_value,
+                                        reinterpret_cast<uint32_t *>(ctr), max_ctas, reinterpret_cast<void *>(stream),
+                                        reinterpret_cast<uint32_t *>(status), nullptr);
+          },
+          py::arg("pool"), py::arg("pool_blocks"), py::arg("indices"), py::arg("num_blocks"), py::arg("block_size"),
+          py::arg("mc_dst") = 0, py::arg("dsts") = std::vector<uintptr_t>{}, py::arg("mc_flag") = 0,
+          py::arg("flags") = std::vector<uintptr_t>{}, py::arg("flag_value") = 1, py::arg("counter") = 0,
+          py::arg("max_ctas") = 0, py::arg("stream") = 0, py::arg("status") = 0);
     m.def("nvls_broadcast",
           [](uintptr_t src, uintptr_t mc, uint64_t bytes, int max_ctas, uintptr_t stream) {
               py::gil_scoped_release r;

@@ -9,6 +9,9 @@ non-zero on any mismatch.
           lands in rank r's memory.
   nvls    NVLS multicast broadcast from rank 0 (falls back to P2P fan-out
           where multicast is unavailable) of a rollout-style batch.
+  gather_bcast  fused host-page gather + broadcast from rank 0 in one kernel
+          (NVLS multimem stores where supported, then P2P bulk stores),
+          completed by a device flag every rank waits on with a bounded wait.
   peer_exit  (2 ranks) rank 1 leaves between steps; rank 0's next PUT to it
           fails on the host, fast, and its engine keeps working.
 """
@@ -136,6 +139,60 @@ def case_nvls(rank, world):
         print(f"nvls case used: {used}", flush=True)
 
 
+def case_gather_bcast(rank, world):
+    bs, pages, n = 65536 + 1024, 384, 96
+    pool_cpu = torch.randint(0, 256, (pages, bs), dtype=torch.uint8, generator=torch.Generator().manual_seed(11))
+    idx_cpu = torch.randperm(pages, generator=torch.Generator().manual_seed(12))[:n]
+    expect = pool_cpu[idx_cpu].reshape(-1)
+    nbytes = n * bs
+    fo = nbytes  # flag word right after the batch (nbytes % 256 == 0)
+    pool = pool_cpu.pin_memory() if rank == 0 else None
+    idx = idx_cpu.cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+    budget = 10_000_000_000
+    used = []
+    try:
+        grp = parallel.NvlsGroup(nbytes + 256)
+    except RuntimeError as e:
+        grp = None
+        used.append(f"nvls unavailable ({e})")
+    if grp is not None:
+        grp.uc.zero_()
+        for rep in (1, 2):
+            grp.uc[:nbytes].zero_()
+            torch.cuda.synchronize()
+            dist.barrier()
+            if rank == 0:
+                ops.gather_bcast(pool.data_ptr(), pages, idx, bs, mc_ptr=grp.mc_ptr, mc_flag=grp.mc_ptr + fo,
+                                 counter=ctr.data_ptr(), status_ptr=status.data_ptr())
+            ops.wait_flag(grp.uc_ptr + fo, rep, budget, status_ptr=status.data_ptr())
+            torch.cuda.synchronize()
+            assert status.item() == 0, f"rank {rank} status {status.item()}"
+            assert torch.equal(grp.uc[:nbytes].cpu(), expect), "fused NVLS broadcast mismatch"
+            dist.barrier()
+        used.append("nvls")
+        grp.close()
+    bufs = parallel.PeerBuffers(nbytes + 256)
+    for rep in (1, 2):
+        bufs.local.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 0:
+            ops.gather_bcast(pool.data_ptr(), pages, idx, bs, dst_ptrs=bufs.ptrs,
+                             flags=[p + fo for p in bufs.ptrs], flag_value=100 + rep, counter=ctr.data_ptr(),
+                             status_ptr=status.data_ptr())
+        ops.wait_flag(bufs.local.data_ptr() + fo, 100 + rep, budget, status_ptr=status.data_ptr())
+        torch.cuda.synchronize()
+        assert status.item() == 0, f"rank {rank} status {status.item()}"
+        assert torch.equal(bufs.local[:nbytes].cpu(), expect), "fused P2P fan-out mismatch"
+        dist.barrier()
+    used.append("p2p")
+    bufs.close()
+    if rank == 0:
+        print(f"gather_bcast case used: {used}", flush=True)
+
+
 def case_peer_exit(rank, world):
     """Rank 1 leaves between steps (its MPComm shut down, nothing in flight)
     and tells rank 0 through the store. Rank 0's next PUT to it must fail
@@ -196,7 +253,7 @@ def case_peer_exit(rank, world):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["putget", "pxn", "nvls", "peer_exit", "all"])
+    p.add_argument("case", choices=["putget", "pxn", "nvls", "gather_bcast", "peer_exit", "all"])
     a = p.parse_args()
     rank, world, _ = parallel.init_from_env("gloo")
     if a.case == "peer_exit":
@@ -206,7 +263,7 @@ def main():
         if rank == 0:
             print("case peer_exit ok", flush=True)
         os._exit(0)
-    cases = ["putget", "pxn", "nvls"] if a.case == "all" else [a.case]
+    cases = ["putget", "pxn", "nvls", "gather_bcast"] if a.case == "all" else [a.case]
     for c in cases:
         globals()[f"case_{c}"](rank, world)
         if rank == 0:

@@ -179,6 +179,49 @@ def test_pxn_forward_local_flag():
     assert torch.equal(dst.cpu(), pool[idx.cpu()])
 
 
+def test_gather_bcast_p2p_local_destinations_and_flags():
+    """Fused gather + fan-out (P2P sink) to two local buffers: both receive
+    the gathered pages bit-exact, both flags are published, the counter
+    resets, a repeat launch works, and an out-of-range index is skipped and
+    flagged."""
+    pages, bs, n = 48, 65536 + 4096, 20
+    pool = _pool(pages, bs, seed=21)
+    idx = torch.randperm(pages, generator=torch.Generator().manual_seed(3))[:n].cuda()
+    a = torch.zeros((n, bs), dtype=torch.uint8, device="cuda")
+    b = torch.zeros((n, bs), dtype=torch.uint8, device="cuda")
+    flags = torch.zeros(2, dtype=torch.int64, device="cuda")
+    ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    expect = pool[idx.cpu()]
+    for rep in (1, 2):
+        ops.gather_bcast(pool.data_ptr(), pages, idx, bs, dst_ptrs=[a.data_ptr(), b.data_ptr()],
+                         flags=[flags.data_ptr(), flags.data_ptr() + 8], flag_value=10 + rep,
+                         counter=ctr.data_ptr(), status_ptr=status.data_ptr())
+        torch.cuda.synchronize()
+        assert flags.tolist() == [10 + rep, 10 + rep] and ctr.item() == 0 and status.item() == 0
+        assert torch.equal(a.cpu(), expect) and torch.equal(b.cpu(), expect)
+    bad = idx.clone()
+    bad[3] = pages + 5
+    a.fill_(9)
+    ops.gather_bcast(pool.data_ptr(), pages, bad, bs, dst_ptrs=[a.data_ptr()], status_ptr=status.data_ptr())
+    torch.cuda.synchronize()
+    assert status.item() & 4  # kStatusBadIndex
+    got = a.cpu()
+    assert (got[3] == 9).all()
+    keep = [i for i in range(n) if i != 3]
+    assert torch.equal(got[keep], expect[keep])
+
+
+def test_gather_bcast_rejects_misaligned():
+    pool = _pool(8, 4096)
+    idx = torch.arange(4, device="cuda")
+    out = torch.zeros(4 * 4096 + 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(RuntimeError):
+        ops.gather_bcast(pool.data_ptr(), 8, idx, 4096, dst_ptrs=[out.data_ptr() + 8])
+    with pytest.raises(RuntimeError):
+        ops.gather_bcast(pool.data_ptr(), 8, idx, 4088, dst_ptrs=[out.data_ptr()])
+
+
 def _fabric_pair():
     comm = mpcomm.MPComm()
     assert comm.init("gpu-test") == 0
