@@ -227,6 +227,19 @@ def main(argv=None):
             rows.append({"variant": v, "with_barrier_ms": round(ms, 4), "kernel_us": k,
                          "kernel_gbs": round(nbytes / (k * 1e-6) / 1e9, 1) if k else None, "ok": ok_v})
         mpcomm._native._set_nvls_variant(0)
+        # The same broadcast from HBM through gather_bcast: bulk (TMA) loads of
+        # 16 KiB tiles into shared memory, multimem.st from there.
+        if rank == 0:
+            mpcomm._native.kernel_trace_reset()
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        ms = timed(lambda: rank == 0 and ops.gather_bcast(staged.data_ptr(), pages, idx, PAGE, mc_ptr=grp.mc_ptr,
+                                                          stream=stream))
+        ok_v = torch.tensor([1 if rank == 0 or torch.equal(grp.uc[:nbytes].cpu(), raw) else 0], device=dev)
+        dist.all_reduce(ok_v, op=dist.ReduceOp.MIN)
+        k = kernel_us("gather_bcast_nvls")
+        rows.append({"variant": "tma_smem", "with_barrier_ms": round(ms, 4), "kernel_us": k,
+                     "kernel_gbs": round(nbytes / (k * 1e-6) / 1e9, 1) if k else None, "ok": bool(ok_v.item())})
         res["nvls_variants"] = rows
 
     if rank == 0 and not a.no_qos:

@@ -11,6 +11,8 @@ Cases (inputs larger than the 126 MB L2 where DRAM/PCIe traffic matters):
   crc32 / crc32_noalloc    4 x 40 MiB blocks
   pxn_local                fused gather + forward (destination on this GPU)
   fanout_local             P2P fan-out store path to 2 local buffers
+  gather_bcast_p2p         fused host gather + delivery (bulk stores) to 2
+                           local buffers, 512 x 64 KiB pages
   nvls                     multimem broadcast through a 1-GPU multicast object
   wait_flag                bounded flag wait on a flag that is already set
 With --time each case is also timed with CUDA events (after 2 warm-ups) and
@@ -30,7 +32,7 @@ from mpcomm import ops
 
 PAGE = 65536
 ALL = ["gather_tma", "gather_sm", "scatter_tma", "copy_d2d", "copy_h2d", "crc32", "crc32_noalloc",
-       "pxn_local", "fanout_local", "nvls", "wait_flag"]
+       "pxn_local", "fanout_local", "gather_bcast_p2p", "nvls", "wait_flag"]
 
 
 def build_cases():
@@ -65,6 +67,9 @@ def build_cases():
                                                      done_flag=flag.data_ptr(), flag_value=1,
                                                      counter=ctr.data_ptr()), nb),
         "fanout_local": (lambda: ops.p2p_fanout(big[:q], [big2.data_ptr(), big2.data_ptr() + q], q), 2 * q),
+        "gather_bcast_p2p": (lambda: ops.gather_bcast(pool.data_ptr(), 2048, idx[:512], PAGE,
+                                                      dst_ptrs=[out.data_ptr(), out.data_ptr() + 512 * PAGE]),
+                             512 * PAGE),
         "wait_flag": (lambda: ops.wait_flag(flag.data_ptr(), 1, 1_000_000, status.data_ptr()), 8),
     }
     keep = (pool, idx, out, big, big2, host, crc_out, flag, status, ctr)
