@@ -49,6 +49,9 @@ def main(argv=None):
     ap.add_argument("--no-qos", action="store_true")
     ap.add_argument("--sweep-ctas", default="", help="comma list: time the broadcast alone per grid size")
     ap.add_argument("--variants", default="", help="comma list of NVLS store variants (0-3) to time alone")
+    ap.add_argument("--pull", action="store_true",
+                    help="also time the all-source broadcast: every rank reads its 1/world slice of rank 0's "
+                         "buffer over NVLink and multicasts it")
     a = ap.parse_args(argv)
     # Device start/end of every broadcast launch (kernel trace ring).
     os.environ.setdefault("MPCOMM_KERNEL_TRACE", "4096")
@@ -242,6 +245,32 @@ def main(argv=None):
                      "kernel_gbs": round(nbytes / (k * 1e-6) / 1e9, 1) if k else None, "ok": bool(ok_v.item())})
         res["nvls_variants"] = rows
 
+    if a.pull and world > 1 and grp is not None:
+        # All-source broadcast of a batch already in rank 0's HBM: rank r
+        # pulls slice r from rank 0 (plain loads over NVLink) and multimem-
+        # stores it, so 8 GPUs share the multicast work instead of one.
+        src = parallel.PeerBuffers(nbytes)
+        if rank == 0:
+            src.local.copy_(staged)
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        mpcomm._native.kernel_trace_reset()
+
+        def step_pull():
+            grp.broadcast_from(src.ptrs[0], nbytes, stream=stream)
+
+        ms = timed(step_pull)
+        ok_v = torch.tensor([1 if torch.equal(grp.uc[:nbytes].cpu(), raw) else 0], device=dev)
+        dist.all_reduce(ok_v, op=dist.ReduceOp.MIN)
+        d = sorted(r["duration_us"] for r in mpcomm._native.kernel_trace() if r["kind"] == "nvls_broadcast")
+        k = torch.tensor([d[len(d) // 2] if d else 0.0], dtype=torch.float64, device=dev)
+        dist.all_reduce(k, op=dist.ReduceOp.MAX)
+        res["nvls_pull"] = {"with_barrier_ms": round(ms, 4), "kernel_us_max_rank": round(k.item(), 2),
+                            "kernel_gbs": round(nbytes / (k.item() * 1e-6) / 1e9, 1) if k.item() else None,
+                            "ok": bool(ok_v.item())}
+        dist.barrier()
+        src.close()
     if rank == 0 and not a.no_qos:
         res["qos"] = qos_experiment(comm, host, dram, idx, staged, pages, stream, a)
     dist.barrier()

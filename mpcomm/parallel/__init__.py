@@ -13,7 +13,9 @@ barriers); the bytes move through this package's own kernels:
                         node), pinned and mapped into every rank's GPU.
 * ``NvlsGroup``       — an NVLS multicast buffer: one allocation per GPU
                         bound to a multicast object; ``multimem.st`` to the
-                        multicast address lands on every GPU.
+                        multicast address lands on every GPU
+                        (``broadcast_from``: all-source broadcast of a
+                        buffer in the root's HBM).
 """
 from __future__ import annotations
 
@@ -223,6 +225,32 @@ class NvlsGroup:
             raise RuntimeError(f"multicast map failed ({err})")
         self.uc = device_view(self.uc_ptr, self.size)
         dist.barrier()
+
+    def broadcast_from(self, root_ptr: int, nbytes: int, max_ctas: int = 0,
+                       stream: Optional[torch.cuda.Stream] = None) -> None:
+        """All-source broadcast of ``nbytes`` that sit in the root's HBM at
+        ``root_ptr`` (an address this rank can load from: the root's own
+        pointer on the root, its CUDA-IPC mapping elsewhere, e.g.
+        ``PeerBuffers.ptrs[root]``) into every rank's ``uc``.
+
+        Every rank calls it: rank r loads slice r (1/world of the bytes, 4 KiB
+        aligned) from the root over NVLink and ``multimem.st``-s it to the
+        multicast address, so all GPUs share the multicast work instead of the
+        root issuing it alone (8 B200s: 104 us instead of 134 us for 57.9 MB).
+        Completion is stream-ordered per rank; the data is complete on every
+        rank once every rank's launch has finished (a barrier, or a flag).
+        """
+        if nbytes > self.size or nbytes % 16:
+            raise ValueError("nbytes must be a multiple of 16 within the group's size")
+        sl = (nbytes // self.world + 4095) // 4096 * 4096
+        off = min(self.rank * sl, nbytes)
+        ln = max(0, min(sl, nbytes - off))
+        if ln == 0:
+            return
+        s = stream if stream is not None else torch.cuda.current_stream()
+        err = _native.nvls_broadcast(root_ptr + off, self.mc_ptr + off, ln, max_ctas, int(s.cuda_stream))
+        if err:
+            raise RuntimeError(f"nvls_broadcast failed with CUDA error {err}")
 
     def close(self):
         torch.cuda.synchronize()

@@ -124,6 +124,19 @@ def case_nvls(rank, world):
         dist.barrier()
         assert torch.equal(grp.uc[:nbytes], src), "NVLS broadcast mismatch"
         dist.barrier()
+        # All-source broadcast: every rank pulls its slice from rank 0's HBM.
+        root = parallel.PeerBuffers(nbytes)
+        if rank == 0:
+            root.local.copy_(torch.flip(src, [0]))
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        grp.broadcast_from(root.ptrs[0], nbytes)
+        torch.cuda.synchronize()
+        dist.barrier()
+        assert torch.equal(grp.uc[:nbytes], torch.flip(src, [0])), "all-source NVLS broadcast mismatch"
+        dist.barrier()
+        root.close()
         grp.close()
     bufs = parallel.PeerBuffers(nbytes)
     dist.barrier()
