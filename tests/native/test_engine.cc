@@ -30,7 +30,9 @@ int main() {
     setenv("MPCOMM_MAX_RDMA_TRANSFER_SIZE", "65536", 1);
     setenv("MPCOMM_STAGING_SLAB_BYTES", "131072", 1);
     const size_t per = 1 << 20;
-    const int threads = 4, rounds = 12;
+    const int threads = 4;
+    const char *rs = std::getenv("MPCOMM_STRESS_ROUNDS");  // more interleavings under TSAN
+    const int rounds = rs && std::atoi(rs) > 0 ? std::atoi(rs) : 12;
     mpcomm::MPComm a, b;
     CHECK(a.init("A") == 0 && b.init("B") == 0 && b.startAcceptThread() == 0);
     std::vector<unsigned char> target(per * threads, 0);

@@ -302,14 +302,21 @@ def test_kernel_trace_off_by_default():
     assert mpcomm.MPComm.get_kernel_launch_count() >= 0
 
 
-@pytest.mark.parametrize("name", ["test_core", "test_engine", "test_engine_san"])
+@pytest.mark.parametrize("name", ["test_core", "test_engine", "test_engine_san", "test_engine_tsan"])
 def test_native_binaries(name):
     """Core unit tests, the multi-threaded engine stress, and the same stress
-    built with AddressSanitizer (memory errors in the engine's lifetime and
-    completion protocol abort with a report)."""
+    built with AddressSanitizer + UBSan (memory errors in the engine's
+    lifetime and completion protocol abort with a report) and with
+    ThreadSanitizer (any data race between the submitting threads, the
+    worker, the publish/query thread and the throttle toggler fails it)."""
     exe = os.path.join(ROOT, "tests", "native", "bin", name)
+    if name == "test_engine_tsan" and not os.path.exists(exe):
+        pytest.skip("toolchain has no ThreadSanitizer runtime")
     assert os.path.exists(exe), "native tests not built (run __graft_entry__.build())"
-    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=0:abort_on_error=1", MPCOMM_LOG_LEVEL="1")
-    r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
+    env = dict(os.environ, ASAN_OPTIONS="detect_leaks=0:abort_on_error=1", MPCOMM_LOG_LEVEL="1",
+               TSAN_OPTIONS="halt_on_error=1:exitcode=66:second_deadlock_stack=1",
+               MPCOMM_STRESS_ROUNDS="40" if name == "test_engine_tsan" else "12")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=600, env=env)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert "ERROR: AddressSanitizer" not in r.stderr
+    assert "WARNING: ThreadSanitizer" not in r.stderr
