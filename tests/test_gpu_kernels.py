@@ -97,9 +97,11 @@ def test_out_of_range_index_is_skipped():
     assert (o[1] == 7).all() and (o[3] == 7).all()  # bad indices never touch memory
 
 
-@pytest.mark.parametrize("bs", [1, 15, 4096, (512 << 10) + 3, 3 << 20])
-def test_crc32_matches_zlib(bs):
-    n = 5
+@pytest.mark.parametrize("n,bs", [(5, 1), (5, 15), (5, 4096), (5, (512 << 10) + 3), (5, 3 << 20),
+                                  (3, (5 << 20) + 16 * 37), (2, 96 << 20), (700, 4096 + 512 + 48)])
+def test_crc32_matches_zlib(n, bs):
+    """Spans of rows, the two-chain split, row tails, unaligned blocks (odd
+    block sizes) and multi-span blocks against zlib."""
     data = torch.randint(0, 256, (n * bs,), dtype=torch.uint8, generator=torch.Generator().manual_seed(bs))
     got = ops.crc32_blocks(data.cuda(), n).cpu().tolist()
     raw = data.numpy().tobytes()
