@@ -10,22 +10,28 @@
 //
 // Kernel layout (crc_rows_kernel). Each block is cut into spans of S bytes
 // (S chosen so the whole input gives about one span per resident warp);
-// a warp owns a span and reads it as 512-byte rows, lane l loading bytes
-// [16l, 16l+16) of every row — fully coalesced 16-byte loads. Lane l thus
-// sees a "column" of its span, 16 bytes every 512. Its register X follows
-//     X <- shift(X, 512) ^ R(row piece)
-// computed as one table shift by 496 bytes (four lookups in the U tables)
-// followed by the ordinary slicing-by-4 steps over the 16 bytes (which
-// shift by the remaining 16). At the end lane l's column contributes
-// shift(X_l, 496 - 16l) to the span and the lanes are xor-reduced. The
+// a warp owns a span and reads it as 1 KiB rows, lane l loading bytes
+// [32l, 32l+32) of every row with one 256-bit load — fully coalesced. Lane
+// l thus sees a "column" of its span, 32 bytes every 1,024. Its register X
+// follows
+//     X <- shift(X, 1024) ^ R(row piece)
+// computed as one table shift by 992 bytes (four lookups in the U tables)
+// followed by the ordinary slicing-by-4 steps over the 32 bytes (which
+// shift by the remaining 32). At the end lane l's column contributes
+// shift(X_l, 992 - 32l) to the span and the lanes are xor-reduced. The
 // span's rows are split in two halves so each lane runs two independent
 // chains. Lookup tables (4 slicing tables + 4 shift tables, 8 KiB) are
-// replicated 16 times, bank-interleaved, and lane l reads copy l % 16, so
-// only lanes l and l + 16 can collide on a bank. A finalize kernel folds
-// the spans of each block with one CTA per block: each thread folds a
-// contiguous run of spans (one multiply by x^(8S) per span), then a tree
-// combines the runs. Multiplication by x^(8L) uses a 41-entry table of
-// powers x^(8*2^k), so a shift costs popcount(L) carry-less multiplies.
+// replicated 16 times, bank-interleaved, and lane l reads copy l % 16 at
+// 32-bit shared addresses, so only lanes l and l + 16 can collide on a bank.
+//
+// crc_finalize_kernel (one CTA per block, launched with programmatic
+// dependent launch so its launch overlaps the row kernel) folds the block's
+// full spans: thread t folds a power-of-two run of spans (one multiply by
+// x^(8S) each), runs are combined by a shuffle tree and across warps with
+// multipliers x^(8S*2^j) from the host, then the partial last span, the
+// initial register and the final xor are applied with host constants.
+// Multiplication by x^(8L) in general uses a 41-entry table of powers
+// x^(8*2^k), so a shift costs popcount(L) carry-less multiplies.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -40,17 +46,31 @@ namespace {
 constexpr uint32_t kPoly = 0xEDB88320u;
 constexpr uint32_t kOne = 0x80000000u;  // x^0 in the reflected representation
 constexpr int kRowThreads = 1024;
-constexpr int kRowBytes = 512;           // one warp-wide row: 32 lanes x 16 bytes
-constexpr int kTables = 8;               // T0..T3 (slicing), U0..U3 (shift by 496 bytes)
+constexpr int kRowBytes = 1024;          // one warp-wide row: 32 lanes x 32 bytes
+constexpr int kTables = 8;               // T0..T3 (slicing), U0..U3 (shift by 992 bytes)
 constexpr int kCopies = 16;
-constexpr size_t kTabSmem = static_cast<size_t>(kTables) * 256 * kCopies * sizeof(uint32_t);  // 128 KiB
+constexpr size_t kTabBytes = static_cast<size_t>(kTables) * 256 * kCopies * sizeof(uint32_t);  // 128 KiB
+constexpr size_t kTabSmem = kTabBytes + 16384;  // room to align the tables to 16 KiB
 constexpr int64_t kNominalWarps = 148 * (kRowThreads / 32);  // one CTA per SM on a B200
 constexpr int64_t kMinSpan = 4096;
 constexpr int kFinThreads = 256;
 
 struct Powers {
     uint32_t x[41];    // x[k] = x^(8 * 2^k) mod P, reflected
-    uint32_t tab[8];   // table multipliers: T_s = x^(8(s+1)), U_k = x^(8(496-k))
+    uint32_t tab[8];   // table multipliers: T_s = x^(8(s+1)), U_k = x^(8(992-k))
+};
+
+// Host-computed constants of one crc32_blocks call (every block has the
+// same size, so one set serves all blocks; cached per (bs, span)).
+struct FinalizeConsts {
+    uint32_t mtab[4][256];         // c -> c * x^(8S): xor of mtab[k][byte k of c]
+    uint32_t mult[kFinThreads];    // thread t's run -> block end: x^(8 S (nfull - end_t))
+    uint32_t x_last;               // x^(8 * last_len)
+    uint32_t init_term;            // shift(0xFFFFFFFF, bs) ^ 0xFFFFFFFF
+    int64_t nfull;                 // full spans per block
+    int64_t last_len;              // bytes of the partial last span (0: none)
+    int64_t spb;                   // spans per block
+    int64_t per;                   // full spans folded per thread
 };
 
 // a * b mod P, reflected bit order (bit 31 is the x^0 coefficient).
@@ -78,40 +98,61 @@ Powers make_powers() {
         v = gf2_mul(v, v);
     }
     for (int s = 0; s < 4; ++s) p.tab[s] = gf2_shift(kOne, static_cast<uint64_t>(s + 1), p.x);
-    for (int k = 0; k < 4; ++k) p.tab[4 + k] = gf2_shift(kOne, static_cast<uint64_t>(kRowBytes - 16 - k), p.x);
+    for (int k = 0; k < 4; ++k) p.tab[4 + k] = gf2_shift(kOne, static_cast<uint64_t>(kRowBytes - 32 - k), p.x);
     return p;
 }
 
-// Table t, entry e, copy c: word ((t * 256 + e) * kCopies + c).
-__device__ __forceinline__ uint32_t lookup(const uint32_t *tab, int t, uint32_t e, int c) {
-    return tab[((t * 256 + static_cast<int>(e)) << 4) + c];
+// Table t, entry e of this lane's copy. The tables start on a 16 KiB
+// boundary of shared memory, so the 32-bit address of entry e is
+// (e << 6) | lane_base (lane_base = table base + copy * 4) plus the table's
+// immediate offset t * 16 KiB: a shift and one LOP3 per lookup.
+template <int T>
+__device__ __forceinline__ uint32_t lut_addr(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(T * 256 * kCopies * 4));
+    return v;
 }
+// Entry index in bits [6, 14) of the address, from byte k of c.
+__device__ __forceinline__ uint32_t at0(uint32_t lb, uint32_t c) { return ((c << 6) & 0x3FC0u) | lb; }
+__device__ __forceinline__ uint32_t at1(uint32_t lb, uint32_t c) { return ((c >> 2) & 0x3FC0u) | lb; }
+__device__ __forceinline__ uint32_t at2(uint32_t lb, uint32_t c) { return ((c >> 10) & 0x3FC0u) | lb; }
+__device__ __forceinline__ uint32_t at3(uint32_t lb, uint32_t c) { return ((c >> 18) & 0x3FC0u) | lb; }
 
 // Four slicing-by-4 lookups: shift(c ^ w, 4).
-__device__ __forceinline__ uint32_t step4(const uint32_t *tab, uint32_t c, uint32_t w, int cp) {
+__device__ __forceinline__ uint32_t step4(uint32_t lb, uint32_t c, uint32_t w) {
     c ^= w;
-    return lookup(tab, 3, c & 0xFFu, cp) ^ lookup(tab, 2, (c >> 8) & 0xFFu, cp) ^
-           lookup(tab, 1, (c >> 16) & 0xFFu, cp) ^ lookup(tab, 0, c >> 24, cp);
+    return lut_addr<3>(at0(lb, c)) ^ lut_addr<2>(at1(lb, c)) ^ lut_addr<1>(at2(lb, c)) ^ lut_addr<0>(at3(lb, c));
 }
 
-// shift(c, 496) by the U tables.
-__device__ __forceinline__ uint32_t shift496(const uint32_t *tab, uint32_t c, int cp) {
-    return lookup(tab, 4, c & 0xFFu, cp) ^ lookup(tab, 5, (c >> 8) & 0xFFu, cp) ^
-           lookup(tab, 6, (c >> 16) & 0xFFu, cp) ^ lookup(tab, 7, c >> 24, cp);
+// shift(c, 992) by the U tables.
+__device__ __forceinline__ uint32_t shift_row(uint32_t lb, uint32_t c) {
+    return lut_addr<4>(at0(lb, c)) ^ lut_addr<5>(at1(lb, c)) ^ lut_addr<6>(at2(lb, c)) ^ lut_addr<7>(at3(lb, c));
 }
 
-__device__ __forceinline__ uint32_t row16(const uint32_t *tab, uint32_t c, int4 v, int cp) {
-    c = shift496(tab, c, cp);
-    c = step4(tab, c, static_cast<uint32_t>(v.x), cp);
-    c = step4(tab, c, static_cast<uint32_t>(v.y), cp);
-    c = step4(tab, c, static_cast<uint32_t>(v.z), cp);
-    return step4(tab, c, static_cast<uint32_t>(v.w), cp);
+struct V8 {
+    uint32_t w[8];
+};
+
+__device__ __forceinline__ V8 ld_v8(const void *p) {
+    V8 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                   "=r"(v.w[6]), "=r"(v.w[7])
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t row32(uint32_t lb, uint32_t c, const V8 &v) {
+    c = shift_row(lb, c);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) c = step4(lb, c, v.w[k]);
+    return c;
 }
 
 // R() of [p, p+len), one byte at a time (tails and unaligned data).
-__device__ __forceinline__ uint32_t crc_bytes(const uint32_t *tab, const unsigned char *p, uint64_t len, int cp) {
+__device__ __forceinline__ uint32_t crc_bytes(uint32_t lb, const unsigned char *p, uint64_t len) {
     uint32_t c = 0;
-    for (uint64_t i = 0; i < len; ++i) c = (c >> 8) ^ lookup(tab, 0, (c ^ p[i]) & 0xFFu, cp);
+    for (uint64_t i = 0; i < len; ++i) c = (c >> 8) ^ lut_addr<0>(at0(lb, c ^ p[i]));
     return c;
 }
 
@@ -122,43 +163,41 @@ __device__ __forceinline__ uint32_t warp_xor(uint32_t v) {
 }
 
 // R() of one span, computed by the whole warp (result valid in every lane).
-__device__ __forceinline__ uint32_t warp_span_crc(const uint32_t *tab, const unsigned char *base, uint64_t len,
-                                                  int lane, uint32_t lane_k, const Powers &pw) {
-    const int cp = lane & (kCopies - 1);
-    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) {
-        // Unaligned: lane l takes a contiguous 1/32 of the span, byte by byte.
+__device__ __forceinline__ uint32_t warp_span_crc(uint32_t lb, const unsigned char *base, uint64_t len, int lane,
+                                                  uint32_t lane_k, const Powers &pw) {
+    if ((reinterpret_cast<uintptr_t>(base) & 31u) != 0) {
+        // Not 32-byte aligned: lane l takes a contiguous 1/32 of the span.
         const uint64_t q = (len + 31) / 32;
         const uint64_t a = q * static_cast<uint64_t>(lane) < len ? q * lane : len;
         const uint64_t b = a + q < len ? a + q : len;
-        return warp_xor(gf2_shift(crc_bytes(tab, base + a, b - a, cp), len - b, pw.x));
+        return warp_xor(gf2_shift(crc_bytes(lb, base + a, b - a), len - b, pw.x));
     }
     const uint64_t nrows = len / kRowBytes;
     const uint64_t tail = len - nrows * kRowBytes;
     const uint64_t ha = nrows / 2, hb = nrows - ha;  // rows of chain A / chain B (hb >= ha)
-    const int4 *pa = reinterpret_cast<const int4 *>(base) + lane;
-    const int4 *pb = reinterpret_cast<const int4 *>(base + ha * kRowBytes) + lane;
-    constexpr int kStride = kRowBytes / 16;
+    const unsigned char *pa = base + 32 * lane;
+    const unsigned char *pb = base + ha * kRowBytes + 32 * lane;
     uint32_t ca = 0, cb = 0;
     if (hb) {
-        int4 na = ha ? ld_stream_v4(pa) : make_int4(0, 0, 0, 0);
-        int4 nb = ld_stream_v4(pb);
+        V8 na = ha ? ld_v8(pa) : V8{};
+        V8 nb = ld_v8(pb);
         for (uint64_t r = 0; r < hb; ++r) {
-            const int4 va = na, vb = nb;
-            if (r + 1 < ha) na = ld_stream_v4(pa + (r + 1) * kStride);
-            if (r + 1 < hb) nb = ld_stream_v4(pb + (r + 1) * kStride);
-            if (r < ha) ca = row16(tab, ca, va, cp);
-            cb = row16(tab, cb, vb, cp);
+            const V8 va = na, vb = nb;
+            if (r + 1 < ha) na = ld_v8(pa + (r + 1) * kRowBytes);
+            if (r + 1 < hb) nb = ld_v8(pb + (r + 1) * kRowBytes);
+            if (r < ha) ca = row32(lb, ca, va);
+            cb = row32(lb, cb, vb);
         }
     }
-    // Column l ends 496 - 16l bytes before the end of its half.
+    // Column l ends 992 - 32l bytes before the end of its half.
     const uint32_t ya = warp_xor(gf2_mul(ca, lane_k));
     const uint32_t yb = warp_xor(gf2_mul(cb, lane_k));
     uint32_t yt = 0;
     if (tail) {
         const unsigned char *t = base + nrows * kRowBytes;
-        const uint64_t a = 16u * lane < tail ? 16u * lane : tail;
-        const uint64_t b = a + 16 < tail ? a + 16 : tail;
-        yt = warp_xor(gf2_shift(crc_bytes(tab, t + a, b - a, cp), tail - b, pw.x));
+        const uint64_t a = 32u * lane < tail ? 32u * lane : tail;
+        const uint64_t b = a + 32 < tail ? a + 32 : tail;
+        yt = warp_xor(gf2_shift(crc_bytes(lb, t + a, b - a), tail - b, pw.x));
     }
     return gf2_shift(ya, hb * kRowBytes + tail, pw.x) ^ gf2_shift(yb, tail, pw.x) ^ yt;
 }
@@ -168,15 +207,22 @@ __device__ __forceinline__ uint32_t warp_span_crc(const uint32_t *tab, const uns
 __global__ void __launch_bounds__(kRowThreads, 1)
     crc_rows_kernel(const unsigned char *__restrict__ data, int64_t n, int64_t bs, int64_t span, int64_t spb,
                     uint32_t *__restrict__ span_crc, const __grid_constant__ Powers pw) {
-    extern __shared__ __align__(16) uint32_t tab[];
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t tab_base = (raw + 16383u) & ~16383u;
+    uint32_t *tab = reinterpret_cast<uint32_t *>(smem_raw + (tab_base - raw));
     for (int i = threadIdx.x; i < kTables * 256; i += blockDim.x) {
         const uint32_t v = gf2_mul(static_cast<uint32_t>(i & 255), pw.tab[i >> 8]);
 #pragma unroll
         for (int c = 0; c < kCopies; ++c) tab[(i << 4) + c] = v;
     }
     __syncthreads();
+    // The finalize kernel may be scheduled now; it waits for this grid's
+    // completion (griddepcontrol.wait) before reading span_crc.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
-    const uint32_t lane_k = gf2_shift(kOne, static_cast<uint64_t>(kRowBytes - 16 - 16 * lane), pw.x);
+    const uint32_t lb = tab_base + static_cast<uint32_t>(lane & (kCopies - 1)) * 4u;
+    const uint32_t lane_k = gf2_shift(kOne, static_cast<uint64_t>(kRowBytes - 32 - 32 * lane), pw.x);
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     const int64_t total = n * spb;
     for (int64_t g = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); g < total;
@@ -184,50 +230,38 @@ __global__ void __launch_bounds__(kRowThreads, 1)
         const int64_t b = g / spb, p = g - b * spb;
         const int64_t off = p * span;
         const int64_t len = bs - off < span ? bs - off : span;
-        const uint32_t r = warp_span_crc(tab, data + b * bs + off, static_cast<uint64_t>(len), lane, lane_k, pw);
+        const uint32_t r = warp_span_crc(lb, data + b * bs + off, static_cast<uint64_t>(len), lane, lane_k, pw);
         if (lane == 0) span_crc[g] = r;
     }
 }
 
-// One CTA per block: thread t folds spans [t*k, (t+1)*k) in order, then the
-// runs are folded by a shuffle tree and across warps.
+// One CTA per block (see the layout note at the top of the file).
 __global__ void __launch_bounds__(kFinThreads)
-    crc_finalize_kernel(const uint32_t *__restrict__ span_crc, int64_t n, int64_t bs, int64_t span, int64_t spb,
-                        uint32_t x_span, uint32_t *__restrict__ out, const __grid_constant__ Powers pw) {
-    __shared__ uint32_t wc[kFinThreads / 32];
-    __shared__ uint64_t wl[kFinThreads / 32];
-    const int64_t b = blockIdx.x;
+    crc_finalize_kernel(const uint32_t *__restrict__ span_crc, uint32_t *__restrict__ out,
+                        const __grid_constant__ FinalizeConsts fc) {
+    __shared__ uint32_t mt[4][256];
+    __shared__ uint32_t wx[kFinThreads / 32];
     const int tid = threadIdx.x;
-    const int64_t per = (spb + kFinThreads - 1) / kFinThreads;
-    const int64_t p0 = tid * per < spb ? tid * per : spb;
-    const int64_t p1 = p0 + per < spb ? p0 + per : spb;
+    for (int i = tid; i < 1024; i += kFinThreads) mt[i >> 8][i & 255] = fc.mtab[i >> 8][i & 255];
+    __syncthreads();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int64_t b = blockIdx.x;
+    const int64_t p0 = tid * fc.per < fc.nfull ? tid * fc.per : fc.nfull;
+    const int64_t p1 = p0 + fc.per < fc.nfull ? p0 + fc.per : fc.nfull;
+    const uint32_t *sc = span_crc + b * fc.spb;
     uint32_t c = 0;
-    uint64_t len = 0;
-    for (int64_t p = p0; p < p1; ++p) {
-        const int64_t l = bs - p * span < span ? bs - p * span : span;
-        // every span but the block's last is exactly `span` bytes: one multiply
-        c = (l == span ? gf2_mul(c, x_span) : gf2_shift(c, static_cast<uint64_t>(l), pw.x)) ^ span_crc[b * spb + p];
-        len += static_cast<uint64_t>(l);
-    }
-    const int lane = tid & 31;
-#pragma unroll
-    for (int k = 0; k < 5; ++k) {
-        const uint32_t oc = __shfl_down_sync(0xffffffffu, c, 1 << k);
-        const uint64_t ol = __shfl_down_sync(0xffffffffu, len, 1 << k);
-        if ((lane & ((2 << k) - 1)) == 0) {
-            c = gf2_shift(c, ol, pw.x) ^ oc;
-            len += ol;
-        }
-    }
-    if (lane == 0) {
-        wc[tid >> 5] = c;
-        wl[tid >> 5] = len;
-    }
+    for (int64_t p = p0; p < p1; ++p)
+        c = mt[0][c & 255u] ^ mt[1][(c >> 8) & 255u] ^ mt[2][(c >> 16) & 255u] ^ mt[3][c >> 24] ^ sc[p];
+    // Each run's contribution, already shifted to the end of the full spans:
+    // xor-combining needs no further shifts.
+    c = warp_xor(gf2_mul(c, fc.mult[tid]));
+    if ((tid & 31) == 0) wx[tid >> 5] = c;
     __syncthreads();
     if (tid == 0) {
         uint32_t acc = 0;
-        for (int w = 0; w < kFinThreads / 32; ++w) acc = gf2_shift(acc, wl[w], pw.x) ^ wc[w];
-        out[b] = gf2_shift(0xFFFFFFFFu, static_cast<uint64_t>(bs), pw.x) ^ acc ^ 0xFFFFFFFFu;
+        for (int w = 0; w < kFinThreads / 32; ++w) acc ^= wx[w];
+        if (fc.last_len) acc = gf2_mul(acc, fc.x_last) ^ sc[fc.nfull];
+        out[b] = fc.init_term ^ acc;
     }
 }
 
@@ -285,10 +319,49 @@ int crc32_blocks_scratch(const void *data, int64_t n, int64_t bs, uint32_t *out,
     note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const uint32_t x_span = gf2_shift(kOne, static_cast<uint64_t>(span), pw.x);
-    crc_finalize_kernel<<<static_cast<unsigned>(n), kFinThreads, 0, st>>>(scratch, n, bs, span, spb, x_span, out,
-                                                                         pw);
+    // Finalize constants (all blocks have the same size), cached per (bs, span).
+    static std::mutex fmu;
+    static int64_t f_bs = -1, f_span = -1;
+    static FinalizeConsts fc;
+    FinalizeConsts fcl;
+    {
+        std::lock_guard<std::mutex> g(fmu);
+        if (f_bs != bs || f_span != span) {
+            const uint32_t q = gf2_shift(kOne, static_cast<uint64_t>(span), pw.x);
+            for (int k = 0; k < 4; ++k)
+                for (uint32_t v = 0; v < 256; ++v) fc.mtab[k][v] = gf2_mul(v << (8 * k), q);
+            fc.nfull = bs / span;
+            fc.last_len = bs - fc.nfull * span;
+            fc.spb = spb;
+            fc.per = (fc.nfull + kFinThreads - 1) / kFinThreads;
+            if (fc.per < 1) fc.per = 1;
+            for (int t = 0; t < kFinThreads; ++t) {
+                int64_t end = (t + 1) * fc.per;
+                if (end > fc.nfull) end = fc.nfull;
+                fc.mult[t] = gf2_shift(kOne, static_cast<uint64_t>((fc.nfull - end) * span), pw.x);
+            }
+            fc.x_last = gf2_shift(kOne, static_cast<uint64_t>(fc.last_len), pw.x);
+            fc.init_term = gf2_shift(0xFFFFFFFFu, static_cast<uint64_t>(bs), pw.x) ^ 0xFFFFFFFFu;
+            f_bs = bs;
+            f_span = span;
+        }
+        fcl = fc;
+    }
+    // Programmatic dependent launch: the finalize grid is set up while the
+    // row kernel runs and waits on griddepcontrol.wait for its completion.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(n));
+    cfg.blockDim = dim3(kFinThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, crc_finalize_kernel, static_cast<const uint32_t *>(scratch), out, fcl);
     note_launch();
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
