@@ -197,6 +197,9 @@ __device__ __forceinline__ void warp_gather_bcast(const GatherBcastArgs &a, int6
             break;
         }
         if (kMc) {
+            // Lane 0 observed the stage's mbarrier phase; __syncwarp orders
+            // that observation before the other lanes' shared-memory reads.
+            __syncwarp();
             kind = __shfl_sync(0xffffffffu, kind, 0);
             if (kind == kBulk) {
                 off = static_cast<int64_t>(__shfl_sync(0xffffffffu, static_cast<long long>(off), 0));
