@@ -308,6 +308,12 @@ class RemoteMaps {
             if (__atomic_load_n(&dir[i].state, __ATOMIC_ACQUIRE) != 1 || dir[i].key != key) continue;
             DirRecord rec;
             std::memcpy(&rec, &dir[i], sizeof(rec));
+            // The owner may free and reuse the slot while it is copied; keys
+            // are never reused, so a slot still valid under the same key after
+            // the copy held this record throughout.
+            if (__atomic_load_n(&dir[i].state, __ATOMIC_ACQUIRE) != 1 ||
+                __atomic_load_n(&dir[i].key, __ATOMIC_RELAXED) != key || rec.key != key)
+                continue;
             if (addr < rec.addr || addr + len > rec.addr + rec.len) return kWcRemAccessErr;
             const int prev = gpu::current_device();
             if (prev != dev) gpu::set_device(dev);
