@@ -15,14 +15,14 @@
 // l thus sees a "column" of its span, 32 bytes every 1,024. Its register X
 // follows
 //     X <- shift(X, 1024) ^ R(row piece)
-// computed as one table shift by 992 bytes (four lookups in the U tables)
+// computed as one table shift by 992 bytes (eight nibble-table lookups)
 // followed by the ordinary slicing-by-4 steps over the 32 bytes (which
 // shift by the remaining 32). At the end lane l's column contributes
 // shift(X_l, 992 - 32l) to the span and the lanes are xor-reduced. The
 // span's rows are split in two halves so each lane runs two independent
-// chains. Lookup tables (4 slicing tables + 4 shift tables, 8 KiB) are
-// replicated 16 times, bank-interleaved, and lane l reads copy l % 16 at
-// 32-bit shared addresses, so only lanes l and l + 16 can collide on a bank.
+// chains. Lookup tables (4 slicing tables of 256 entries + 8 nibble shift
+// tables of 16 entries, 4.5 KiB) are replicated 32 times, bank-interleaved,
+// and lane l reads copy l at 32-bit shared addresses: no bank conflicts.
 //
 // crc_finalize_kernel (one CTA per block, launched with programmatic
 // dependent launch so its launch overlaps the row kernel) folds the block's
@@ -47,17 +47,23 @@ constexpr uint32_t kPoly = 0xEDB88320u;
 constexpr uint32_t kOne = 0x80000000u;  // x^0 in the reflected representation
 constexpr int kRowThreads = 1024;
 constexpr int kRowBytes = 1024;          // one warp-wide row: 32 lanes x 32 bytes
-constexpr int kTables = 8;               // T0..T3 (slicing), U0..U3 (shift by 992 bytes)
-constexpr int kCopies = 16;
-constexpr size_t kTabBytes = static_cast<size_t>(kTables) * 256 * kCopies * sizeof(uint32_t);  // 128 KiB
-constexpr size_t kTabSmem = kTabBytes + 16384;  // room to align the tables to 16 KiB
+constexpr int kCopies = 32;             // one table copy per lane: conflict-free lookups
+// Slicing tables T0..T3 (256 entries) then nibble shift tables N0..N7 (16
+// entries), each entry replicated kCopies times (128 bytes per entry).
+constexpr uint32_t kEntryBytes = kCopies * 4;
+constexpr uint32_t kTBytes = 256 * kEntryBytes;                 // 32 KiB per slicing table
+constexpr uint32_t kNBase = 4 * kTBytes;                        // nibble tables start at 128 KiB
+constexpr uint32_t kNBytes = 16 * kEntryBytes;                  // 2 KiB per nibble table
+constexpr size_t kTabBytes = kNBase + 8 * kNBytes;              // 144 KiB
+constexpr size_t kTabSmem = kTabBytes + 32768;                  // room to align the tables to 32 KiB
 constexpr int64_t kNominalWarps = 148 * (kRowThreads / 32);  // one CTA per SM on a B200
 constexpr int64_t kMinSpan = 4096;
 constexpr int kFinThreads = 256;
 
 struct Powers {
     uint32_t x[41];    // x[k] = x^(8 * 2^k) mod P, reflected
-    uint32_t tab[8];   // table multipliers: T_s = x^(8(s+1)), U_k = x^(8(992-k))
+    uint32_t tab[4];   // slicing-table multipliers: T_s = x^(8(s+1))
+    uint32_t nib[8];   // nibble-table multipliers: x^(8 * 992) (entry v of N_j is (v << 4j) times it)
 };
 
 // Host-computed constants of one crc32_blocks call (every block has the
@@ -98,35 +104,45 @@ Powers make_powers() {
         v = gf2_mul(v, v);
     }
     for (int s = 0; s < 4; ++s) p.tab[s] = gf2_shift(kOne, static_cast<uint64_t>(s + 1), p.x);
-    for (int k = 0; k < 4; ++k) p.tab[4 + k] = gf2_shift(kOne, static_cast<uint64_t>(kRowBytes - 32 - k), p.x);
+    // Nibble j of the register sits 4j bits into it: N_j[v] = (v << 4j) * x^(8*992).
+    const uint32_t row = gf2_shift(kOne, static_cast<uint64_t>(kRowBytes - 32), p.x);
+    for (int j = 0; j < 8; ++j) p.nib[j] = row;
     return p;
 }
 
-// Table t, entry e of this lane's copy. The tables start on a 16 KiB
-// boundary of shared memory, so the 32-bit address of entry e is
-// (e << 6) | lane_base (lane_base = table base + copy * 4) plus the table's
-// immediate offset t * 16 KiB: a shift and one LOP3 per lookup.
-template <int T>
+// Lookups. The tables start on a 32 KiB boundary of shared memory and
+// lane l reads copy l, so the 32-bit address of an entry is
+// (entry << 7) | lane_base (lane_base = table base + 4 * lane) plus the
+// table's immediate offset: a shift and one LOP3 per lookup.
+template <uint32_t OFF>
 __device__ __forceinline__ uint32_t lut_addr(uint32_t a) {
     uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(T * 256 * kCopies * 4));
+    asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
     return v;
 }
-// Entry index in bits [6, 14) of the address, from byte k of c.
-__device__ __forceinline__ uint32_t at0(uint32_t lb, uint32_t c) { return ((c << 6) & 0x3FC0u) | lb; }
-__device__ __forceinline__ uint32_t at1(uint32_t lb, uint32_t c) { return ((c >> 2) & 0x3FC0u) | lb; }
-__device__ __forceinline__ uint32_t at2(uint32_t lb, uint32_t c) { return ((c >> 10) & 0x3FC0u) | lb; }
-__device__ __forceinline__ uint32_t at3(uint32_t lb, uint32_t c) { return ((c >> 18) & 0x3FC0u) | lb; }
+// Byte k of c as a slicing-table entry address.
+__device__ __forceinline__ uint32_t at0(uint32_t lb, uint32_t c) { return ((c << 7) & 0x7F80u) | lb; }
+__device__ __forceinline__ uint32_t at1(uint32_t lb, uint32_t c) { return ((c >> 1) & 0x7F80u) | lb; }
+__device__ __forceinline__ uint32_t at2(uint32_t lb, uint32_t c) { return ((c >> 9) & 0x7F80u) | lb; }
+__device__ __forceinline__ uint32_t at3(uint32_t lb, uint32_t c) { return ((c >> 17) & 0x7F80u) | lb; }
 
 // Four slicing-by-4 lookups: shift(c ^ w, 4).
 __device__ __forceinline__ uint32_t step4(uint32_t lb, uint32_t c, uint32_t w) {
     c ^= w;
-    return lut_addr<3>(at0(lb, c)) ^ lut_addr<2>(at1(lb, c)) ^ lut_addr<1>(at2(lb, c)) ^ lut_addr<0>(at3(lb, c));
+    return lut_addr<3 * kTBytes>(at0(lb, c)) ^ lut_addr<2 * kTBytes>(at1(lb, c)) ^
+           lut_addr<1 * kTBytes>(at2(lb, c)) ^ lut_addr<0>(at3(lb, c));
 }
 
-// shift(c, 992) by the U tables.
+// shift(c, 992) by the nibble tables: nibble j of c, address bits [7, 11).
 __device__ __forceinline__ uint32_t shift_row(uint32_t lb, uint32_t c) {
-    return lut_addr<4>(at0(lb, c)) ^ lut_addr<5>(at1(lb, c)) ^ lut_addr<6>(at2(lb, c)) ^ lut_addr<7>(at3(lb, c));
+    return lut_addr<kNBase + 0 * kNBytes>(((c << 7) & 0x780u) | lb) ^
+           lut_addr<kNBase + 1 * kNBytes>(((c << 3) & 0x780u) | lb) ^
+           lut_addr<kNBase + 2 * kNBytes>(((c >> 1) & 0x780u) | lb) ^
+           lut_addr<kNBase + 3 * kNBytes>(((c >> 5) & 0x780u) | lb) ^
+           lut_addr<kNBase + 4 * kNBytes>(((c >> 9) & 0x780u) | lb) ^
+           lut_addr<kNBase + 5 * kNBytes>(((c >> 13) & 0x780u) | lb) ^
+           lut_addr<kNBase + 6 * kNBytes>(((c >> 17) & 0x780u) | lb) ^
+           lut_addr<kNBase + 7 * kNBytes>(((c >> 21) & 0x780u) | lb);
 }
 
 struct V8 {
@@ -152,7 +168,7 @@ __device__ __forceinline__ uint32_t row32(uint32_t lb, uint32_t c, const V8 &v) 
 // R() of [p, p+len), one byte at a time (tails and unaligned data).
 __device__ __forceinline__ uint32_t crc_bytes(uint32_t lb, const unsigned char *p, uint64_t len) {
     uint32_t c = 0;
-    for (uint64_t i = 0; i < len; ++i) c = (c >> 8) ^ lut_addr<0>(at0(lb, c ^ p[i]));
+    for (uint64_t i = 0; i < len; ++i) c = (c >> 8) ^ lut_addr<0>(at0(lb, c ^ p[i]));  // T0
     return c;
 }
 
@@ -209,19 +225,22 @@ __global__ void __launch_bounds__(kRowThreads, 1)
                     uint32_t *__restrict__ span_crc, const __grid_constant__ Powers pw) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t tab_base = (raw + 16383u) & ~16383u;
+    const uint32_t tab_base = (raw + 32767u) & ~32767u;
     uint32_t *tab = reinterpret_cast<uint32_t *>(smem_raw + (tab_base - raw));
-    for (int i = threadIdx.x; i < kTables * 256; i += blockDim.x) {
-        const uint32_t v = gf2_mul(static_cast<uint32_t>(i & 255), pw.tab[i >> 8]);
-#pragma unroll
-        for (int c = 0; c < kCopies; ++c) tab[(i << 4) + c] = v;
+    for (int i = threadIdx.x; i < 4 * 256 + 8 * 16; i += blockDim.x) {
+        // slicing entries first (i < 1024), then the nibble entries
+        const uint32_t v = i < 1024 ? gf2_mul(static_cast<uint32_t>(i & 255), pw.tab[i >> 8])
+                                    : gf2_mul(static_cast<uint32_t>((i - 1024) & 15) << (4 * ((i - 1024) >> 4)),
+                                              pw.nib[(i - 1024) >> 4]);
+#pragma unroll 8
+        for (int c = 0; c < kCopies; ++c) tab[i * kCopies + c] = v;
     }
     __syncthreads();
     // The finalize kernel may be scheduled now; it waits for this grid's
     // completion (griddepcontrol.wait) before reading span_crc.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int lane = threadIdx.x & 31;
-    const uint32_t lb = tab_base + static_cast<uint32_t>(lane & (kCopies - 1)) * 4u;
+    const uint32_t lb = tab_base + static_cast<uint32_t>(lane) * 4u;
     const uint32_t lane_k = gf2_shift(kOne, static_cast<uint64_t>(kRowBytes - 32 - 32 * lane), pw.x);
     const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     const int64_t total = n * spb;
