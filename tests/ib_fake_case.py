@@ -4,7 +4,11 @@ mlx5_0 + cross-NUMA mlx5_4 is absent, so mlx5_0 <-> mlx5_0 and mlx5_1 <->
 mlx5_1), buffer query, PUT/GET/scatter with byte checks. With
 MPCOMM_FAULT_INJECT_* set, the QPs of rail 0 go to ERR and the transfer must
 still complete (completions flush, rail 0 is quarantined, chunks re-post on
-rail 1). Prints "ib fake ok" on success."""
+rail 1). With --gpu the buffers are B200 HBM (torch CUDA tensors): the
+backend must register them through GPUDirect dma-buf
+(cuMemGetHandleForAddressRange -> ibv_reg_dmabuf_mr; the fake moves their
+bytes with the driver's UVA copy) and the PUT/GET must round-trip
+bit-exact. Prints "ib fake ok" on success."""
 import ctypes
 import os
 import sys
@@ -56,5 +60,47 @@ def main():
     print("ib fake ok", flush=True)
 
 
+def main_gpu():
+    import torch
+
+    lib = ctypes.CDLL(os.environ["MPCOMM_IBVERBS_LIB"])
+    lib.fake_ibv_dmabuf_registrations.restype = ctypes.c_int
+    n = (24 << 20) + 4096
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda", generator=g)
+    dst = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    tgt = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    a, b = mpcomm.MPComm(), mpcomm.MPComm()
+    assert a.init("A") == 0 and b.init("B") == 0
+    assert a.get_fabric_name() == "ib", a.get_fabric_name()
+    before = lib.fake_ibv_dmabuf_registrations()
+    assert b.register_memory(tgt.data_ptr(), n) == 0
+    assert b.publish_buffer(tgt.data_ptr(), n) == 0
+    assert b.start_accept_thread() == 0
+    for x in (src, dst):
+        assert a.register_memory(x.data_ptr(), n) == 0
+    regs = lib.fake_ibv_dmabuf_registrations() - before
+    # every buffer on every NIC went through the dma-buf path
+    assert regs == 3 * len(a.get_active_devices()), regs
+    port = b.get_tcp_port()
+    assert a.connect("B", "127.0.0.1", port) == 0
+    assert a.query_remote_buffers("B", "127.0.0.1", port)
+    h = a.put_async(src.data_ptr(), "B", tgt.data_ptr(), n)
+    assert a.wait_transfer(h, 20000) == 0, "PUT into HBM failed"
+    a.release_transfer(h)
+    torch.cuda.synchronize()
+    assert torch.equal(tgt, src), "PUT mismatch"
+    h = a.get_async(dst.data_ptr() + 4096, "B", tgt.data_ptr() + 4096, n - 4096)
+    assert a.wait_transfer(h, 20000) == 0, "GET from HBM failed"
+    a.release_transfer(h)
+    torch.cuda.synchronize()
+    assert torch.equal(dst[4096:], src[4096:]) and not dst[:4096].any(), "GET mismatch"
+    a.shutdown()
+    b.shutdown()
+    print(f"ib fake ok (dma-buf registrations: {regs})", flush=True)
+
+
 if __name__ == "__main__":
-    main()
+    main_gpu() if "--gpu" in sys.argv else main()

@@ -5,9 +5,22 @@
 // rkey and bounds checks against the destination device's registrations and
 // queues one completion per WR on the send CQ, drained by poll_cq (slot 11).
 // A QP in ERR flushes WRs with status 5 (IBV_WC_WR_FLUSH_ERR).
+// ibv_reg_dmabuf_mr accepts a dma-buf fd (as exported by the CUDA driver
+// for device memory) and registers the iova range; WRs touching such a
+// region are executed with the driver's UVA cuMemCpy in the region's
+// context, so GPU tests exercise the GPUDirect registration path
+// (cuMemGetHandleForAddressRange -> ibv_reg_dmabuf_mr) on real HBM without
+// a NIC. fake_ibv_dmabuf_registrations() counts those registrations.
 // Built as a shared library by CMake; it shares the ABI declarations of
 // csrc/transport/ib_verbs.h, so it checks the backend's logic, not the
 // system ABI.
+#include <cuda.h>
+#include <dlfcn.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <cerrno>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -46,6 +59,7 @@ struct FakeQp {
 struct FakeMr {
     Mr mr;
     FakeCtx *owner;
+    bool device = false;  // GPU memory (dma-buf, or plain reg_mr of a device pointer)
 };
 
 std::mutex g_mu;
@@ -54,12 +68,69 @@ std::map<uint32_t, FakeQp *> g_qps;
 std::map<uint32_t, FakeMr *> g_mrs;  // key -> region (lkey == rkey)
 uint32_t g_next_qpn = 0x300, g_next_key = 0x4000;
 
-bool mr_ok(uint32_t key, uint64_t addr, uint64_t len) {
+std::atomic<int> g_dmabuf_regs{0};
+
+FakeMr *mr_find(uint32_t key, uint64_t addr, uint64_t len) {
     auto it = g_mrs.find(key);
-    if (it == g_mrs.end()) return false;
+    if (it == g_mrs.end()) return nullptr;
     const Mr &m = it->second->mr;
     const uint64_t a = reinterpret_cast<uint64_t>(m.addr);
-    return addr >= a && addr + len <= a + m.length;
+    return addr >= a && addr + len <= a + m.length ? it->second : nullptr;
+}
+
+// CUDA driver entry points, resolved when the first dma-buf region arrives.
+struct CuApi {
+    CUresult (*memcpy)(CUdeviceptr, CUdeviceptr, size_t) = nullptr;
+    CUresult (*ptr_attr)(void *, CUpointer_attribute, CUdeviceptr) = nullptr;
+    CUresult (*push)(CUcontext) = nullptr;
+    CUresult (*pop)(CUcontext *) = nullptr;
+};
+const CuApi *cu();
+
+// True for device memory of a CUDA context in this process (the driver
+// must already be loaded; CPU-only processes never see device pointers).
+bool is_device_ptr(const void *p) {
+    const CuApi *api = cu();
+    if (!api) return false;
+    unsigned int type = 0;
+    return api->ptr_attr(&type, CU_POINTER_ATTRIBUTE_MEMORY_TYPE, reinterpret_cast<CUdeviceptr>(p)) ==
+               CUDA_SUCCESS &&
+           type == CU_MEMORYTYPE_DEVICE;
+}
+
+const CuApi *cu() {
+    static CuApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libcuda.so.1", RTLD_NOW | RTLD_NOLOAD);  // only if the process uses CUDA
+        if (h) {
+            api.memcpy = reinterpret_cast<decltype(api.memcpy)>(dlsym(h, "cuMemcpy"));
+            api.ptr_attr = reinterpret_cast<decltype(api.ptr_attr)>(dlsym(h, "cuPointerGetAttribute"));
+            api.push = reinterpret_cast<decltype(api.push)>(dlsym(h, "cuCtxPushCurrent_v2"));
+            api.pop = reinterpret_cast<decltype(api.pop)>(dlsym(h, "cuCtxPopCurrent_v2"));
+        }
+    });
+    return api.memcpy && api.ptr_attr && api.push && api.pop ? &api : nullptr;
+}
+
+// The "NIC DMA": host memmove, or a UVA copy in the device region's context.
+bool move_bytes(void *dst, const void *src, size_t n, const FakeMr *dev_mr) {
+    if (!dev_mr) {
+        std::memmove(dst, src, n);
+        return true;
+    }
+    const CuApi *api = cu();
+    if (!api) return false;
+    CUcontext ctx = nullptr;
+    if (api->ptr_attr(&ctx, CU_POINTER_ATTRIBUTE_CONTEXT, reinterpret_cast<CUdeviceptr>(dev_mr->mr.addr)) !=
+            CUDA_SUCCESS ||
+        !ctx || api->push(ctx) != CUDA_SUCCESS)
+        return false;
+    const bool ok = api->memcpy(reinterpret_cast<CUdeviceptr>(dst), reinterpret_cast<CUdeviceptr>(src), n) ==
+                    CUDA_SUCCESS;
+    CUcontext popped = nullptr;
+    api->pop(&popped);
+    return ok;
 }
 
 int fake_post_send(Qp *qp, SendWr *wr, SendWr **bad) {
@@ -80,19 +151,22 @@ int fake_post_send(Qp *qp, SendWr *wr, SendWr **bad) {
         } else {
             const Sge &s = w->sg_list[0];
             auto peer = g_qps.find(q->dest_qpn);
-            if (!mr_ok(s.lkey, s.addr, s.length)) {
+            FakeMr *lm = mr_find(s.lkey, s.addr, s.length);
+            FakeMr *rm = lm ? mr_find(w->wr.rkey, w->wr.remote_addr, s.length) : nullptr;
+            if (!lm) {
                 c.status = 4;  // local protection error
             } else if (peer == g_qps.end() || peer->second->qp.state == kQpsErr) {
                 c.status = 12;  // retry exceeded
-            } else if (!mr_ok(w->wr.rkey, w->wr.remote_addr, s.length)) {
+            } else if (!rm) {
                 c.status = 10;  // remote access error
             } else {
                 void *local = reinterpret_cast<void *>(s.addr);
                 void *remote = reinterpret_cast<void *>(w->wr.remote_addr);
-                if (w->opcode == kWrRdmaWrite) std::memmove(remote, local, s.length);
-                else std::memmove(local, remote, s.length);
-                c.status = 0;
-                c.byte_len = s.length;
+                const FakeMr *dev = lm->device ? lm : (rm->device ? rm : nullptr);
+                const bool ok = w->opcode == kWrRdmaWrite ? move_bytes(remote, local, s.length, dev)
+                                                          : move_bytes(local, remote, s.length, dev);
+                c.status = ok ? 0 : 4;
+                c.byte_len = ok ? s.length : 0;
             }
         }
         if (w->send_flags & kSendSignaled) cq->wcs.push_back(c);
@@ -175,9 +249,34 @@ Mr *ibv_reg_mr(Pd *pd, void *addr, size_t len, int) {
     m->mr.addr = addr;
     m->mr.length = len;
     m->mr.lkey = m->mr.rkey = g_next_key++;
+    m->device = is_device_ptr(addr);  // nvidia-peermem style registration of HBM
     g_mrs[m->mr.lkey] = m;
     return &m->mr;
 }
+// GPUDirect registration of a dma-buf (device memory exported by the CUDA
+// driver): `iova` is the virtual address WRs use, `offset` the start within
+// the dma-buf. The fd must be open; the fake keeps no reference to it.
+Mr *ibv_reg_dmabuf_mr(Pd *pd, uint64_t offset, size_t len, uint64_t iova, int fd, int) {
+    struct stat st;
+    if (fd < 0 || fstat(fd, &st) != 0 || len == 0 || !cu()) {
+        errno = EINVAL;
+        return nullptr;
+    }
+    (void)offset;
+    std::lock_guard<std::mutex> g(g_mu);
+    FakeMr *m = new FakeMr();
+    m->owner = reinterpret_cast<FakeCtx *>(pd);
+    m->mr.context = &m->owner->ctx;
+    m->mr.pd = pd;
+    m->mr.addr = reinterpret_cast<void *>(iova);
+    m->mr.length = len;
+    m->mr.lkey = m->mr.rkey = g_next_key++;
+    m->device = true;
+    g_mrs[m->mr.lkey] = m;
+    g_dmabuf_regs.fetch_add(1);
+    return &m->mr;
+}
+int fake_ibv_dmabuf_registrations() { return g_dmabuf_regs.load(); }
 int ibv_dereg_mr(Mr *mr) {
     std::lock_guard<std::mutex> g(g_mu);
     g_mrs.erase(mr->lkey);

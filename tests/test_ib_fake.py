@@ -9,12 +9,12 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 LIB = os.path.join(ROOT, "tests", "native", "bin", "libfake_ibverbs.so")
 
 
-def _run(extra):
+def _run(extra, args=()):
     assert os.path.exists(LIB), "fake provider not built (run __graft_entry__.build())"
     env = dict(os.environ, MPCOMM_FABRIC="ib", MPCOMM_IBVERBS_LIB=LIB, MPCOMM_GID_INDEX="-1",
                MPCOMM_LOG_LEVEL="1", PYTHONPATH=ROOT, **extra)
-    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "ib_fake_case.py")], capture_output=True,
-                       text=True, env=env, timeout=120)
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "tests", "ib_fake_case.py"), *args],
+                       capture_output=True, text=True, env=env, timeout=120)
     assert r.returncode == 0 and "ib fake ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
     return r
 
@@ -32,3 +32,16 @@ def test_ib_fault_injection_reposts_on_healthy_rail(mode):
     moved = [int(x) for x in re.findall(r"fault injection \(\w+\) moved (\d+) QPs to ERR", r.stderr)]
     assert moved and max(moved) > 0, r.stderr[-2000:]
     assert "quarantined" in r.stderr
+
+
+@pytest.mark.gpu
+def test_ib_gpudirect_dmabuf_registration_of_hbm():
+    """HBM buffers on the ib fabric are registered through dma-buf
+    (cuMemGetHandleForAddressRange on the B200, ibv_reg_dmabuf_mr on every
+    NIC) and PUT/GET between them round-trip bit-exact."""
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    r = _run({}, ["--gpu"])
+    assert "dma-buf registrations: 6" in r.stdout, r.stdout[-2000:]
