@@ -188,12 +188,25 @@ class IbRail final : public Rail {
             using HandleFn = CUresult (*)(void *, CUdeviceptr, size_t, CUmemRangeHandleType,
                                           unsigned long long);
             auto fn = reinterpret_cast<HandleFn>(gpu::driver_symbol("cuMemGetHandleForAddressRange"));
+            // Export the whole allocation (the driver refuses sub-ranges of a
+            // cudaMalloc allocation on this platform) and register the
+            // buffer at its offset in it; 64 KiB-aligned span otherwise.
             const uintptr_t page = 64 * 1024;
-            const uintptr_t a0 = reinterpret_cast<uintptr_t>(addr) & ~(page - 1);
-            const size_t span = ((reinterpret_cast<uintptr_t>(addr) + len + page - 1) & ~(page - 1)) - a0;
+            uintptr_t a0 = reinterpret_cast<uintptr_t>(addr) & ~(page - 1);
+            size_t span = ((reinterpret_cast<uintptr_t>(addr) + len + page - 1) & ~(page - 1)) - a0;
+            if (pi.base && pi.size && pi.base <= reinterpret_cast<uintptr_t>(addr) &&
+                reinterpret_cast<uintptr_t>(addr) + len <= pi.base + pi.size) {
+                a0 = pi.base;
+                span = pi.size;
+            }
             int fd = -1;
-            if (fn && fn(&fd, static_cast<CUdeviceptr>(a0), span, CU_MEM_RANGE_HANDLE_TYPE_DMA_BUF_FD, 0) ==
-                          CUDA_SUCCESS) {
+            // flags 0, then 1 (CU_MEM_RANGE_FLAG_DMA_BUF_MAPPING_TYPE_PCIE, CUDA 12.8+: a
+            // PCIe BAR1 mapping, which some platforms require for NIC access).
+            bool exported = false;
+            for (unsigned long long flags = 0; fn && !exported && flags <= 1; ++flags)
+                exported = fn(&fd, static_cast<CUdeviceptr>(a0), span, CU_MEM_RANGE_HANDLE_TYPE_DMA_BUF_FD,
+                              flags) == CUDA_SUCCESS;
+            if (exported) {
                 mr = api_->reg_dmabuf_mr(pd_, reinterpret_cast<uintptr_t>(addr) - a0, len,
                                          reinterpret_cast<uintptr_t>(addr), fd, access);
                 ::close(fd);

@@ -75,6 +75,28 @@ def main_gpu():
     a, b = mpcomm.MPComm(), mpcomm.MPComm()
     assert a.init("A") == 0 and b.init("B") == 0
     assert a.get_fabric_name() == "ib", a.get_fabric_name()
+    # What the driver offers: dma-buf support of the device, and an export
+    # of this exact range (the backend exports 64 KiB-aligned spans).
+    cuda = ctypes.CDLL("libcuda.so.1")
+    dev = ctypes.c_int()
+    assert cuda.cuDeviceGet(ctypes.byref(dev), 0) == 0
+    sup = ctypes.c_int(-1)
+    cuda.cuDeviceGetAttribute(ctypes.byref(sup), 124, dev)  # CU_DEVICE_ATTRIBUTE_DMA_BUF_SUPPORTED
+    def export_rc(a0, span, flags=0):
+        fd = ctypes.c_int(-1)
+        rc = cuda.cuMemGetHandleForAddressRange(ctypes.byref(fd), ctypes.c_uint64(a0), ctypes.c_size_t(span),
+                                                1, ctypes.c_ulonglong(flags))  # CU_MEM_RANGE_HANDLE_TYPE_DMA_BUF_FD
+        if rc == 0:
+            os.close(fd.value)
+        return rc
+
+    base, size = ctypes.c_uint64(0), ctypes.c_size_t(0)
+    assert cuda.cuMemGetAddressRange_v2(ctypes.byref(base), ctypes.byref(size), ctypes.c_uint64(src.data_ptr())) == 0
+    rc = export_rc(base.value, size.value)  # the whole allocation, as the backend exports it
+    sub = export_rc(src.data_ptr() & ~0xFFFF, ((src.data_ptr() + n + 0xFFFF) & ~0xFFFF) - (src.data_ptr() & ~0xFFFF))
+    pcie = export_rc(base.value, size.value, 1)  # CU_MEM_RANGE_FLAG_DMA_BUF_MAPPING_TYPE_PCIE
+    print(f"driver: dma_buf_supported={sup.value} export_rc={rc} subrange_rc={sub} pcie_flag_rc={pcie} "
+          f"allocation={size.value} bytes", flush=True)
     before = lib.fake_ibv_dmabuf_registrations()
     assert b.register_memory(tgt.data_ptr(), n) == 0
     assert b.publish_buffer(tgt.data_ptr(), n) == 0
@@ -82,8 +104,13 @@ def main_gpu():
     for x in (src, dst):
         assert a.register_memory(x.data_ptr(), n) == 0
     regs = lib.fake_ibv_dmabuf_registrations() - before
-    # every buffer on every NIC went through the dma-buf path
-    assert regs == 3 * len(a.get_active_devices()), regs
+    if sup.value == 1 and rc == 0:
+        # every buffer on every NIC went through the dma-buf path
+        assert regs == 3 * len(a.get_active_devices()), regs
+    else:
+        # no dma-buf export here: the backend falls back to ibv_reg_mr
+        # (nvidia-peermem style); the transfers below still run on HBM
+        assert regs == 0, regs
     port = b.get_tcp_port()
     assert a.connect("B", "127.0.0.1", port) == 0
     assert a.query_remote_buffers("B", "127.0.0.1", port)
@@ -99,7 +126,8 @@ def main_gpu():
     assert torch.equal(dst[4096:], src[4096:]) and not dst[:4096].any(), "GET mismatch"
     a.shutdown()
     b.shutdown()
-    print(f"ib fake ok (dma-buf registrations: {regs})", flush=True)
+    print(f"ib fake ok (dma-buf registrations: {regs}, dma_buf_supported={sup.value}, export_rc={rc})",
+          flush=True)
 
 
 if __name__ == "__main__":
