@@ -120,11 +120,18 @@ __device__ __forceinline__ uint32_t lut_addr(uint32_t a) {
     asm volatile("ld.shared.u32 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(OFF));
     return v;
 }
-// Byte k of c as a slicing-table entry address.
-__device__ __forceinline__ uint32_t at0(uint32_t lb, uint32_t c) { return ((c << 7) & 0x7F80u) | lb; }
-__device__ __forceinline__ uint32_t at1(uint32_t lb, uint32_t c) { return ((c >> 1) & 0x7F80u) | lb; }
-__device__ __forceinline__ uint32_t at2(uint32_t lb, uint32_t c) { return ((c >> 9) & 0x7F80u) | lb; }
-__device__ __forceinline__ uint32_t at3(uint32_t lb, uint32_t c) { return ((c >> 17) & 0x7F80u) | lb; }
+// Byte k of c as a slicing-table entry address: PRMT extracts the byte and
+// a multiply-add scales it (mad.lo runs on the FMA pipe, which the table
+// walk leaves idle, instead of a shift and a LOP3 on the integer ALU).
+__device__ __forceinline__ uint32_t mad128(uint32_t e, uint32_t lb) {
+    uint32_t a;
+    asm("mad.lo.u32 %0, %1, 128, %2;" : "=r"(a) : "r"(e), "r"(lb));
+    return a;
+}
+__device__ __forceinline__ uint32_t at0(uint32_t lb, uint32_t c) { return mad128(__byte_perm(c, 0u, 0x4440u), lb); }
+__device__ __forceinline__ uint32_t at1(uint32_t lb, uint32_t c) { return mad128(__byte_perm(c, 0u, 0x4441u), lb); }
+__device__ __forceinline__ uint32_t at2(uint32_t lb, uint32_t c) { return mad128(__byte_perm(c, 0u, 0x4442u), lb); }
+__device__ __forceinline__ uint32_t at3(uint32_t lb, uint32_t c) { return mad128(c >> 24, lb); }
 
 // Four slicing-by-4 lookups: shift(c ^ w, 4).
 __device__ __forceinline__ uint32_t step4(uint32_t lb, uint32_t c, uint32_t w) {
