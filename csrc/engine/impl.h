@@ -273,6 +273,7 @@ class MPComm::Impl {
 
     // impl_xfer.cc
     void workerLoop(Worker *w);
+    void wakeWorker(Worker *w);
     void postChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched);
     void handleCompletion(Worker *w, const fabric::WorkCompletion &wc);
     void retire(Worker *w);
@@ -351,6 +352,10 @@ class MPComm::Impl {
     mutable std::mutex xfer_mu_;
     std::unordered_map<uint64_t, std::shared_ptr<Transfer>> transfers_;
     std::unique_ptr<std::atomic<Transfer *>[]> handle_table_;
+    // waitTransfer blocks here after a short spin; finishTransfer notifies.
+    std::mutex done_mu_;
+    std::condition_variable done_cv_;
+    std::atomic<int> done_waiters_{0};
     // Submitted transfers not yet taken by their worker (keeps them alive
     // even if the user releases the handle immediately).
     std::mutex admit_mu_;
@@ -421,6 +426,13 @@ struct MPComm::Impl::Worker {
     std::mutex inbox_mu;
     std::vector<fabric::WorkCompletion> inbox;
     std::atomic<bool> inbox_nonempty{false};
+    // Idle sleep with a doorbell: submitters (and workers forwarding
+    // completions) bump `doorbell` and wake the worker when it sleeps, so a
+    // transfer that arrives after a quiet period starts at once.
+    std::mutex wake_mu;
+    std::condition_variable wake_cv;
+    std::atomic<uint64_t> doorbell{0};
+    std::atomic<bool> sleeping{false};
     std::array<size_t, kMaxRails> rail_posted{}, rail_completed{};
     std::array<std::array<size_t, kMaxQpsPerRail>, kMaxRails> qp_posted{}, qp_completed{};
     uint64_t seen_epoch = 0;

@@ -148,6 +148,7 @@ void MPComm::Impl::shutdown() {
     stopQosChannels();
     if (staging_) staging_.reset();
     running_ = false;
+    for (auto &w : workers_) wakeWorker(w.get());
     for (auto &w : workers_)
         if (w->thread.joinable()) w->thread.join();
     workers_.clear();

@@ -2,6 +2,8 @@
 // Parity: reference src/mpcomm.cpp:4929-5479 (submit), :5969-7061 (worker),
 // :7213-7357 (completion routing), :5563-5740 (completion API),
 // :7068-7155 (quarantine probe), :5802-5929 (fault injection).
+#include <sys/prctl.h>
+
 #include <algorithm>
 #include <cstring>
 #include <limits>
@@ -151,7 +153,16 @@ TransferHandle MPComm::Impl::submit(uintptr_t local, const std::vector<std::stri
     }
     Worker *w = workers_[t->owner].get();
     while (!w->queue.try_push(h)) cpu_relax();
+    wakeWorker(w);
     return h;
+}
+
+void MPComm::Impl::wakeWorker(Worker *w) {
+    w->doorbell.fetch_add(1);  // seq_cst: ordered against the worker's `sleeping` store
+    if (w->sleeping.load()) {
+        std::lock_guard<std::mutex> g(w->wake_mu);
+        w->wake_cv.notify_one();
+    }
 }
 
 std::shared_ptr<Transfer> MPComm::Impl::newCompositeTransfer(Direction dir, uintptr_t local,
@@ -179,6 +190,9 @@ std::shared_ptr<Transfer> MPComm::Impl::newCompositeTransfer(Direction dir, uint
 // ---------------------------------------------------------------------------
 void MPComm::Impl::workerLoop(Worker *w) {
     topo::bind_thread_to_cpus(topo::numa_cpus(w->numa));
+    // Short sleeps of this thread should be short: the default 50 us timer
+    // slack would stretch the 20 us poll sleep to ~70 us.
+    prctl(PR_SET_TIMERSLACK, 1000UL, 0, 0, 0);
     std::vector<fabric::WorkCompletion> wcs(std::max<size_t>(cfg_.poll_batch_size, 1));
     std::vector<fabric::QueuePair *> touched;
     std::vector<fabric::WorkCompletion> inbox;
@@ -267,7 +281,22 @@ void MPComm::Impl::workerLoop(Worker *w) {
         if (progress) {
             idle = 0;
         } else if (++idle > cfg_.max_idle_spins) {
-            std::this_thread::sleep_for(std::chrono::microseconds(20));
+            if (w->active.empty()) {
+                // Nothing in flight: sleep until a submission or a forwarded
+                // completion rings the doorbell (1 ms cap for maintenance).
+                const uint64_t seen = w->doorbell.load();
+                w->sleeping.store(true);
+                {
+                    std::unique_lock<std::mutex> lk(w->wake_mu);
+                    w->wake_cv.wait_for(lk, std::chrono::milliseconds(1), [&] {
+                        return w->doorbell.load() != seen || !running_.load(std::memory_order_acquire);
+                    });
+                }
+                w->sleeping.store(false);
+            } else {
+                // Waiting on completions: poll every ~20 us.
+                std::this_thread::sleep_for(std::chrono::microseconds(20));
+            }
         } else {
             cpu_relax();
         }
@@ -414,9 +443,12 @@ void MPComm::Impl::handleCompletion(Worker *w, const fabric::WorkCompletion &wc)
     if (!t || t->composite || rail >= rails_.size() || q >= kMaxQpsPerRail) return;  // orphan
     if (t->owner != w->id) {
         Worker *o = workers_[t->owner].get();
-        std::lock_guard<std::mutex> g(o->inbox_mu);
-        o->inbox.push_back(wc);
-        o->inbox_nonempty.store(true, std::memory_order_release);
+        {
+            std::lock_guard<std::mutex> g(o->inbox_mu);
+            o->inbox.push_back(wc);
+            o->inbox_nonempty.store(true, std::memory_order_release);
+        }
+        wakeWorker(o);
         return;
     }
     ++w->rail_completed[rail];
@@ -542,17 +574,30 @@ int MPComm::Impl::waitTransfer(TransferHandle h, int timeout_ms) {
     auto t = findTransfer(h);
     if (!t) return MPCOMM_ERR_INVALID_HANDLE;
     const auto t0 = Clock::now();
-    size_t spins = 0;
-    while (!t->finished.load(std::memory_order_acquire)) {
-        if (++spins < 20000) {
-            cpu_relax();
-        } else {
-            std::this_thread::sleep_for(std::chrono::microseconds(5));
-        }
-        if (timeout_ms >= 0 && (spins & 63) == 0 &&
-            std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count() >= timeout_ms)
-            return MPCOMM_ERR_TIMEOUT;
+    // Spin briefly (short transfers finish within it), then block on the
+    // completion condition variable, which finishTransfer notifies.
+    for (size_t spins = 0; spins < 4096; ++spins) {
+        if (t->finished.load(std::memory_order_acquire)) return t->error.load(std::memory_order_acquire);
+        cpu_relax();
     }
+    done_waiters_.fetch_add(1);
+    {
+        std::unique_lock<std::mutex> lk(done_mu_);
+        while (!t->finished.load(std::memory_order_acquire)) {
+            auto step = std::chrono::milliseconds(10);
+            if (timeout_ms >= 0) {
+                const auto left = std::chrono::milliseconds(timeout_ms) -
+                                  std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0);
+                if (left.count() <= 0) {
+                    done_waiters_.fetch_sub(1);
+                    return MPCOMM_ERR_TIMEOUT;
+                }
+                if (left < step) step = left;
+            }
+            done_cv_.wait_for(lk, step);
+        }
+    }
+    done_waiters_.fetch_sub(1);
     return t->error.load(std::memory_order_acquire);
 }
 
@@ -610,7 +655,11 @@ void MPComm::Impl::releaseTransfer(TransferHandle h) {
 void MPComm::Impl::finishTransfer(Transfer *t) {
     t->t_end = Clock::now();
     nvtx::end(t->nvtx);
-    t->finished.store(true, std::memory_order_release);
+    t->finished.store(true);  // seq_cst: ordered against done_waiters_ below
+    if (done_waiters_.load() > 0) {
+        std::lock_guard<std::mutex> g(done_mu_);  // a waiter is either before its check or in wait
+        done_cv_.notify_all();
+    }
     if (t->life.fetch_or(1) & 2) {
         handle_table_[t->handle].store(nullptr, std::memory_order_release);
         handles_.release(t->handle);
