@@ -320,3 +320,21 @@ def test_native_binaries(name):
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     assert "ERROR: AddressSanitizer" not in r.stderr
     assert "WARNING: ThreadSanitizer" not in r.stderr
+
+
+def test_type_stub_covers_the_native_module():
+    """mpcomm/_mpcomm.pyi declares every public method of MPComm and every
+    module function, so IDEs and type checkers see the whole API."""
+    import ast
+
+    import mpcomm
+
+    tree = ast.parse(open(os.path.join(ROOT, "mpcomm", "_mpcomm.pyi")).read())
+    cls = next(n for n in tree.body if isinstance(n, ast.ClassDef) and n.name == "MPComm")
+    stub_methods = {f.name for f in cls.body if isinstance(f, ast.FunctionDef)}
+    native = {n for n in dir(mpcomm._mpcomm.MPComm) if not n.startswith("_")}
+    assert native <= stub_methods, sorted(native - stub_methods)
+    stub_funcs = {f.name for f in tree.body if isinstance(f, ast.FunctionDef)}
+    funcs = {n for n in dir(mpcomm._mpcomm) if not n.startswith("_") and callable(getattr(mpcomm._mpcomm, n))
+             and n not in ("MPComm", "MPCommError")}
+    assert funcs <= stub_funcs, sorted(funcs - stub_funcs)
