@@ -239,6 +239,10 @@ void MPComm::Impl::stopAcceptThread() {
     if (accept_thread_.joinable()) accept_thread_.join();
 }
 
+namespace {
+constexpr int kFirstWordTimeoutMs = 2000;
+}  // namespace
+
 void MPComm::Impl::acceptLoop() {
     while (accept_running_.load()) {
         int fd = ::accept4(listen_fd_, nullptr, nullptr, SOCK_CLOEXEC);
@@ -250,7 +254,12 @@ void MPComm::Impl::acceptLoop() {
             ::close(fd);
             break;
         }
-        net::set_timeouts(fd, net::ctrl_timeout_ms());
+        // Connections are served one at a time (as the reference does), so a
+        // client that connects and stays silent (a port scanner, a half-open
+        // peer) may hold the loop only briefly: every legitimate client sends
+        // its first word right after connecting.
+        const int full = net::ctrl_timeout_ms();
+        net::set_timeouts(fd, full > 0 && full < kFirstWordTimeoutMs ? full : kFirstWordTimeoutMs);
         int one = 1;
         setsockopt(fd, IPPROTO_TCP, TCP_NODELAY, &one, sizeof(one));
         uint32_t msg = 0;
@@ -258,6 +267,7 @@ void MPComm::Impl::acceptLoop() {
             ::close(fd);
             continue;
         }
+        net::set_timeouts(fd, full);
         if (msg == kMsgTypeBufferQuery) {
             handleBufferQuery(fd);
         } else if (msg == kMsgTypeQosControlOpen) {

@@ -117,3 +117,54 @@ def test_quarantine_probe_readmits_rail(lo_env, monkeypatch):
     finally:
         a.shutdown()
         b.shutdown()
+
+
+def test_silent_client_holds_the_accept_loop_only_briefly(server):
+    """A client that connects and sends nothing (port scanner, half-open
+    peer) must not block the control plane for the full control timeout:
+    a buffer query right behind it is answered within a few seconds."""
+    idle = socket.create_connection(("127.0.0.1", server.get_tcp_port()))
+    try:
+        time.sleep(0.1)  # the accept loop is now waiting on the silent client
+        t0 = time.monotonic()
+        with socket.create_connection(("127.0.0.1", server.get_tcp_port())) as s:
+            s.settimeout(15)
+            s.sendall(struct.pack("<I", 0x4D504251))
+            assert struct.unpack("<I", _recv(s, 4))[0] == 0
+        assert time.monotonic() - t0 < 5.0
+    finally:
+        idle.close()
+
+
+def test_malformed_frames_do_not_break_the_control_plane(server):
+    """Random and truncated frames (unknown message words, connects with
+    absurd NIC counts, names with huge lengths, handshakes cut short) are
+    dropped; the server keeps answering valid buffer queries."""
+    import random
+
+    rng = random.Random(1234)
+    port = server.get_tcp_port()
+    frames = [
+        struct.pack("<I", 0xDEADBEEF),                       # unknown message
+        struct.pack("<I", 0x7FFFFFFF),                       # NIC count far beyond the limit
+        struct.pack("<I", 2),                                # connect, then hang up
+        struct.pack("<I", 2) + struct.pack("<i", 0) * 2 + struct.pack("<I", 0xFFFFFFF0),  # name length 4 GiB
+        struct.pack("<I", 0x4D505143) + b"\x01" * 7,         # QoS hello cut short
+        struct.pack("<I", 0x4D505143) + struct.pack("<I", 99) + b"x" * 128,  # QoS hello, bad version
+        b"\x00",                                             # fewer than 4 bytes
+    ]
+    frames += [bytes(rng.getrandbits(8) for _ in range(rng.randrange(1, 200))) for _ in range(40)]
+    for f in frames:
+        with socket.create_connection(("127.0.0.1", port)) as s:
+            s.settimeout(5)
+            try:
+                s.sendall(f)
+                s.shutdown(socket.SHUT_WR)
+                while s.recv(4096):
+                    pass
+            except OSError:
+                pass
+    with socket.create_connection(("127.0.0.1", port)) as s:
+        s.settimeout(10)
+        s.sendall(struct.pack("<I", 0x4D504251))
+        assert struct.unpack("<I", _recv(s, 4))[0] == 0
