@@ -8,7 +8,6 @@ and the "lo" fabric.
 import ctypes
 import os
 import subprocess
-import sys
 import zlib
 
 import pytest

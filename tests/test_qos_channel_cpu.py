@@ -4,7 +4,6 @@ WRITEs into it; GETs are never held; a closed channel lifts the policy
 (fail-open); frames in the reference's byte layout from a raw socket are
 honoured."""
 import ctypes
-import os
 import socket
 import struct
 import time
