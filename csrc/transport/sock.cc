@@ -101,7 +101,7 @@ class SockQp final : public QueuePair {
 
 class SockRail final : public Rail {
  public:
-    SockRail(std::string name, int index) : name_(std::move(name)) {
+    SockRail(std::string name, int index, int dscp) : name_(std::move(name)), tos_((dscp & 63) << 2) {
         int port = 0;
         listen_fd_ = net::listen_tcp(0, 128, &port);
         gid_ = "sock:" + sock_addr() + ":" + std::to_string(port) + ":" + std::to_string(index);
@@ -124,6 +124,25 @@ class SockRail final : public Rail {
             if (t.joinable()) t.join();
     }
     bool ok() const { return listen_fd_ >= 0; }
+    // DSCP marking of this rail's data connections (MPCOMM_ROCE_DSCP, the
+    // same knob the ib fabric puts in the GRH traffic class): IP_TOS, or
+    // IPV6_TCLASS for IPv6 sockets, on both ends.
+    void mark(int fd) const {
+        if (!tos_ || fd < 0) return;
+        sockaddr_storage ss{};
+        socklen_t sl = sizeof(ss);
+        const bool v6 = getsockname(fd, reinterpret_cast<sockaddr *>(&ss), &sl) == 0 && ss.ss_family == AF_INET6;
+        const int level = v6 ? IPPROTO_IPV6 : IPPROTO_IP, opt = v6 ? IPV6_TCLASS : IP_TOS;
+        int tos = tos_, got = -1;
+        socklen_t gl = sizeof(got);
+        if (setsockopt(fd, level, opt, &tos, sizeof(tos)) != 0 || getsockopt(fd, level, opt, &got, &gl) != 0 ||
+            (got & 0xFC) != tos_) {
+            MPCOMM_LOG_WARN("MPComm[sock]: %s: cannot set traffic class 0x%02x on fd %d\n", name_.c_str(), tos_, fd);
+            return;
+        }
+        MPCOMM_LOG_DEBUG("MPComm[sock]: %s: data connection fd %d traffic class 0x%02x (DSCP %d)\n", name_.c_str(),
+                         fd, got & 0xFC, (got & 0xFC) >> 2);
+    }
     const std::string &name() const override { return name_; }
     std::string gid() const override { return gid_; }
     int numa_node() const override { return 0; }
@@ -171,6 +190,7 @@ class SockRail final : public Rail {
                 if (stop_) return;
                 continue;
             }
+            mark(fd);
             std::lock_guard<std::mutex> g(srv_mu_);
             server_fds_.push_back(fd);
             servers_.emplace_back([this, fd] { serve(fd); });
@@ -209,6 +229,7 @@ class SockRail final : public Rail {
     int listen_fd_ = -1;
     std::atomic<bool> stop_{false};
     std::thread accept_thread_;
+    int tos_ = 0;
     std::mutex srv_mu_;
     std::vector<int> server_fds_;
     std::vector<std::thread> servers_;
@@ -253,6 +274,7 @@ int SockQp::to_rtr(const EndpointInfo &remote) {
     int port = std::atoi(remote.gid.substr(a + 1, b - a - 1).c_str());
     int fd = net::connect_tcp(ip, port, 0);
     if (fd < 0) return MPCOMM_ERR_CONNECTION;
+    rail_->mark(fd);
     Hello h{kHelloMagic, remote.qp_num, qpn_};
     if (!net::send_pod(fd, h)) {
         ::close(fd);
@@ -348,7 +370,7 @@ class SockBackend final : public Backend {
                 for (auto &f : filter) ok |= (f == nm);
                 if (!ok) continue;
             }
-            auto r = std::make_unique<SockRail>(nm, i);
+            auto r = std::make_unique<SockRail>(nm, i, cfg.roce_dscp);
             if (r->ok()) rails->push_back(std::move(r));
         }
         return rails->empty() ? MPCOMM_ERR_DEVICE : MPCOMM_SUCCESS;

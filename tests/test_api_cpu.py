@@ -8,6 +8,7 @@ and the "lo" fabric.
 import ctypes
 import os
 import subprocess
+import sys
 import zlib
 
 import pytest
@@ -337,3 +338,30 @@ def test_type_stub_covers_the_native_module():
     funcs = {n for n in dir(mpcomm._mpcomm) if not n.startswith("_") and callable(getattr(mpcomm._mpcomm, n))
              and n not in ("MPComm", "MPCommError")}
     assert funcs <= stub_funcs, sorted(funcs - stub_funcs)
+
+
+def test_sock_fabric_marks_data_connections_with_dscp():
+    """MPCOMM_ROCE_DSCP marks the sock fabric's TCP data connections (both
+    ends) with that DSCP, as it sets the traffic class of RDMA QPs."""
+    code = r"""
+import ctypes, os, mpcomm
+n = 1 << 16
+a, b = mpcomm.MPComm(), mpcomm.MPComm()
+assert a.init("A") == 0 and b.init("B") == 0 and b.start_accept_thread() == 0
+t = ctypes.create_string_buffer(n); s = ctypes.create_string_buffer(os.urandom(n), n)
+assert b.register_memory(ctypes.addressof(t), n) == 0 and b.publish_buffer(ctypes.addressof(t), n) == 0
+assert a.register_memory(ctypes.addressof(s), n) == 0
+port = b.get_tcp_port()
+assert a.connect("B", "127.0.0.1", port) == 0 and a.query_remote_buffers("B", "127.0.0.1", port)
+h = a.put_async(ctypes.addressof(s), "B", ctypes.addressof(t), n)
+assert a.wait_transfer(h, 10000) == 0 and t.raw == s.raw
+a.release_transfer(h); a.shutdown(); b.shutdown()
+print("dscp case ok")
+"""
+    env = dict(os.environ, MPCOMM_FABRIC="sock", MPCOMM_ROCE_DSCP="46", MPCOMM_LOG_LEVEL="3", PYTHONPATH=ROOT)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env,
+                       timeout=120)
+    assert r.returncode == 0 and "dscp case ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+    marked = r.stdout.count("traffic class 0xb8 (DSCP 46)")
+    assert marked >= 2, r.stdout[-3000:]  # initiator and target ends
+    assert "cannot set traffic class" not in r.stderr
