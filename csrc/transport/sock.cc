@@ -203,7 +203,7 @@ class SockRail final : public Rail {
             ::close(fd);
             return;
         }
-        std::vector<char> sink;
+        std::vector<char> sink;  // discard buffer of rejected writes
         for (;;) {
             ReqHdr r;
             if (!net::recv_pod(fd, &r) || r.magic != kReqMagic) break;
@@ -213,8 +213,17 @@ class SockRail final : public Rail {
                 if (ok) {
                     if (!net::recv_all(fd, reinterpret_cast<void *>(r.raddr), r.length)) break;
                 } else {
-                    sink.resize(r.length);
-                    if (r.length && !net::recv_all(fd, sink.data(), r.length)) break;
+                    // Rejected write: drain its payload in bounded pieces (the
+                    // length comes from the peer; never size a buffer by it).
+                    sink.resize(64 * 1024);
+                    uint64_t left = r.length;
+                    bool io = true;
+                    while (left && io) {
+                        const size_t k = left < sink.size() ? static_cast<size_t>(left) : sink.size();
+                        io = net::recv_all(fd, sink.data(), k);
+                        left -= k;
+                    }
+                    if (!io) break;
                 }
                 if (!net::send_pod(fd, st)) break;
             } else {

@@ -365,3 +365,48 @@ print("dscp case ok")
     marked = r.stdout.count("traffic class 0xb8 (DSCP 46)")
     assert marked >= 2, r.stdout[-3000:]  # initiator and target ends
     assert "cannot set traffic class" not in r.stderr
+
+
+def test_sock_fabric_rejected_write_is_drained_without_allocating_its_length():
+    """A write that fails the sock fabric's rkey check is answered with a
+    remote-access error and its payload drained in bounded pieces: a peer
+    announcing a 3 GiB payload cannot make the target allocate 3 GiB, and
+    the connection keeps serving requests."""
+    import socket
+    import struct
+
+    code = r"""
+import os, socket, struct, mpcomm
+def rss():
+    for line in open("/proc/self/status"):
+        if line.startswith("VmRSS:"):
+            return int(line.split()[1]) * 1024
+b = mpcomm.MPComm()
+assert b.init("B") == 0
+gid = b.get_gid(0)                       # sock:<ip>:<port>:<n>
+_, ip, port, _ = gid.split(":")
+s = socket.create_connection((ip, int(port)))
+s.sendall(struct.pack("<III", 0x4D505348, 0, 0))          # hello
+def req(op, rkey, length, addr=0):
+    return struct.pack("<IIIIQ", 0x4D505352, op, rkey, length, addr)
+def status():
+    b_ = b""
+    while len(b_) < 4:
+        c = s.recv(4 - len(b_)); assert c; b_ += c
+    return struct.unpack("<i", b_)[0]
+s.sendall(req(0, 0xBAD, 1 << 20) + os.urandom(1 << 20))   # rejected 1 MiB write
+assert status() != 0
+s.sendall(req(1, 0xBAD, 4096))                           # rejected read: status only
+assert status() != 0
+before = rss()
+s.sendall(req(0, 0xBAD, 3 << 30) + b"x" * 4096)          # 3 GiB announced, 4 KiB sent
+import time; time.sleep(0.5)
+grown = rss() - before
+s.close()
+b.shutdown()
+assert grown < (256 << 20), grown
+print("drain ok", grown)
+"""
+    env = dict(os.environ, MPCOMM_FABRIC="sock", MPCOMM_LOG_LEVEL="1", PYTHONPATH=ROOT)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
+    assert r.returncode == 0 and "drain ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
