@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <mutex>
 
+#include "cuda/gpu.h"
 #include "kernels/common.cuh"
 #include "kernels/crc32_noalloc.h"
 
@@ -71,7 +72,10 @@ __global__ void __launch_bounds__(kThreads)
     }
     __syncthreads();
 
-    const int64_t block = blockIdx.y, piece = blockIdx.x;
+    // One CTA per (block, piece), flattened onto x: a grid's y extent stops
+    // at 65535, below the 65536 pieces the scratch holds.
+    const int64_t block = static_cast<int64_t>(blockIdx.x) / ppb;
+    const int64_t piece = static_cast<int64_t>(blockIdx.x) - block * ppb;
     int64_t plen = bs - piece * kPieceBytes;
     if (plen > kPieceBytes) plen = kPieceBytes;
     const unsigned char *p = data + block * bs + piece * kPieceBytes + static_cast<int64_t>(tid) * kSegBytes;
@@ -129,17 +133,26 @@ __global__ void noalloc_crc_finalize(const uint32_t *__restrict__ scratch, int64
     out[b] = shift_bytes(0xFFFFFFFFu, static_cast<uint64_t>(bs), pw.x) ^ acc ^ 0xFFFFFFFFu;
 }
 
-// Device address of g_crc_scratch for the current device, looked up once
-// per device. Returns a CUDA error code.
+// Device address of g_crc_scratch in the current device's current context.
+// The lookup is cached per (device, context): a context that is torn down and
+// created again (cudaDeviceReset, primary-context release) may load the
+// module at another address, so a new context gets a new lookup. Returns a
+// CUDA error code.
 int scratch_for_current_device(uint32_t **out) {
+    using CtxGetCurrent = int (*)(void **);
+    static const CtxGetCurrent ctx_get_current =
+        reinterpret_cast<CtxGetCurrent>(mpcomm::gpu::driver_symbol("cuCtxGetCurrent"));
     static std::mutex mu;
     static uint32_t *addr[kMaxDevices] = {nullptr};
+    static void *addr_ctx[kMaxDevices] = {nullptr};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    void *ctx = nullptr;
+    if (!ctx_get_current || ctx_get_current(&ctx) != 0) ctx = nullptr;
     std::lock_guard<std::mutex> g(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || !ctx || addr_ctx[dev] != ctx) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_crc_scratch);
         if (e != cudaSuccess) {
@@ -147,7 +160,10 @@ int scratch_for_current_device(uint32_t **out) {
                          dev, cudaGetErrorString(e));
             return e;
         }
+        // The lookup makes the primary context current if nothing was yet.
+        if (!ctx && ctx_get_current && ctx_get_current(&ctx) != 0) ctx = nullptr;
         addr[dev] = static_cast<uint32_t *>(p);
+        addr_ctx[dev] = ctx;
     }
     *out = addr[dev];
     return cudaSuccess;
@@ -170,12 +186,16 @@ extern "C" int mpcomm_crc32_blocks_noalloc(const void *data, int64_t num_blocks,
                      MPCOMM_CRC32_NOALLOC_MAX_WORDS);
         return -1;
     }
+    // A runtime error left pending by the caller's earlier work is returned
+    // untouched (and not cleared) before anything is queued.
+    cudaError_t pending = cudaPeekAtLastError();
+    if (pending != cudaSuccess) return pending;
     uint32_t *scratch = nullptr;
     int e = scratch_for_current_device(&scratch);
     if (e != cudaSuccess) return e;
     static const Powers pw = powers_table();
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    noalloc_crc_pieces<<<dim3(static_cast<unsigned>(ppb), static_cast<unsigned>(num_blocks)), kThreads, 0, st>>>(
+    noalloc_crc_pieces<<<static_cast<unsigned>(num_blocks * ppb), kThreads, 0, st>>>(
         static_cast<const unsigned char *>(data), block_size, ppb, scratch, pw);
     mpcomm::kern::note_launch();
     cudaError_t le = cudaGetLastError();

@@ -23,7 +23,12 @@
 //
 // Setup: the first call on each device (with that device current) looks up
 // the array's device address with cudaGetSymbolAddress; make that first call
-// before any CUDA stream capture.
+// before any CUDA stream capture. The address is cached per device and
+// context; a call in a context created since (after cudaDeviceReset, say)
+// looks it up again, so that call too belongs outside a capture.
+//
+// Errors: a runtime error already pending when the call starts (left by the
+// caller's earlier work) is returned as is, before anything is queued.
 //
 // Sharing: all calls on a device share the one array and it keeps the last
 // call's contents. Each call writes every scratch word it later reads, in

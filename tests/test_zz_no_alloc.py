@@ -47,6 +47,22 @@ def test_noalloc_matches_allocating_entry_point_twice():
         assert torch.equal(out, ref), (n, bs)
 
 
+def test_noalloc_at_the_scratch_and_block_count_limits():
+    """65,536 blocks of one piece each fill every scratch word (and pass the
+    65,535 a grid's y extent allows); 65,535 blocks of an odd size sit just
+    below. Both equal the allocating entry point."""
+    fn = _entry()
+    for n, bs, seed in [(MAX_WORDS, 4096, 21), (MAX_WORDS - 1, 4097, 22)]:
+        g = torch.Generator(device="cuda").manual_seed(seed)
+        data = torch.randint(0, 256, (n * bs,), dtype=torch.uint8, device="cuda", generator=g)
+        out = torch.zeros(n, dtype=torch.int32, device="cuda")
+        assert _call(fn, data, n, bs, out) == 0
+        ref = ops.crc32_blocks(data, n)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref), (n, bs)
+        del data
+
+
 def test_noalloc_rejects_requests_beyond_scratch():
     fn = _entry()
     data = torch.zeros(16, dtype=torch.uint8, device="cuda")
@@ -56,5 +72,9 @@ def test_noalloc_rejects_requests_beyond_scratch():
     # words; rejected before anything touches memory.
     bs = (MAX_WORDS // 2 + 1) * (512 << 10)
     rc = fn(ctypes.c_void_p(data.data_ptr()), 2, bs, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(stream))
+    assert rc == -1
+    # One block more than the scratch has words (16-byte blocks): rejected.
+    rc = fn(ctypes.c_void_p(data.data_ptr()), MAX_WORDS + 1, 16, ctypes.c_void_p(out.data_ptr()),
+            ctypes.c_void_p(stream))
     assert rc == -1
     torch.cuda.synchronize()
