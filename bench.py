@@ -19,6 +19,19 @@ through the Python API with wall-clock timing, adding per step the H2D copy
 of the step's request table and a D2H read of the GET result's CRC-32s
 (verified against the source CRCs).
 
+At N >= 2 the same run then measures the paths that cross NVLink
+(mpcomm.bench.multigpu): GPU-pair PUT/GET through the engine, the fused PXN
+gather + forward and the fused rollout-batch gather + broadcast, each
+CRC-checked on every rank and reported against its roofline as extra keys.
+The headline is also reported against independent ceilings: the copy
+engine on one link alone (rank 0, others idle) times N, and the host's own
+DRAM write/read bandwidth (CPU threads, no GPU involved).
+
+Reference arm (--impl reference): runs the reference build installed in
+baseline/_ref when there is one; otherwise it configures the reference's
+source tree (baseline/_ref/src_tree) with CMake and reports the error that
+stops it.
+
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 For N>1 launch with torch.distributed.run (one rank per GPU).
 """
@@ -35,9 +48,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "PUT/GET GB/s zero-copy & staging (1 GB, batch=4); gather/PXN GB/s + % roofline"
 BASELINE_GBS = 195.7  # reference README.md:113 (zero-copy PUT/GET, 1 GB, batch=4, 4 NICs)
-REF_UNAVAILABLE = ("reference build fails offline: its CMakeLists.txt:38 requires libibverbs "
-                   "(find_library IBVERBS_LIBRARY) and libnuma, absent here and on the GPU boxes; its "
-                   "init() also requires an RDMA NIC and the boxes expose none")
+BASELINE_NOTE = ("different hardware and path: the published 195.7 GB/s is 4 x CX-7 NIC-to-NIC RDMA between two "
+                 "hosts; this value is HBM <-> host DRAM over each GPU's own PCIe Gen5 x16 link (no RDMA NIC on "
+                 "these boxes), so the ratio is context, not parity")
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
 
 def parse():
@@ -49,6 +63,8 @@ def parse():
     p.add_argument("--block-mb", type=int, default=1024)
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the inter-GPU paths and the ceilings measured after the headline")
     p.add_argument("--pool-alloc", choices=["pinned", "hugepage"], default="pinned",
                    help="pinned: cudaHostAlloc via torch; hugepage: anonymous mmap with MADV_HUGEPAGE, "
                         "pinned by MPComm.register_memory (fewer IOMMU translations per byte)")
@@ -100,12 +116,40 @@ def bind_numa_local(dev: int):
     return -1
 
 
+def reference_unavailable_reason() -> str:
+    """Why the reference cannot run here, found by trying: its installed
+    package (pip --target baseline/_ref) and the init() it needs, else a CMake
+    configure of its source tree."""
+    import subprocess
+    import tempfile
+
+    pkg = os.path.join(REF_DIR, "mpcomm")
+    if os.path.isdir(pkg):
+        code = ("import sys; sys.path.insert(0, %r); import mpcomm; c = mpcomm.MPComm(); "
+                "print('init_rc', c.init('ref-bench'))" % REF_DIR)
+        r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+        out = (r.stdout + r.stderr).strip().splitlines()
+        return "installed reference did not initialise: " + " | ".join(out[-3:])
+    src = os.path.join(REF_DIR, "src_tree")
+    if not os.path.isfile(os.path.join(src, "CMakeLists.txt")):
+        return "reference not installed in baseline/_ref and its source tree is absent"
+    with tempfile.TemporaryDirectory(prefix="mpcomm-ref-") as bdir:
+        r = subprocess.run(["cmake", "-S", src, "-B", bdir], capture_output=True, text=True, timeout=300)
+    if r.returncode == 0:
+        return "reference configured but is not installed (pip install into baseline/_ref failed earlier)"
+    lines = [ln.strip() for ln in (r.stdout + r.stderr).splitlines() if ln.strip()]
+    err = [ln for i, ln in enumerate(lines) if "Error" in ln or (i and "Error" in lines[i - 1])]
+    return ("reference build fails offline (CMake configure rc=%d): %s; the boxes have no rdma-core and no "
+            "RDMA NIC, which its init() also requires" % (r.returncode, " ".join(err[:3]) or lines[-1]))
+
+
 def main():
     args = parse()
     rank, world, local = rank_env()
     if args.impl == "reference":
+        # Every rank reaches the same conclusion; rank 0 reports it.
         if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": REF_UNAVAILABLE}), flush=True)
+            print(json.dumps({"impl": "reference", "unavailable": reference_unavailable_reason()}), flush=True)
         return 0
 
     import torch
@@ -131,6 +175,12 @@ def main():
     batch = args.batch
     total = block * batch
 
+    # Host DRAM ceiling, measured by CPU threads alone (rank 0; GPUs idle).
+    host_bw = {}
+    if rank == 0 and not args.no_extras:
+        host_bw = mpcomm._native.host_bandwidth(2 << 30, 0, numa, 3)
+    barrier()
+
     gen = torch.Generator(device=dev)
     gen.manual_seed(2 + rank)
     src = torch.randint(0, 256, (total,), dtype=torch.uint8, device=dev, generator=gen)
@@ -152,13 +202,14 @@ def main():
 
     sp, pp, dp = src.data_ptr(), pool.data_ptr(), dst.data_ptr()
 
-    def run_phase(put: bool):
+    def run_phase(put: bool, s_ptr: int = 0, d_ptr: int = 0):
+        s_ptr, d_ptr = s_ptr or sp, d_ptr or dp
         hs = []
         for i in range(batch):
             if put:
-                h = comm.put_async(sp + i * block, "pool", pp + i * block, block)
+                h = comm.put_async(s_ptr + i * block, "pool", pp + i * block, block)
             else:
-                h = comm.get_async(dp + i * block, "pool", pp + i * block, block)
+                h = comm.get_async(d_ptr + i * block, "pool", pp + i * block, block)
             assert h != mpcomm.INVALID_TRANSFER_HANDLE
             hs.append(h)
         for h in hs:
@@ -261,6 +312,72 @@ def main():
         e2e = {"value": round(world * 2 * total / wall.item() / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": req_host.numel() * 8, "d2h_bytes_per_step": batch * 4}
 
+    # Staging (non-zero-copy) PUT/GET: the same 4 x 1 GiB from and into HBM
+    # that was never registered; the library stages it through slabs in the
+    # same GPU's HBM (device-to-device stage copies, then the zero-copy
+    # engine). Every kernel of it runs on the fabric stream, so CUDA events
+    # there bracket the whole transfer.
+    staging = {}
+    if not args.no_extras:
+        ssrc = src.clone()
+        sdst = torch.zeros_like(dst)
+        torch.cuda.synchronize()
+        st_ms = []
+        for put in (True, False):
+            for _ in range(2):
+                run_phase(put, ssrc.data_ptr(), sdst.data_ptr())
+            torch.cuda.synchronize()
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(fstream)
+            for _ in range(3):
+                run_phase(put, ssrc.data_ptr(), sdst.data_ptr())
+            b.record(fstream)
+            torch.cuda.synchronize()
+            t = torch.tensor([a.elapsed_time(b) / 3], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            st_ms.append(t.item())
+        ok = torch.equal(crc32_blocks(sdst, batch), crc_src)
+        okt = torch.tensor([1 if ok else 0], device=dev)
+        if world > 1:
+            dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+        staging = {"staging_put_gbs": round(world * total / (st_ms[0] * 1e-3) / 1e9, 3),
+                   "staging_get_gbs": round(world * total / (st_ms[1] * 1e-3) / 1e9, 3),
+                   "staging_crc_ok": bool(okt.item()),
+                   "staging_what": "PUT/GET of 4 x 1 GiB from/into unregistered HBM through the staging pool "
+                                   "(HBM slabs, device stage copies, then the zero-copy engine); published "
+                                   "reference bcopy 91.9 / 84.5 GB/s is NIC-to-NIC on other hardware"}
+        del ssrc, sdst
+
+    # Copy engine on one link alone (rank 0; the others wait): the per-link
+    # ceiling, N times which the headline could reach if nothing were shared.
+    solo = [0.0, 0.0]
+    if not args.no_extras:
+        barrier()
+        if rank == 0:
+            for k, d2h in enumerate((True, False)):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(s_ce):
+                    a.record(s_ce)
+                    for _ in range(2):
+                        (pool.copy_(src, non_blocking=True) if d2h else dst.copy_(pool, non_blocking=True))
+                    b.record(s_ce)
+                s_ce.synchronize()
+                solo[k] = 2 * total / (a.elapsed_time(b) * 1e-3) / 1e9
+        barrier()
+
+    # The host pool is not used past this point.
+    comm.unpublish_buffer(pp)
+    comm.unregister_memory(pp)
+    del pool
+    extras = {}
+    if world > 1 and not args.no_extras:
+        from mpcomm.bench import multigpu
+
+        torch.cuda.synchronize()
+        extras = multigpu.run(comm, src, dst, block, batch, fstream)
+
     value = world * 2 * total / (ms * 1e-3) / 1e9
     if rank == 0:
         cs = clocks.summary()
@@ -275,6 +392,7 @@ def main():
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": round(value / BASELINE_GBS, 4),
+            "vs_baseline_note": BASELINE_NOTE,
             "dtype": "uint8",
             "data": "synthetic (uint8 uniform, seed 2+rank, torch generator on device)",
             "config": {
@@ -307,6 +425,23 @@ def main():
         }
         if e2e:
             out["e2e"] = e2e
+        if solo[0] and host_bw:
+            put_gbs, get_gbs = out["put_gbs"], out["get_gbs"]
+            out["ceilings"] = {
+                "what": "N x the copy engine on one link alone (rank 0, others idle), and the host DRAM "
+                        "bandwidth of CPU threads alone (memset / read; no GPU involved)",
+                "solo_ce_d2h_gbs": round(solo[0], 3), "solo_ce_h2d_gbs": round(solo[1], 3),
+                "links_put_gbs": round(world * solo[0], 3), "links_get_gbs": round(world * solo[1], 3),
+                "put_frac_of_links": round(put_gbs / (world * solo[0]), 4),
+                "get_frac_of_links": round(get_gbs / (world * solo[1]), 4),
+                "host_cpu_write_gbs": round(host_bw["write_gbs"], 3),
+                "host_cpu_read_gbs": round(host_bw["read_gbs"], 3),
+                "host_cpu_threads": host_bw["threads"],
+                "put_frac_of_host_cpu_write": round(put_gbs / host_bw["write_gbs"], 4),
+                "get_frac_of_host_cpu_read": round(get_gbs / host_bw["read_gbs"], 4),
+            }
+        out.update(staging)
+        out.update(extras)
         print(json.dumps(out), flush=True)
     comm.shutdown()
     if world > 1:

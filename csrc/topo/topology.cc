@@ -10,6 +10,9 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <thread>
 #include <cstdint>
 #include <cctype>
 #include <cstring>
@@ -209,6 +212,70 @@ bool bind_thread_to_cpus(const std::vector<int> &cpus) {
     }
     if (n == 0) return false;
     return pthread_setaffinity_np(pthread_self(), sizeof(want), &want) == 0;
+}
+
+namespace {
+
+// Sums the words of [p, p + n) (n a multiple of 64); the result only keeps
+// the loads from being dropped.
+uint64_t sum_words(const uint64_t *p, size_t n) {
+    uint64_t a = 0, b = 0, c = 0, d = 0;
+    for (size_t i = 0; i < n; i += 4) {
+        a += p[i];
+        b += p[i + 1];
+        c += p[i + 2];
+        d += p[i + 3];
+    }
+    return a ^ b ^ c ^ d;
+}
+
+}  // namespace
+
+bool host_bandwidth(size_t bytes, int threads, int node, int reps, HostBandwidth *out) {
+    std::vector<int> cpus;
+    cpu_set_t cur;
+    if (sched_getaffinity(0, sizeof(cur), &cur) == 0)
+        for (int c = 0; c < CPU_SETSIZE; ++c)
+            if (CPU_ISSET(c, &cur)) cpus.push_back(c);
+    if (threads <= 0) threads = cpus.empty() ? 1 : static_cast<int>(cpus.size());
+    bytes &= ~static_cast<size_t>(4095);
+    const size_t slice = (bytes / static_cast<size_t>(threads)) & ~static_cast<size_t>(4095);
+    if (slice == 0) return false;
+    char *buf = static_cast<char *>(numa_alloc(slice * static_cast<size_t>(threads), node));
+    if (!buf) return false;
+    std::atomic<uint64_t> sink{0};
+    auto pass = [&](bool write) {
+        std::vector<std::thread> ts;
+        std::atomic<int> ready{0};
+        std::atomic<bool> go{false};
+        for (int t = 0; t < threads; ++t) {
+            ts.emplace_back([&, t] {
+                if (!cpus.empty()) bind_thread_to_cpus({cpus[static_cast<size_t>(t) % cpus.size()]});
+                char *p = buf + static_cast<size_t>(t) * slice;
+                ready.fetch_add(1);
+                while (!go.load(std::memory_order_acquire)) std::this_thread::yield();
+                if (write)
+                    std::memset(p, t & 0xFF, slice);
+                else
+                    sink.fetch_xor(sum_words(reinterpret_cast<const uint64_t *>(p), slice / 8));
+            });
+        }
+        while (ready.load() < threads) std::this_thread::yield();
+        const auto t0 = std::chrono::steady_clock::now();
+        go.store(true, std::memory_order_release);
+        for (auto &th : ts) th.join();
+        const double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        return static_cast<double>(slice) * threads / s / 1e9;
+    };
+    HostBandwidth r;
+    r.threads = threads;
+    for (int i = 0; i < std::max(1, reps); ++i) {
+        r.write_gbs = std::max(r.write_gbs, pass(true));
+        r.read_gbs = std::max(r.read_gbs, pass(false));
+    }
+    numa_free(buf, slice * static_cast<size_t>(threads));
+    *out = r;
+    return true;
 }
 
 }  // namespace topo

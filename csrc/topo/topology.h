@@ -50,6 +50,18 @@ void numa_free(void *p, size_t bytes);
 // Pins the calling thread to `cpus` intersected with its current affinity.
 bool bind_thread_to_cpus(const std::vector<int> &cpus);
 
+// Host DRAM bandwidth seen by the CPUs, independent of any device: `threads`
+// threads (0 = one per CPU of this process's affinity, each pinned to one)
+// stream over disjoint slices of one `bytes` buffer on NUMA node `node`
+// (-1 = no policy). Best of `reps` passes, GB/s (1e9): write = memset,
+// read = 64-bit sums of every word. Returns false when allocation fails.
+struct HostBandwidth {
+    double write_gbs = 0;
+    double read_gbs = 0;
+    int threads = 0;
+};
+bool host_bandwidth(size_t bytes, int threads, int node, int reps, HostBandwidth *out);
+
 }  // namespace topo
 }  // namespace mpcomm
 

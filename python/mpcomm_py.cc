@@ -14,6 +14,7 @@
 #include "kernels/launch.h"
 #include "mpcomm.h"
 #include "parallel/vmm.h"
+#include "topo/topology.h"
 #include "transport/loopback_hooks.h"
 
 namespace py = pybind11;
@@ -581,6 +582,25 @@ PYBIND11_MODULE(_mpcomm, m) {
         return py::make_tuple(e, reinterpret_cast<uintptr_t>(d), pinned);
     });
     m.def("host_unregister", [](uintptr_t ptr) { return gpu::host_unpin(reinterpret_cast<void *>(ptr)); });
+    m.def(
+        "host_bandwidth",
+        [](size_t bytes, int threads, int node, int reps) {
+            topo::HostBandwidth b;
+            bool ok;
+            {
+                py::gil_scoped_release r;
+                ok = topo::host_bandwidth(bytes, threads, node, reps, &b);
+            }
+            py::dict d;
+            if (!ok) return d;
+            d["write_gbs"] = b.write_gbs;
+            d["read_gbs"] = b.read_gbs;
+            d["threads"] = b.threads;
+            return d;
+        },
+        py::arg("bytes"), py::arg("threads") = 0, py::arg("node") = -1, py::arg("reps") = 3,
+        "Host DRAM write (memset) and read bandwidth of `threads` CPU threads over a `bytes` buffer, GB/s; "
+        "no device involved. Empty dict if the buffer cannot be allocated.");
     m.def("enable_peer_access", &gpu::enable_peer_access, py::arg("device"), py::arg("peer"),
           "Lets kernels on `device` access memory of `peer` (0 or a CUDA error).");
     m.def("multicast_supported", &vmm::multicast_supported, py::arg("device"));

@@ -28,3 +28,23 @@ def test_staging_bench_config1_small():
     d = _run("mpcomm.bench.staging", "--blocks", "8", "--block-size", "256K", "--iters", "2")
     assert d["staging"]["crc32_verified"] and d["zero_copy"]["crc32_verified"]
     assert d["staging"]["put_gbs"] > 0 and d["staging"]["get_gbs"] > 0
+
+
+def test_host_bandwidth_probe():
+    """CPU threads alone stream a buffer; both directions report a rate."""
+    import mpcomm
+
+    d = mpcomm._native.host_bandwidth(64 << 20, 2, -1, 1)
+    assert d["threads"] == 2
+    assert d["write_gbs"] > 0 and d["read_gbs"] > 0
+
+
+def test_reference_arm_reports_why_it_cannot_run():
+    """The reference arm tries the reference (installed package, else a CMake
+    configure of its source tree) and prints one `unavailable` line with the
+    reason it found."""
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference"],
+                       capture_output=True, text=True, cwd=ROOT, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    assert d["impl"] == "reference" and d["unavailable"]
