@@ -120,6 +120,7 @@ Config Config::from_env() {
     read_int("MPCOMM_STAGING_SLAB_BYTES", 4096, 1ll << 32, &c.staging_slab_bytes);
     read_int("MPCOMM_STAGING_SLABS", 2, 4096, &c.staging_slabs);
     read_int("MPCOMM_STAGING_THREADS", 1, 256, &c.staging_threads);
+    read_int("MPCOMM_STAGING_DEVICE_SLAB_BYTES", 4096, 1ll << 32, &c.staging_device_slab_bytes);
     if (read_str("MPCOMM_NIC_PAIRING", &c.nic_pairing) && c.nic_pairing != "suffix" &&
         c.nic_pairing != "index") {
         MPCOMM_LOG_WARN("MPComm: unknown MPCOMM_NIC_PAIRING=%s, using suffix\n",

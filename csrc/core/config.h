@@ -60,6 +60,7 @@ struct Config {
     size_t staging_slab_bytes = 4ull << 20;  // MPCOMM_STAGING_SLAB_BYTES
     size_t staging_slabs = 16;               // MPCOMM_STAGING_SLABS
     size_t staging_threads = 4;              // MPCOMM_STAGING_THREADS
+    size_t staging_device_slab_bytes = 32ull << 20;  // MPCOMM_STAGING_DEVICE_SLAB_BYTES
     std::string nic_pairing = "suffix";      // MPCOMM_NIC_PAIRING suffix|index
     bool repost_on_failure = true;           // MPCOMM_REPOST_ON_FAILURE
     std::string config_file;                 // MPCOMM_CONFIG_FILE (version json)

@@ -229,6 +229,7 @@ class MPComm::Impl {
     int h2dMove(bool gather, uintptr_t dram, const int64_t *idx, void *gpu_buf, int n, int bs,
                 int max_sm, int mode, void *stream);
     int setFabricStream(void *stream);
+    void *fabricStream() const { return fabric_stream_; }
 
     // ---- topology / introspection (impl_core.cc) ----
     size_t numNics() const { return rails_.size(); }

@@ -139,6 +139,23 @@ def test_scatter_gather_broadcast(pair):
         assert t.bytes(i * seg, seg) == s.bytes(0, seg)
 
 
+def test_staging_refuses_unmapped_local_range(pair):
+    """An unregistered local range that is neither device memory nor mapped
+    host memory is refused at submit (no handle, nothing touched)."""
+    a, b = pair
+    t = Buf(1 << 20)
+    connect(a, b, t, 1 << 20)
+    libc = ctypes.CDLL(None)
+    libc.mmap.restype = ctypes.c_void_p
+    libc.mmap.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_long]
+    libc.munmap.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+    addr = libc.mmap(None, 1 << 20, 3, 0x22, -1, 0)  # PROT_READ|WRITE, MAP_PRIVATE|ANONYMOUS
+    assert addr and addr != ctypes.c_void_p(-1).value
+    assert libc.munmap(addr, 1 << 20) == 0  # the range is unmapped from here on
+    assert a.put_async(addr, "B", t.ptr, 1 << 20) == mpcomm.INVALID_TRANSFER_HANDLE
+    assert a.get_async(addr, "B", t.ptr, 1 << 20) == mpcomm.INVALID_TRANSFER_HANDLE
+
+
 def test_staging_config1_put_get_crc(pair):
     """Config 1: 64 x 1 MiB host->host PUT then GET through the staging pool."""
     import random
