@@ -128,6 +128,7 @@ Config Config::from_env() {
         c.nic_pairing = "suffix";
     }
     read_flag("MPCOMM_REPOST_ON_FAILURE", &c.repost_on_failure);
+    read_flag("MPCOMM_FUSED_BROADCAST", &c.fused_broadcast);
     read_str("MPCOMM_CONFIG_FILE", &c.config_file);
     return c;
 }

@@ -63,6 +63,7 @@ struct Config {
     size_t staging_device_slab_bytes = 32ull << 20;  // MPCOMM_STAGING_DEVICE_SLAB_BYTES
     std::string nic_pairing = "suffix";      // MPCOMM_NIC_PAIRING suffix|index
     bool repost_on_failure = true;           // MPCOMM_REPOST_ON_FAILURE
+    bool fused_broadcast = true;             // MPCOMM_FUSED_BROADCAST
     std::string config_file;                 // MPCOMM_CONFIG_FILE (version json)
 
     // Reads all variables from the process environment.

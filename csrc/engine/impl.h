@@ -108,6 +108,11 @@ struct Transfer {
     int owner = 0;  // worker id
     size_t outstanding_limit = 2;
     bool composite = false;  // completion driven by the staging engine
+    // Fused broadcast: every chunk is ONE one-to-many WRITE on fanout_rail
+    // (plan = the chunks of one destination; each completion covers all).
+    bool fanout = false;
+    size_t fanout_rail = 0;
+    bool host_source = false;  // local buffer in host memory (H2D QoS window)
 
     // Worker-owned progress.
     size_t next_chunk = 0;
@@ -146,6 +151,7 @@ class MPComm::Impl {
     int init(const std::string &host_id, const std::string &device_names, int tcp_port);
     void shutdown();
     int registerMemory(void *addr, size_t len);
+    int registerMulticastMemory(void *uc, size_t len, void *mc, uint64_t token, int members);
     int unregisterMemory(void *addr);
     uint32_t getRkey(size_t nic, void *addr) const;
     bool lookupRegion(uintptr_t addr, size_t len, Region *out) const;
@@ -276,6 +282,7 @@ class MPComm::Impl {
     void workerLoop(Worker *w);
     void wakeWorker(Worker *w);
     void postChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched);
+    void postFanoutChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched);
     void handleCompletion(Worker *w, const fabric::WorkCompletion &wc);
     void retire(Worker *w);
     void probeQuarantine();

@@ -235,6 +235,26 @@ int MPComm::Impl::registerMemory(void *addr, size_t len) {
     return MPCOMM_SUCCESS;
 }
 
+int MPComm::Impl::registerMulticastMemory(void *uc, size_t len, void *mc, uint64_t token, int members) {
+    if (!uc || !mc || !len || !token || members < 2) return MPCOMM_ERR_INVALID_ARG;
+    int e = registerMemory(uc, len);
+    if (e != MPCOMM_SUCCESS) return e;
+    Region r;
+    if (!lookupRegion(reinterpret_cast<uintptr_t>(uc), len, &r)) return MPCOMM_ERR_MEMORY;
+    int ok = 0;
+    for (size_t i = 0; i < rails_.size() && i < r.keys.size(); ++i)
+        if (rails_[i]->rail->set_multicast(r.keys[i], reinterpret_cast<uintptr_t>(uc), len,
+                                           reinterpret_cast<uintptr_t>(mc), token, members) == 0)
+            ++ok;
+    if (!ok) {
+        MPCOMM_LOG_ERROR("MPComm: fabric '%s' cannot use multicast memory %p\n", fabric_name_.c_str(), uc);
+        return MPCOMM_ERR_INVALID_ARG;
+    }
+    MPCOMM_LOG_DEBUG("MPComm: %p+%zu registered as a copy of multicast group %llx (%d GPUs)\n", uc, len,
+                     static_cast<unsigned long long>(token), members);
+    return MPCOMM_SUCCESS;
+}
+
 int MPComm::Impl::unregisterMemory(void *addr) {
     if (!initialized_) return MPCOMM_ERR_CONTEXT;
     std::unique_lock<std::shared_mutex> g(regions_mu_);

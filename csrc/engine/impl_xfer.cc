@@ -127,8 +127,33 @@ TransferHandle MPComm::Impl::submit(uintptr_t local, const std::vector<std::stri
         if (!rails_[r]->quarantined.load(std::memory_order_relaxed)) healthy.push_back(r);
     if (!healthy.empty()) cand.swap(healthy);
     t->candidates = cand;
-    const size_t chunk = effectiveChunk(cand);
-    t->plan.build(local, raddrs, lens, chunk, dir == Direction::kBroadcast);
+    size_t chunk = effectiveChunk(cand);
+    // Fused broadcast: when one candidate rail reaches every destination and
+    // can write them all in one device operation (GPU fabric: a gather_bcast
+    // launch per chunk that reads each source tile once; NVLS multicast
+    // stores when the destinations form one multicast group), each chunk is
+    // posted once as a one-to-many WRITE instead of once per destination
+    // (the reference posts one RDMA WRITE per host, src/mpcomm.cpp:4937-4954).
+    if (dir == Direction::kBroadcast && cfg_.fused_broadcast) {
+        for (size_t r : cand) {
+            fabric::Rail *rl = rails_[r]->rail.get();
+            const size_t al = std::max<size_t>(1, rl->fanout_alignment());
+            if (hosts.size() > rl->max_fanout() || chunk < al) continue;
+            bool ok = local % al == 0 && lens[0] % al == 0;
+            for (size_t i = 0; ok && i < hosts.size(); ++i)
+                ok = lens[i] == lens[0] && raddrs[i] % al == 0 && t->conns[i]->group_for(r) != nullptr;
+            if (!ok) continue;
+            t->fanout = true;
+            t->fanout_rail = r;
+            t->host_source = region.gpu < 0;
+            chunk -= chunk % al;
+            break;
+        }
+    }
+    if (t->fanout)
+        t->plan.build(local, {raddrs[0]}, {lens[0]}, chunk, true);
+    else
+        t->plan.build(local, raddrs, lens, chunk, dir == Direction::kBroadcast);
     size_t ol = throttle_outstanding_.load(std::memory_order_relaxed);
     if (ol == 0) ol = rails_[cand[0]]->rail->preferred_outstanding(cfg_);
     t->outstanding_limit = std::max<size_t>(1, ol);
@@ -312,8 +337,124 @@ void MPComm::Impl::workerLoop(Worker *w) {
     w->active.clear();
 }
 
+void MPComm::Impl::postFanoutChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched) {
+    const size_t total = t->plan.total();
+    const size_t r = t->fanout_rail;
+    const size_t nh = t->hosts.size();
+    std::vector<fabric::FanoutTarget> targets(nh);
+    while (true) {
+        size_t chunk;
+        bool from_retry = false;
+        if (!t->retry.empty()) {
+            chunk = t->retry.front();
+            from_retry = true;
+        } else if (t->next_chunk < total) {
+            chunk = t->next_chunk;
+        } else {
+            break;
+        }
+        if (rails_[r]->quarantined.load(std::memory_order_relaxed)) {
+            // A fused WRITE has no other rail that reaches every destination.
+            t->error.store(MPCOMM_ERR_TRANSFER);
+            t->aborted = true;
+            break;
+        }
+        const Chunk c = t->plan.get(chunk);
+        QpGroup *g0 = t->conns[0]->group_for(r);
+        if (!g0 || g0->qps.empty()) {
+            t->error.store(MPCOMM_ERR_CONNECTION);
+            t->aborted = true;
+            break;
+        }
+        const size_t rail_out = w->rail_posted[r] - w->rail_completed[r];
+        if (rail_out >= t->outstanding_limit * std::min(cfg_.qps_per_connection, g0->qps.size())) break;
+        size_t q = SIZE_MAX, q_out = SIZE_MAX;
+        const size_t nq = std::min(g0->qps.size(), kMaxQpsPerRail);
+        for (size_t i = 0; i < nq; ++i) {
+            const size_t out = w->qp_posted[r][i] - w->qp_completed[r][i];
+            if (out < t->outstanding_limit && out < q_out) {
+                q = i;
+                q_out = out;
+            }
+        }
+        if (q == SIZE_MAX) break;
+        const size_t off = c.remote_addr - t->remote_addrs[0];
+        bool deferred = false, missing = false;
+        for (size_t i = 0; i < nh; ++i) {
+            QpGroup *g = t->conns[i]->group_for(r);
+            const uintptr_t ra = t->remote_addrs[i] + off;
+            if (!g || g->qps.empty()) {
+                missing = true;
+                break;
+            }
+            if (!qosAllowRemoteWrite(*t->conns[i], ra, c.length)) {
+                deferred = true;
+                break;
+            }
+            targets[i].qp = g->qps[std::min(q, g->qps.size() - 1)].get();
+            targets[i].remote_addr = ra;
+            targets[i].rkey = t->conns[i]->rkey_for(ra, g->remote_rail);
+            if (targets[i].rkey == 0) missing = true;
+        }
+        if (deferred) break;
+        if (missing) {
+            MPCOMM_LOG_ERROR("MPComm: fused broadcast: no connection or rkey for a destination (query the peers' "
+                             "buffers first)\n");
+            t->error.store(MPCOMM_ERR_MEMORY);
+            t->aborted = true;
+            break;
+        }
+        if (!t->lkey_ok[r]) {
+            Region reg;
+            if (!lookupRegion(c.local_addr, c.length, &reg) || r >= reg.keys.size()) {
+                t->error.store(MPCOMM_ERR_MEMORY);
+                t->aborted = true;
+                break;
+            }
+            t->lkeys[r] = reg.keys[r];
+            t->lkey_ok[r] = true;
+        }
+        fabric::WorkRequest wr;
+        wr.wr_id = WrId::encode(r, q, t->handle, chunk);
+        wr.op = fabric::Opcode::kWrite;
+        wr.local_addr = c.local_addr;
+        wr.lkey = t->lkeys[r].lkey;
+        wr.remote_addr = 0;
+        wr.rkey = 0;
+        wr.length = static_cast<uint32_t>(c.length);
+        // A host-memory source is an H2D read on the rail's GPU: it gets a QoS
+        // window like tmaGather, so READ posts on that GPU's rails yield.
+        kern::H2DWindow *win = nullptr;
+        uint32_t *wctr = nullptr;
+        if (t->host_source) acquireH2DWindow(rails_[r]->gpu, &win, &wctr);
+        fabric::QueuePair *qp = g0->qps[q].get();
+        if (qp->post_fanout(wr, targets.data(), nh, win) != 0) {
+            if (win) __atomic_store_n(&win->armed, 0u, __ATOMIC_RELEASE);
+            MPCOMM_LOG_ERROR("MPComm: fused broadcast post failed on %s\n", rails_[r]->name.c_str());
+            t->error.store(MPCOMM_ERR_TRANSFER);
+            t->aborted = true;
+            break;
+        }
+        ++w->rail_posted[r];
+        ++w->qp_posted[r][q];
+        ++t->in_flight;
+        if (from_retry) t->retry.pop_front();
+        else ++t->next_chunk;
+        if (std::find(touched->begin(), touched->end(), qp) == touched->end()) touched->push_back(qp);
+        if (!t->first_posted) {
+            t->first_posted = true;
+            t->t_first_post = Clock::now();
+        }
+        if (t->next_chunk == total && t->retry.empty()) t->t_all_posted = Clock::now();
+    }
+}
+
 void MPComm::Impl::postChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched) {
     if (t->finished.load(std::memory_order_relaxed) || t->aborted) return;
+    if (t->fanout) {
+        postFanoutChunks(w, t, touched);
+        return;
+    }
     const size_t total = t->plan.total();
     const size_t qps_cap = cfg_.qps_per_connection;
     while (true) {
@@ -458,13 +599,15 @@ void MPComm::Impl::handleCompletion(Worker *w, const fabric::WorkCompletion &wc)
     const int dom = t->op == fabric::Opcode::kRead
                         ? t->local_gpu
                         : (t->remote_gpu.empty() ? -1 : t->remote_gpu[c.host_idx]);
-    if (cfg_.pcie_stat_enable) pcieOnCompleted(dom, c.length);
+    if (cfg_.pcie_stat_enable && !t->fanout) pcieOnCompleted(dom, c.length);
     if (wc.status == fabric::kWcSuccess || cfg_.fault_tolerate) {
-        t->bytes.fetch_add(c.length, std::memory_order_relaxed);
-        t->rail_bytes[rail].fetch_add(c.length, std::memory_order_relaxed);
+        // A fused broadcast chunk wrote its bytes to every destination.
+        const uint64_t moved = t->fanout ? c.length * t->hosts.size() : c.length;
+        t->bytes.fetch_add(moved, std::memory_order_relaxed);
+        t->rail_bytes[rail].fetch_add(moved, std::memory_order_relaxed);
         t->done_chunks.fetch_add(1, std::memory_order_relaxed);
-        nic_completed_bytes_.fetch_add(c.length, std::memory_order_relaxed);
-        rails_[rail]->completed_bytes.fetch_add(c.length, std::memory_order_relaxed);
+        nic_completed_bytes_.fetch_add(moved, std::memory_order_relaxed);
+        rails_[rail]->completed_bytes.fetch_add(moved, std::memory_order_relaxed);
         return;
     }
     MPCOMM_LOG_WARN("MPComm: WC error %d on %s (handle %lu chunk %zu)\n", wc.status,

@@ -41,7 +41,7 @@ constexpr int kGbStages = 3;
 constexpr uint32_t kGbStageBytes = 16384;
 constexpr size_t kGbSmem = static_cast<size_t>(kGbWarps) * kGbStages * kGbStageBytes +
                            static_cast<size_t>(kGbWarps) * kGbStages * sizeof(uint64_t);
-constexpr int kGbMaxDst = 8;
+constexpr int kGbMaxDst = kMaxFanoutDsts;
 
 struct GatherBcastArgs {
     const char *pool;
@@ -56,6 +56,7 @@ struct GatherBcastArgs {
     uint64_t flag_value;
     uint32_t *ctr;             // last-CTA counter (zero, self-resetting)
     KernelStamp *stamp;
+    H2DWindow *win;            // H2D QoS window of a host-memory source (may be null)
 };
 
 // Lane-held description of one tile: source address, byte offset of the tile
@@ -72,7 +73,7 @@ __device__ __forceinline__ GbTile gb_tile(const GatherBcastArgs &a, int64_t t) {
     const int64_t off = (t - b * a.tpb) * static_cast<int64_t>(kGbStageBytes);
     const int64_t rem = a.bs - off;
     const uint32_t len = static_cast<uint32_t>(rem < kGbStageBytes ? rem : kGbStageBytes);
-    const int64_t p = __ldg(a.idx + b);
+    const int64_t p = a.idx ? __ldg(a.idx + b) : b;  // no index list: page i is pool page i
     if (p < 0 || (a.pool_blocks > 0 && p >= a.pool_blocks)) return GbTile{nullptr, 0, len, kBad};
     return GbTile{a.pool + p * a.bs + off, b * a.bs + off, len, kBulk};
 }
@@ -239,6 +240,7 @@ __global__ void __launch_bounds__(kGbWarps * 32, 1)
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw + static_cast<size_t>(kGbWarps) * kGbStages * kGbStageBytes) +
                      warp * kGbStages;
     trace_begin(a.stamp);
+    window_open(a.win);
     warp_gather_bcast<kMc>(a, static_cast<int64_t>(blockIdx.x) * kGbWarps + warp,
                            static_cast<int64_t>(gridDim.x) * kGbWarps, stage_mem, bars, status, budget);
     // Every lane's multimem stores (or lane 0's completed bulk stores) are
@@ -253,10 +255,12 @@ __global__ void __launch_bounds__(kGbWarps * 32, 1)
         if (prev == gridDim.x - 1) {
             *a.ctr = 0u;
             __threadfence_system();
-            if (kMc) {
-                if (a.mc_flag) multimem_red_release_add_u64(a.mc_flag, 1ull);
-            } else {
-                for (int k = 0; k < a.nflag; ++k) st_release_sys_u64(a.flag[k], a.flag_value);
+            if (kMc && a.mc_flag) multimem_red_release_add_u64(a.mc_flag, 1ull);
+            for (int k = 0; k < a.nflag; ++k) st_release_sys_u64(a.flag[k], a.flag_value);
+            if (a.win) {
+                uint32_t *gate = *reinterpret_cast<uint32_t *volatile *>(&a.win->gate);
+                if (gate) atomicSub(gate, 1u);
+                st_release_sys_u64(&a.win->end_ns, globaltimer_ns() | 1ull);
             }
         }
     }
@@ -282,8 +286,9 @@ bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int gather_bcast(const void *pool, int64_t pool_blocks, const int64_t *idx, int64_t n, int64_t bs, void *mc_dst,
                  void *const *dsts, int ndst, uint64_t *mc_flag, uint64_t *const *flags, int nflag,
                  uint64_t flag_value, uint32_t *ctr, int max_ctas, void *stream, uint32_t *status,
-                 LaunchInfo *info) {
-    if (!pool || !idx || n <= 0 || bs <= 0) return cudaErrorInvalidValue;
+                 LaunchInfo *info, H2DWindow *window) {
+    if (!pool || n <= 0 || bs <= 0) return cudaErrorInvalidValue;
+    if (window && !ctr) return cudaErrorInvalidValue;
     if (!al16(pool) || (bs & 15)) return cudaErrorMisalignedAddress;  // bulk copies need 16-byte spans
     const bool mc = mc_dst != nullptr;
     if (mc) {
@@ -293,8 +298,8 @@ int gather_bcast(const void *pool, int64_t pool_blocks, const int64_t *idx, int6
         if (!dsts || ndst <= 0 || ndst > kGbMaxDst) return cudaErrorInvalidValue;
         for (int k = 0; k < ndst; ++k)
             if (!dsts[k] || !al16(dsts[k])) return cudaErrorMisalignedAddress;
-        if (nflag < 0 || nflag > kGbMaxDst || (nflag > 0 && (!flags || !ctr))) return cudaErrorInvalidValue;
     }
+    if (nflag < 0 || nflag > kGbMaxDst || (nflag > 0 && (!flags || !ctr))) return cudaErrorInvalidValue;
     int dev = 0;
     cudaGetDevice(&dev);
     cudaError_t e = mc ? configure<true>(dev) : configure<false>(dev);
@@ -311,10 +316,11 @@ int gather_bcast(const void *pool, int64_t pool_blocks, const int64_t *idx, int6
     a.ndst = mc ? 0 : ndst;
     for (int k = 0; k < a.ndst; ++k) a.dst[k] = static_cast<char *>(dsts[k]);
     a.mc_flag = mc ? mc_flag : nullptr;
-    a.nflag = mc ? 0 : nflag;
+    a.nflag = nflag;
     for (int k = 0; k < a.nflag; ++k) a.flag[k] = flags[k];
     a.flag_value = flag_value;
-    a.ctr = (mc ? mc_flag != nullptr : nflag > 0) ? ctr : nullptr;
+    a.ctr = ((mc && mc_flag) || nflag > 0 || window) ? ctr : nullptr;
+    a.win = window;
     const uint64_t bytes = static_cast<uint64_t>(n) * static_cast<uint64_t>(bs);
     a.stamp = trace_acquire(mc ? "gather_bcast_nvls" : "gather_bcast_p2p", bytes);
 

@@ -107,16 +107,22 @@ int p2p_fanout(const void *src, void *const *dsts, int ndst, uint64_t bytes, int
 // stores to `mc_dst` (an NVLS multicast address: every bound GPU receives
 // it) or, when mc_dst is null, by bulk stores to each of the `ndst` (<= 8)
 // device pointers in `dsts` (IPC-mapped peer HBM and/or local HBM).
+// `idx` may be null: page i is then pool page i (a contiguous source).
 // Completion (optional; `ctr` is a zeroed device word, self-resetting,
-// launches sharing it must be stream-ordered): with mc_dst, the last CTA
-// adds 1 to the 64-bit flag at multicast address `mc_flag` (release,
-// system scope), so every bound GPU's copy of the flag counts broadcasts;
-// without, it stores `flag_value` to each of the `nflag` flag pointers.
+// launches sharing it must be stream-ordered): with mc_dst and `mc_flag`,
+// the last CTA adds 1 to the 64-bit flag at multicast address `mc_flag`
+// (release, system scope), so every bound GPU's copy of the flag counts
+// broadcasts; in either mode it then stores `flag_value` (release, system
+// scope) to each of the `nflag` (<= 8) flag pointers, which may be
+// host-mapped words.
+// `window` (optional, needs `ctr`): H2D QoS window of a host-memory pool,
+// opened by the first CTA and closed by the last, as the H2D movers do.
 // Requires 16-byte aligned pool/destinations and bs % 16 == 0.
+constexpr int kMaxFanoutDsts = 8;  // P2P sink destinations per gather_bcast launch
 int gather_bcast(const void *pool, int64_t pool_blocks, const int64_t *idx, int64_t n, int64_t bs, void *mc_dst,
                  void *const *dsts, int ndst, uint64_t *mc_flag, uint64_t *const *flags, int nflag,
                  uint64_t flag_value, uint32_t *ctr, int max_ctas, void *stream, uint32_t *status,
-                 LaunchInfo *info);
+                 LaunchInfo *info, H2DWindow *window = nullptr);
 // Bounded wait on a 64-bit flag written by another GPU or the host: waits
 // until *flag >= value or budget_ns elapses (then sets kStatusFlagTimeout).
 int wait_flag(const uint64_t *flag, uint64_t value, uint64_t budget_ns, void *stream,

@@ -138,5 +138,9 @@ std::vector<MPComm::KernelTraceRecord> MPComm::getKernelTrace() {
     return out;
 }
 std::string MPComm::getFabricName() const { return impl_->fabricName(); }
+int MPComm::registerMulticastMemory(void *uc_addr, size_t length, void *mc_addr, uint64_t group_token,
+                                    int group_size) {
+    return impl_->registerMulticastMemory(uc_addr, length, mc_addr, group_token, group_size);
+}
 
 }  // namespace mpcomm

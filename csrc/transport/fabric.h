@@ -65,6 +65,17 @@ struct EndpointInfo {
 
 enum class QpState { kReset, kInit, kRtr, kRts, kErr };
 
+class QueuePair;
+
+// One destination of a one-to-many WRITE (post_fanout): the QP of that
+// destination's connection (on the same local rail as the posting QP), the
+// remote address and its rkey.
+struct FanoutTarget {
+    QueuePair *qp;
+    uintptr_t remote_addr;
+    uint32_t rkey;
+};
+
 struct MemKey {
     uint32_t lkey = 0;
     uint32_t rkey = 0;
@@ -88,6 +99,17 @@ class QueuePair {
     // Rings the doorbell for everything posted since the last flush. For
     // the nvl backend this is where a kernel launch happens.
     virtual void flush() {}
+    // One-to-many WRITE: wr.length bytes at wr.local_addr (wr.lkey) to every
+    // target, moved by ONE device operation that reads the source once
+    // (wr.remote_addr and wr.rkey are ignored). One completion carries
+    // wr.wr_id, on this QP's rail. Only rails with max_fanout() >= n accept
+    // it; others return MPCOMM_ERR_INVALID_ARG and queue nothing.
+    // `h2d_window` (a kern::H2DWindow, may be null) is the QoS window the
+    // device operation opens and closes when its source is host memory.
+    virtual int post_fanout(const WorkRequest & /*wr*/, const FanoutTarget * /*targets*/, size_t /*n*/,
+                            void * /*h2d_window*/) {
+        return -7;  // MPCOMM_ERR_INVALID_ARG
+    }
 };
 
 class Rail {
@@ -114,6 +136,22 @@ class Rail {
     }
     // Routes kernel launches (nvl) into a caller stream; others ignore it.
     virtual int set_stream(void * /*stream*/) { return 0; }
+    // Largest number of destinations one post_fanout may carry (0 = none).
+    virtual size_t max_fanout() const { return 0; }
+    // Source and destination alignment a one-to-many WRITE needs (bytes).
+    virtual size_t fanout_alignment() const { return 1; }
+    // Marks the registration `key` (covering [uc_addr, uc_addr + len)) as
+    // this process's copy of an NVLS multicast group: `mc_addr` is this
+    // process's mapping of the group's multicast address for offset 0 of
+    // uc_addr, `token` names the group across processes, `members` counts
+    // the GPUs bound to it. A one-to-many WRITE whose destinations are
+    // exactly the group's other members (at one common offset) is then
+    // issued as multicast stores. Unsupported rails return
+    // MPCOMM_ERR_INVALID_ARG.
+    virtual int set_multicast(const MemKey & /*key*/, uintptr_t /*uc_addr*/, size_t /*len*/, uintptr_t /*mc_addr*/,
+                              uint64_t /*token*/, int /*members*/) {
+        return -7;
+    }
     // Device QoS gate for H2D copies (nvl): while *gate != 0 the rail's copy
     // kernels pause before each tile, at most budget_ns per pipeline.
     // Null disables it. Other fabrics ignore it.

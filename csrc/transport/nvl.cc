@@ -36,6 +36,7 @@
 #include <cstring>
 #include <deque>
 #include <map>
+#include <set>
 #include <mutex>
 #include <tuple>
 #include <unordered_map>
@@ -53,7 +54,7 @@ namespace mpcomm {
 namespace fabric {
 namespace {
 
-constexpr uint32_t kDirMagic = 0x4E564C45;  // "NVLE": layout with file-backed host records
+constexpr uint32_t kDirMagic = 0x4E564C4D;  // "NVLM": layout with file-backed host and multicast records
 constexpr size_t kDirSlots = 4096;
 
 struct DirRecord {
@@ -68,6 +69,11 @@ struct DirRecord {
     unsigned char ipc[gpu::kIpcHandleBytes];
     uint64_t file_off;  // host memory: offset of `addr` in the backing file
     char path[160];     // host memory: backing file ("" = private, unreachable)
+    // NVLS group this registration is the owner's copy of (0 = none): `addr`
+    // is the group buffer's offset 0 on the owner's GPU.
+    uint32_t mc_members;
+    uint32_t mc_pad;
+    uint64_t mc_token;
 };
 
 // Backing file of a host range that lies inside one shared file mapping of
@@ -136,6 +142,16 @@ struct Region {
     size_t slot;
     std::string path;   // host memory: shared backing file ("" if private)
     uint64_t file_off;
+    uint64_t mc_token = 0;    // NVLS group of which [addr, addr+len) is this process's copy
+    uintptr_t mc_addr = 0;    // this process's multicast mapping of the group's offset 0
+    int mc_members = 0;
+};
+
+// Multicast identity of a registration, as seen by a process posting to it.
+struct McInfo {
+    uint64_t token = 0;
+    int members = 0;
+    uintptr_t base = 0;  // owner's address of the group buffer's offset 0
 };
 
 // Process-wide registry of nvl registrations + the shared directory.
@@ -223,6 +239,37 @@ class Registry {
         return true;
     }
 
+    int set_multicast(uint32_t key, uintptr_t uc, size_t len, uintptr_t mc, uint64_t token, int members) {
+        std::lock_guard<std::mutex> g(mu_);
+        auto it = regions_.find(key);
+        if (it == regions_.end() || !it->second.device || it->second.addr != uc || len > it->second.len ||
+            !mc || !token || members < 2)
+            return MPCOMM_ERR_INVALID_ARG;
+        Region &r = it->second;
+        r.mc_token = token;
+        r.mc_addr = mc;
+        r.mc_members = members;
+        if (dir_ && r.slot < kDirSlots) {
+            // Members before the token: a reader that sees the token sees a
+            // member count too (or none, and then does not use multicast).
+            DirRecord *rec = records() + r.slot;
+            __atomic_store_n(&rec->mc_members, static_cast<uint32_t>(members), __ATOMIC_RELEASE);
+            __atomic_store_n(&rec->mc_token, token, __ATOMIC_RELEASE);
+        }
+        return 0;
+    }
+
+    // This process's registration of NVLS group `token` (false if none).
+    bool find_multicast(uint64_t token, Region *out) {
+        std::lock_guard<std::mutex> g(mu_);
+        for (auto &kv : regions_)
+            if (kv.second.mc_token == token) {
+                *out = kv.second;
+                return true;
+            }
+        return false;
+    }
+
     ~Registry() {
         if (dir_) {
             munmap(dir_, dir_bytes());
@@ -273,6 +320,9 @@ class Registry {
             recs[i].file_off = r.file_off;
             std::memset(recs[i].path, 0, sizeof(recs[i].path));
             if (r.path.size() < sizeof(recs[i].path)) std::memcpy(recs[i].path, r.path.data(), r.path.size());
+            recs[i].mc_members = 0;
+            recs[i].mc_pad = 0;
+            recs[i].mc_token = 0;
             __atomic_store_n(&recs[i].state, 1u, __ATOMIC_RELEASE);
             return i;
         }
@@ -299,9 +349,47 @@ class RemoteMaps {
     // success. Sets *host when the memory is host DRAM (a PCIe-bound copy).
     // IPC mappings belong to the context current when they are opened, so
     // they are opened with `dev` current and cached per (pid, base, dev).
-    int resolve(long pid, uint32_t key, uintptr_t addr, size_t len, int dev, uintptr_t *out, bool *host) {
+    int resolve(long pid, uint32_t key, uintptr_t addr, size_t len, int dev, uintptr_t *out, bool *host,
+                McInfo *mc = nullptr) {
         *host = false;
         std::lock_guard<std::mutex> g(mu_);
+        DirRecord rec;
+        const int found = find_record(pid, key, addr, len, &rec);
+        if (found != 0) return found;
+        if (mc) {
+            mc->token = rec.mc_token;
+            mc->members = static_cast<int>(rec.mc_members);
+            mc->base = rec.addr;
+        }
+        const int prev = gpu::current_device();
+        if (prev != dev) gpu::set_device(dev);
+        int st;
+        if (rec.kind != 0) {
+            *host = true;
+            st = resolve_host(pid, rec, addr, out);
+        } else {
+            st = resolve_device(pid, rec, addr, dev, out);
+        }
+        if (prev >= 0 && prev != dev) gpu::set_device(prev);
+        return st;
+    }
+    // Multicast identity of process `pid`'s registration `key`, after the
+    // same range check as resolve(), without mapping anything.
+    int describe(long pid, uint32_t key, uintptr_t addr, size_t len, McInfo *mc) {
+        std::lock_guard<std::mutex> g(mu_);
+        DirRecord rec;
+        const int found = find_record(pid, key, addr, len, &rec);
+        if (found != 0) return found;
+        mc->token = rec.mc_token;
+        mc->members = static_cast<int>(rec.mc_members);
+        mc->base = rec.addr;
+        return 0;
+    }
+
+ private:
+    // Copy of the live record `key` of `pid` covering [addr, addr+len).
+    // Caller holds mu_.
+    int find_record(long pid, uint32_t key, uintptr_t addr, size_t len, DirRecord *out) {
         const DirRecord *dir = open_dir(pid);
         if (!dir) return kWcRemAccessErr;
         for (size_t i = 0; i < kDirSlots; ++i) {
@@ -315,21 +403,12 @@ class RemoteMaps {
                 __atomic_load_n(&dir[i].key, __ATOMIC_RELAXED) != key || rec.key != key)
                 continue;
             if (addr < rec.addr || addr + len > rec.addr + rec.len) return kWcRemAccessErr;
-            const int prev = gpu::current_device();
-            if (prev != dev) gpu::set_device(dev);
-            int st;
-            if (rec.kind != 0) {
-                *host = true;
-                st = resolve_host(pid, rec, addr, out);
-            } else {
-                st = resolve_device(pid, rec, addr, dev, out);
-            }
-            if (prev >= 0 && prev != dev) gpu::set_device(prev);
-            return st;
+            *out = rec;
+            return 0;
         }
         return kWcRemAccessErr;
     }
- private:
+
     const DirRecord *open_dir(long pid) {
         auto it = dirs_.find(pid);
         if (it != dirs_.end()) return it->second;
@@ -466,6 +545,7 @@ class NvlQp final : public QueuePair {
         return to_rts();
     }
     int post(const WorkRequest *wrs, size_t n) override;
+    int post_fanout(const WorkRequest &wr, const FanoutTarget *targets, size_t n, void *h2d_window) override;
     void flush() override;
     // Retires completed launches into the rail CQ. Caller holds rail mutex.
     void reap(std::deque<WorkCompletion> *cq);
@@ -488,6 +568,21 @@ class NvlQp final : public QueuePair {
     std::vector<uint32_t> pending_lens_;
     bool pending_host_ = false;
     bool pending_h2d_ = false;  // a READ from host memory into this GPU's HBM
+    // One-to-many WRITEs queued since the last flush: one launch each.
+    struct PendingFanout {
+        const void *src;
+        std::vector<void *> dsts;  // P2P sink (empty with a multicast sink)
+        void *mc;                  // multicast address of the common offset (NVLS sink)
+        uint32_t bytes;
+        uint64_t wr_id;
+        kern::H2DWindow *win;      // QoS window of a host-memory source (may be null)
+    };
+    std::vector<PendingFanout> pending_fanout_;
+    // Resolves a remote range of this QP's peer to a device pointer on this
+    // rail's GPU (kWcSuccess or a WC error status); fills *mc if non-null.
+    int resolve_remote(uint32_t rkey, uintptr_t raddr, size_t len, uintptr_t *out, bool *host, McInfo *mc);
+    // Multicast identity of a remote range of this QP's peer (no mapping).
+    int describe_remote(uint32_t rkey, uintptr_t raddr, size_t len, McInfo *mc);
     std::deque<Inflight> inflight_;
 };
 
@@ -549,6 +644,12 @@ class NvlRail final : public Rail {
     }
     size_t preferred_outstanding(const Config &cfg) const override {
         return cfg.max_outstanding_set ? cfg.max_outstanding_per_qp : cfg.nvl_outstanding_per_qp;
+    }
+    size_t max_fanout() const override { return kern::kMaxFanoutDsts; }
+    size_t fanout_alignment() const override { return 16; }
+    int set_multicast(const MemKey &key, uintptr_t uc, size_t len, uintptr_t mc, uint64_t token,
+                      int members) override {
+        return Registry::get().set_multicast(key.lkey, uc, len, mc, token, members);
     }
     int set_stream(void *stream) override {
         // A stream belongs to one device: only that device's rail adopts it.
@@ -695,23 +796,10 @@ int NvlQp::post(const WorkRequest *wrs, size_t n) {
         }
         uintptr_t rptr = 0;
         bool remote_host = false;
-        if (remote_pid_ == getpid()) {
-            Region rr;
-            if (!Registry::get().lookup(wr.rkey, &rr) || wr.remote_addr < rr.addr ||
-                wr.remote_addr + wr.length > rr.addr + rr.len) {
-                rail_->cq_.push_back(WorkCompletion{wr.wr_id, kWcRemAccessErr, 0});
-                continue;
-            }
-            if (rr.device && rr.dev != rail_->dev_) gpu::enable_peer_access(rail_->dev_, rr.dev);
-            rptr = wr.remote_addr;
-            remote_host = !rr.device;
-        } else {
-            int st = RemoteMaps::get().resolve(remote_pid_, wr.rkey, wr.remote_addr, wr.length, rail_->dev_, &rptr,
-                                               &remote_host);
-            if (st != 0) {
-                rail_->cq_.push_back(WorkCompletion{wr.wr_id, st, 0});
-                continue;
-            }
+        const int st = resolve_remote(wr.rkey, wr.remote_addr, wr.length, &rptr, &remote_host, nullptr);
+        if (st != kWcSuccess) {
+            rail_->cq_.push_back(WorkCompletion{wr.wr_id, st, 0});
+            continue;
         }
         if (lr.device && lr.dev != rail_->dev_) gpu::enable_peer_access(rail_->dev_, lr.dev);
         kern::CopyDesc d;
@@ -732,9 +820,134 @@ int NvlQp::post(const WorkRequest *wrs, size_t n) {
     return 0;
 }
 
+int NvlQp::resolve_remote(uint32_t rkey, uintptr_t raddr, size_t len, uintptr_t *out, bool *host, McInfo *mc) {
+    *host = false;
+    if (remote_pid_ == getpid()) {
+        Region rr;
+        if (!Registry::get().lookup(rkey, &rr) || raddr < rr.addr || raddr + len > rr.addr + rr.len)
+            return kWcRemAccessErr;
+        if (rr.device && rr.dev != rail_->dev_) gpu::enable_peer_access(rail_->dev_, rr.dev);
+        *out = raddr;
+        *host = !rr.device;
+        if (mc) {
+            mc->token = rr.mc_token;
+            mc->members = rr.mc_members;
+            mc->base = rr.addr;
+        }
+        return kWcSuccess;
+    }
+    return RemoteMaps::get().resolve(remote_pid_, rkey, raddr, len, rail_->dev_, out, host, mc);
+}
+
+int NvlQp::describe_remote(uint32_t rkey, uintptr_t raddr, size_t len, McInfo *mc) {
+    if (remote_pid_ == getpid()) {
+        Region rr;
+        if (!Registry::get().lookup(rkey, &rr) || raddr < rr.addr || raddr + len > rr.addr + rr.len)
+            return kWcRemAccessErr;
+        mc->token = rr.mc_token;
+        mc->members = rr.mc_members;
+        mc->base = rr.addr;
+        return kWcSuccess;
+    }
+    return RemoteMaps::get().describe(remote_pid_, rkey, raddr, len, mc);
+}
+
+// One-to-many WRITE. Every target QP is a QP of this rail (one per
+// destination connection); each resolves its own peer's range. The bytes go
+// out in one gather_bcast launch that reads each source tile once: as
+// multicast stores when the destinations are exactly the other members of
+// one NVLS group at a common offset (and this process holds the group's
+// multicast mapping), else as bulk stores to each destination (<= 8).
+int NvlQp::post_fanout(const WorkRequest &wr, const FanoutTarget *targets, size_t n, void *h2d_window) {
+    if (n == 0 || n > static_cast<size_t>(kern::kMaxFanoutDsts) || wr.op != Opcode::kWrite ||
+        (wr.local_addr | wr.length) & 15u)
+        return MPCOMM_ERR_INVALID_ARG;
+    for (size_t i = 0; i < n; ++i) {
+        auto *q = dynamic_cast<NvlQp *>(targets[i].qp);
+        if (!q || q->rail_ != rail_ || (targets[i].remote_addr & 15u)) return MPCOMM_ERR_INVALID_ARG;
+    }
+    std::lock_guard<std::mutex> g(rail_->mu_);
+    auto fail = [&](int st) {
+        rail_->cq_.push_back(WorkCompletion{wr.wr_id, st, 0});
+        if (h2d_window) __atomic_store_n(&static_cast<kern::H2DWindow *>(h2d_window)->armed, 0u, __ATOMIC_RELEASE);
+        return 0;
+    };
+    for (size_t i = 0; i < n; ++i) {
+        auto *q = static_cast<NvlQp *>(targets[i].qp);
+        const QpState qs = q->state_.load();
+        if (qs == QpState::kErr) return fail(kWcFlushErr);
+        if (qs != QpState::kRts) return MPCOMM_ERR_CONNECTION;
+        if (q->remote_pid_ > 0 && q->remote_pid_ != getpid() &&
+            kill(static_cast<pid_t>(q->remote_pid_), 0) != 0 && errno == ESRCH) {
+            MPCOMM_LOG_WARN("MPComm[nvl]: peer process %ld is gone; QP %u on %s -> error\n", q->remote_pid_,
+                            q->qpn_, rail_->name().c_str());
+            q->state_ = QpState::kErr;
+            return fail(kWcRetryExcErr);
+        }
+    }
+    Region lr;
+    if (!Registry::get().lookup(wr.lkey, &lr) || wr.local_addr < lr.addr ||
+        wr.local_addr + wr.length > lr.addr + lr.len)
+        return fail(kWcLocProtErr);
+    if (lr.device && lr.dev != rail_->dev_) gpu::enable_peer_access(rail_->dev_, lr.dev);
+    PendingFanout f;
+    f.src = reinterpret_cast<const void *>(wr.local_addr);
+    f.mc = nullptr;
+    f.bytes = wr.length;
+    f.wr_id = wr.wr_id;
+    f.win = static_cast<kern::H2DWindow *>(h2d_window);
+    // Pass 1: multicast identity of every target (nothing mapped yet; a
+    // group copy may be a VMM allocation that CUDA IPC cannot open).
+    uint64_t token = 0;
+    int members = 0;
+    uintptr_t offset = 0;
+    bool same_group = true;
+    std::set<std::pair<long, uintptr_t>> owners;  // distinct group copies among the targets
+    for (size_t i = 0; i < n; ++i) {
+        auto *q = static_cast<NvlQp *>(targets[i].qp);
+        McInfo mc;
+        const int st = q->describe_remote(targets[i].rkey, targets[i].remote_addr, wr.length, &mc);
+        if (st != kWcSuccess) return fail(st);
+        const uintptr_t off = targets[i].remote_addr - mc.base;
+        if (i == 0) {
+            token = mc.token;
+            members = mc.members;
+            offset = off;
+        }
+        same_group &= mc.token != 0 && mc.token == token && mc.members == members && off == offset;
+        owners.emplace(q->remote_pid_, mc.base);
+    }
+    same_group &= owners.size() == n;
+    // Multicast reaches every member, the sending GPU's own copy included:
+    // used only when the targets are exactly the members other than this
+    // process's copy, and the source does not overlap that copy's target
+    // range except by being it (its multicast store would overwrite bytes
+    // still to be read).
+    Region mine;
+    if (same_group && static_cast<int>(n) + 1 == members && Registry::get().find_multicast(token, &mine) &&
+        mine.dev == rail_->dev_ && offset + wr.length <= mine.len) {
+        const uintptr_t own = mine.addr + offset;
+        const bool overlap = wr.local_addr < own + wr.length && own < wr.local_addr + wr.length;
+        if (!overlap || wr.local_addr == own) f.mc = reinterpret_cast<void *>(mine.mc_addr + offset);
+    }
+    // Pass 2 (P2P sink): each destination mapped on this rail's GPU.
+    if (!f.mc) {
+        for (size_t i = 0; i < n; ++i) {
+            auto *q = static_cast<NvlQp *>(targets[i].qp);
+            uintptr_t ptr = 0;
+            bool host = false;
+            const int st = q->resolve_remote(targets[i].rkey, targets[i].remote_addr, wr.length, &ptr, &host, nullptr);
+            if (st != kWcSuccess) return fail(st);
+            f.dsts.push_back(reinterpret_cast<void *>(ptr));
+        }
+    }
+    pending_fanout_.push_back(std::move(f));
+    return 0;
+}
+
 void NvlQp::flush() {
     std::lock_guard<std::mutex> g(rail_->mu_);
-    if (pending_.empty()) return;
+    if (pending_.empty() && pending_fanout_.empty()) return;
     nvtx::Range range("mpcomm::nvl_doorbell");
     gpu::set_device(rail_->dev_);
     void *stream = rail_->override_stream_ ? rail_->override_stream_ : stream_;
@@ -776,6 +989,35 @@ void NvlQp::flush() {
     pending_lens_.clear();
     pending_host_ = false;
     pending_h2d_ = false;
+    for (auto &pf : pending_fanout_) {
+        Inflight f;
+        f.event = nullptr;
+        f.failed = false;
+        f.seq = ++seq_;
+        f.wr_ids.assign(1, pf.wr_id);
+        f.lens.assign(1, pf.bytes);
+        uint64_t *flag = done_word_;
+        int e = done_word_ ? 0 : -1;
+        if (e == 0)
+            e = kern::gather_bcast(pf.src, 0, nullptr, 1, pf.bytes, pf.mc, pf.dsts.data(),
+                                   static_cast<int>(pf.dsts.size()), nullptr, &flag, 1, f.seq, status_ + 4, 0, stream,
+                                   status_, nullptr, pf.win);
+        if (e == 0) {
+            f.event = rail_->take_event();
+            if (!f.event || gpu::event_record(f.event, stream) != 0) e = -1;
+        }
+        if (e != 0) {
+            MPCOMM_LOG_ERROR("MPComm[nvl]: fan-out launch failed on %s: %s\n", rail_->name().c_str(),
+                             e > 0 ? gpu::error_string(e) : "event");
+            rail_->cq_.push_back(WorkCompletion{pf.wr_id, kWcGeneralErr, 0});
+            if (f.event) rail_->give_event(f.event);
+            if (pf.win) __atomic_store_n(&pf.win->armed, 0u, __ATOMIC_RELEASE);
+        } else {
+            f.launched = std::chrono::steady_clock::now();
+            inflight_.push_back(std::move(f));
+        }
+    }
+    pending_fanout_.clear();
 }
 
 void NvlQp::reap(std::deque<WorkCompletion> *cq) {

@@ -198,7 +198,21 @@ int main(int argc, char **argv) {
     for (const std::string &tt : split(tests, ',')) {
         auto one_round = [&]() -> int {
             std::vector<mpcomm::TransferHandle> hs;
-            for (size_t b = 0; b < batch; ++b) {
+            if (tt == "broadcast") {
+                // One request per batch slot to every target at once (one
+                // length, the same local bytes; on the GPU fabric the engine
+                // writes all targets in one launch per chunk).
+                std::vector<std::string> ids;
+                for (auto &t : targets) ids.push_back(t.id);
+                for (size_t b = 0; b < batch; ++b) {
+                    std::vector<uintptr_t> rs;
+                    for (size_t t = 0; t < targets.size(); ++t) rs.push_back(remote[t] + b * size);
+                    mpcomm::TransferHandle h = comm.broadcastAsync(lp + b * size, size, ids, rs);
+                    if (h == mpcomm::INVALID_TRANSFER_HANDLE) return -1;
+                    hs.push_back(h);
+                }
+            }
+            for (size_t b = 0; b < batch && tt != "broadcast"; ++b) {
                 for (size_t t = 0; t < targets.size(); ++t) {
                     const uintptr_t l = lp + (t * batch + b) * size;
                     const uintptr_t r = remote[t] + b * size;
@@ -207,7 +221,6 @@ int main(int argc, char **argv) {
                     else if (tt == "get") h = comm.getAsync(l, targets[t].id, r, size);
                     else if (tt == "scatter") h = comm.scatterAsync(l, {targets[t].id}, {r}, {size});
                     else if (tt == "gather") h = comm.gatherAsync(l, {targets[t].id}, {r}, {size});
-                    else if (tt == "broadcast") h = comm.broadcastAsync(lp, size, {targets[t].id}, {r});
                     if (h == mpcomm::INVALID_TRANSFER_HANDLE) return -1;
                     hs.push_back(h);
                 }

@@ -312,6 +312,21 @@ class MPComm {
     static std::vector<KernelTraceRecord> getKernelTrace();
     // Name of the fabric backend in use ("nvl", "lo", "sock", "ib").
     std::string getFabricName() const;
+    // Registers this process's copy of an NVLS multicast group buffer (GPU
+    // fabric): [uc_addr, uc_addr + length) is bound to the group at offset
+    // 0, `mc_addr` is this process's mapping of the group's multicast
+    // address, `group_token` (non-zero) names the group in every member
+    // process and `group_size` counts its GPUs. Every member registers its
+    // copy (then publishes it as usual). A broadcastAsync whose destinations
+    // are exactly the group's other members at one common offset is then
+    // sent as NVLS multicast stores, one launch per chunk (the switch
+    // replicates each store; the source crosses this GPU's NVLinks once).
+    // The sending GPU's own copy at that offset receives the bytes too.
+    // Broadcasts to other destination sets use one launch per chunk that
+    // stores to each destination (up to 8). Both fused forms need 16-byte
+    // aligned addresses and lengths; MPCOMM_FUSED_BROADCAST=0 turns them off.
+    int registerMulticastMemory(void *uc_addr, size_t length, void *mc_addr, uint64_t group_token,
+                                int group_size);
 
     class Impl;  // opaque implementation type
 

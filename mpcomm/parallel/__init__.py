@@ -181,9 +181,11 @@ class NvlsGroup:
         self.size = (nbytes + gran - 1) // gran * gran
         self.mc = self.mem = self.uc_ptr = self.mc_ptr = 0
         name = None
+        token = 0
         srv = None
         fd = -1
         if self.rank == root:
+            token = uuid.uuid4().int & ((1 << 63) - 1) | 1
             err, self.mc, fd = _native.multicast_create(self.size, self.world)
             if err:
                 raise RuntimeError(f"cuMulticastCreate failed ({err})")
@@ -191,9 +193,9 @@ class NvlsGroup:
             srv = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
             srv.bind(name)
             srv.listen(self.world)
-        holder = [name]
+        holder = [name, token]
         dist.broadcast_object_list(holder, src=root)
-        name = holder[0]
+        name, self.token = holder
         try:
             if self.rank == root:
                 for _ in range(self.world - 1):
@@ -251,6 +253,15 @@ class NvlsGroup:
         err = _native.nvls_broadcast(root_ptr + off, self.mc_ptr + off, ln, max_ctas, int(s.cuda_stream))
         if err:
             raise RuntimeError(f"nvls_broadcast failed with CUDA error {err}")
+
+    def register(self, comm) -> None:
+        """Registers this rank's copy with an ``MPComm`` (GPU fabric) as a
+        member of this multicast group: ``broadcast_async`` from one member to
+        all the others' copies (published and queried as usual) then goes out
+        as NVLS multicast stores, one launch per chunk."""
+        err = comm.register_multicast_memory(self.uc_ptr, self.size, self.mc_ptr, self.token, self.world)
+        if err:
+            raise RuntimeError(f"register_multicast_memory failed ({err})")
 
     def close(self):
         torch.cuda.synchronize()

@@ -37,6 +37,11 @@ class PyMPComm {
         return c_.registerMemory(reinterpret_cast<void *>(a), l);
     }
     int unregister_memory(uintptr_t a) { return c_.unregisterMemory(reinterpret_cast<void *>(a)); }
+    int register_multicast_memory(uintptr_t uc, size_t l, uintptr_t mc, uint64_t token, int members) {
+        py::gil_scoped_release r;
+        return c_.registerMulticastMemory(reinterpret_cast<void *>(uc), l, reinterpret_cast<void *>(mc), token,
+                                          members);
+    }
     int connect(const std::string &id, const std::string &addr, int port) {
         py::gil_scoped_release r;
         return c_.connect(id, addr, port);
@@ -313,6 +318,10 @@ PYBIND11_MODULE(_mpcomm, m) {
         .def("shutdown", &C::shutdown)
         .def("register_memory", &C::register_memory, py::arg("addr"), py::arg("length"))
         .def("unregister_memory", &C::unregister_memory, py::arg("addr"))
+        .def("register_multicast_memory", &C::register_multicast_memory, py::arg("uc_addr"), py::arg("length"),
+             py::arg("mc_addr"), py::arg("group_token"), py::arg("group_size"),
+             "Registers this process's copy of an NVLS multicast group buffer; broadcast_async to the group's "
+             "other members then goes out as multicast stores.")
         .def("connect", &C::connect, py::arg("remote_host_id"), py::arg("remote_tcp_addr"),
              py::arg("remote_tcp_port"))
         .def("start_accept_thread", &C::start_accept_thread)

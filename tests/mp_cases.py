@@ -14,6 +14,10 @@ non-zero on any mismatch.
           completed by a device flag every rank waits on with a bounded wait.
   peer_exit  (2 ranks) rank 1 leaves between steps; rank 0's next PUT to it
           fails on the host, fast, and its engine keeps working.
+  engine_bcast  MPComm.broadcast_async from rank 0 to every other rank: one
+          fused launch per chunk (bulk stores to each peer's published
+          buffer), then to the other members' copies of an NVLS group
+          (multicast stores); the kernel trace shows which launch ran.
 """
 import argparse
 import datetime
@@ -264,9 +268,87 @@ def case_peer_exit(rank, world):
     return True
 
 
+def case_engine_bcast(rank, world):
+    os.environ["MPCOMM_NVL_CHUNK_SIZE"] = str(16 << 20)  # several chunks per broadcast
+    n = (40 << 20) + 4096
+    comm = mpcomm.MPComm()
+    assert comm.init(f"b{rank}") == 0 and comm.get_fabric_name() == "nvl"
+    assert comm.start_accept_thread() == 0
+    g = torch.Generator(device="cuda").manual_seed(77)
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda", generator=g)  # same on every rank
+    inbox = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    for t in (src, inbox):
+        assert comm.register_memory(t.data_ptr(), n) == 0
+    assert comm.publish_buffer(inbox.data_ptr(), n) == 0
+    ports = [None] * world
+    dist.all_gather_object(ports, comm.get_tcp_port())
+    dist.barrier()
+    hosts = [f"b{r}" for r in range(1, world)]
+    if rank == 0:
+        for r in range(1, world):
+            assert comm.connect(f"b{r}", "127.0.0.1", ports[r]) == 0
+
+    def trace_kinds():
+        return [t["kind"] for t in mpcomm._native.kernel_trace()]
+
+    def bcast(raddrs, want_kind):
+        mpcomm._native.kernel_trace_reset()
+        h = comm.broadcast_async(src.data_ptr(), n, hosts, raddrs)
+        assert h != mpcomm.INVALID_TRANSFER_HANDLE
+        assert comm.wait_transfer(h, 60000) == 0, "broadcast failed"
+        res = comm.get_transfer_result(h)
+        comm.release_transfer(h)
+        assert res["bytes_transferred"] == n * (world - 1), res
+        kinds = trace_kinds()
+        # 3 chunks of at most 16 MiB: one fused launch each, no per-destination copies.
+        assert kinds.count(want_kind) == 3 and "copy_batch" not in kinds, kinds
+
+    if rank == 0:
+        raddrs = []
+        for r in range(1, world):
+            info = comm.query_remote_buffers(f"b{r}", "127.0.0.1", ports[r])
+            raddrs.append(next(b["addr"] for b in info["buffers"] if b["length"] == n))
+        bcast(raddrs, "gather_bcast_p2p")
+    dist.barrier()
+    if rank != 0:
+        assert torch.equal(inbox, src), "fused P2P broadcast mismatch"
+    used = ["p2p"]
+    try:
+        grp = parallel.NvlsGroup(n)
+    except RuntimeError as e:
+        grp = None
+        used.append(f"nvls unavailable ({e})")
+    if grp is not None:
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        grp.register(comm)
+        assert comm.publish_buffer(grp.uc_ptr, grp.size, 7) == 0
+        ucs = [None] * world
+        dist.all_gather_object(ucs, grp.uc_ptr)
+        dist.barrier()
+        if rank == 0:
+            for r in range(1, world):  # refresh the peers' buffer lists
+                assert comm.query_remote_buffers(f"b{r}", "127.0.0.1", ports[r])
+            bcast(ucs[1:], "gather_bcast_nvls")
+        dist.barrier()
+        # Every member's copy holds the batch, the sender's own included.
+        assert torch.equal(grp.uc[:n], src), "fused NVLS broadcast mismatch"
+        dist.barrier()
+        comm.unpublish_buffer(grp.uc_ptr)
+        comm.unregister_memory(grp.uc_ptr)
+        dist.barrier()
+        grp.close()
+        used.append("nvls")
+    dist.barrier()
+    comm.shutdown()
+    if rank == 0:
+        print(f"engine_bcast case used: {used}", flush=True)
+
+
 def main():
+    os.environ.setdefault("MPCOMM_KERNEL_TRACE", "4096")
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["putget", "pxn", "nvls", "gather_bcast", "peer_exit", "all"])
+    p.add_argument("case", choices=["putget", "pxn", "nvls", "gather_bcast", "peer_exit", "engine_bcast", "all"])
     a = p.parse_args()
     rank, world, _ = parallel.init_from_env("gloo")
     if a.case == "peer_exit":
@@ -276,7 +358,7 @@ def main():
         if rank == 0:
             print("case peer_exit ok", flush=True)
         os._exit(0)
-    cases = ["putget", "pxn", "nvls", "gather_bcast"] if a.case == "all" else [a.case]
+    cases = ["putget", "pxn", "nvls", "gather_bcast", "engine_bcast"] if a.case == "all" else [a.case]
     for c in cases:
         globals()[f"case_{c}"](rank, world)
         if rank == 0:
