@@ -113,6 +113,15 @@ struct Transfer {
     bool fanout = false;
     size_t fanout_rail = 0;
     bool host_source = false;  // local buffer in host memory (H2D QoS window)
+    // Paged PUT: the source is pages of a pool (indices on the GPU of
+    // paged_rail); chunk k covers pages [k * pages_per_chunk, ...).
+    bool paged = false;
+    size_t paged_rail = 0;
+    uintptr_t pool = 0;
+    uint64_t pool_pages = 0;
+    const int64_t *indices = nullptr;
+    uint32_t page_bytes = 0;
+    size_t pages_per_chunk = 0;
 
     // Worker-owned progress.
     size_t next_chunk = 0;
@@ -175,6 +184,8 @@ class MPComm::Impl {
     TransferHandle submit(uintptr_t local, const std::vector<std::string> &hosts,
                           const std::vector<uintptr_t> &raddrs, const std::vector<size_t> &lens,
                           Direction dir);
+    TransferHandle submitPaged(uintptr_t dram_dev_ptr, const int64_t *indices, int num_blocks, int block_size,
+                               const std::string &host, uintptr_t raddr);
     bool isTransferComplete(TransferHandle h);
     int waitTransfer(TransferHandle h, int timeout_ms);
     TransferResult getTransferResult(TransferHandle h);
@@ -283,6 +294,7 @@ class MPComm::Impl {
     void wakeWorker(Worker *w);
     void postChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched);
     void postFanoutChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched);
+    void postPagedChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched);
     void handleCompletion(Worker *w, const fabric::WorkCompletion &wc);
     void retire(Worker *w);
     void probeQuarantine();

@@ -182,6 +182,86 @@ TransferHandle MPComm::Impl::submit(uintptr_t local, const std::vector<std::stri
     return h;
 }
 
+// Paged PUT (the fused PXN gather + forward as a transfer): the GPU that
+// holds `indices` gathers the pages from the pool and stores them into the
+// remote range, one launch per chunk of pages, on its own rail.
+TransferHandle MPComm::Impl::submitPaged(uintptr_t pool, const int64_t *indices, int n, int bs,
+                                         const std::string &host, uintptr_t raddr) {
+    if (!initialized_ || !pool || !indices || n <= 0 || bs <= 0) {
+        MPCOMM_LOG_ERROR("MPComm: putPagesAsync failed - invalid arguments\n");
+        return INVALID_TRANSFER_HANDLE;
+    }
+    auto conn = connection(host);
+    if (!conn) {
+        MPCOMM_LOG_ERROR("MPComm: putPagesAsync failed - not connected to %s\n", host.c_str());
+        return INVALID_TRANSFER_HANDLE;
+    }
+    const int gpu = gpu::device_of(indices);
+    size_t rail = SIZE_MAX;
+    for (size_t r = 0; r < rails_.size(); ++r)
+        if (rails_[r]->gpu == gpu && gpu >= 0 && rails_[r]->rail->supports_paged() && conn->group_for(r)) rail = r;
+    if (rail == SIZE_MAX) {
+        MPCOMM_LOG_ERROR("MPComm: putPagesAsync failed - the indices must be device memory of a GPU whose "
+                         "fabric rail is connected to %s (GPU fabric; MPCOMM_PXN_ENABLE=1 opens a rail per GPU)\n",
+                         host.c_str());
+        return INVALID_TRANSFER_HANDLE;
+    }
+    auto t = std::make_shared<Transfer>();
+    t->t_start = Clock::now();
+    t->dir = Direction::kScatter;
+    t->op = fabric::Opcode::kWrite;
+    t->paged = true;
+    t->paged_rail = rail;
+    t->pool = pool;
+    t->indices = indices;
+    t->page_bytes = static_cast<uint32_t>(bs);
+    {
+        // Index bound from the DRAM mapping that holds the pool, if known.
+        std::lock_guard<std::mutex> g(map_mu_);
+        for (auto &kv : mappings_) {
+            const uintptr_t d0 = kv.second.dev_ptr, d1 = d0 + kv.second.len;
+            if (pool >= d0 && pool < d1) t->pool_pages = (d1 - pool) / static_cast<uintptr_t>(bs);
+        }
+    }
+    const size_t total = static_cast<size_t>(n) * static_cast<size_t>(bs);
+    t->local_addr = 0;
+    t->hosts = {host};
+    t->remote_addrs = {raddr};
+    t->lengths = {total};
+    t->conns = {conn};
+    t->candidates = {rail};
+    t->local_gpu = gpu;
+    t->host_source = gpu::device_of(reinterpret_cast<const void *>(pool)) < 0;
+    t->pages_per_chunk = std::max<size_t>(1, effectiveChunk({rail}) / static_cast<size_t>(bs));
+    t->plan.build(0, {raddr}, {total}, t->pages_per_chunk * static_cast<size_t>(bs), false);
+    size_t ol = throttle_outstanding_.load(std::memory_order_relaxed);
+    if (ol == 0) ol = rails_[rail]->rail->preferred_outstanding(cfg_);
+    t->outstanding_limit = std::max<size_t>(1, ol);
+    t->repost_budget = t->plan.total() + 16;
+    t->handle = handles_.allocate();
+    if (t->handle == INVALID_TRANSFER_HANDLE) {
+        MPCOMM_LOG_ERROR("MPComm: putPagesAsync failed - handle pool exhausted\n");
+        return INVALID_TRANSFER_HANDLE;
+    }
+    t->owner = rails_[rail]->numa % static_cast<int>(std::max<size_t>(1, workers_.size()));
+    t->numa = t->owner;
+    t->t_queued = Clock::now();
+    const uint64_t h = t->handle;
+    {
+        std::lock_guard<std::mutex> g(xfer_mu_);
+        transfers_[h] = t;
+    }
+    handle_table_[h].store(t.get(), std::memory_order_release);
+    {
+        std::lock_guard<std::mutex> g(admit_mu_);
+        admit_[h] = t;
+    }
+    Worker *w = workers_[t->owner].get();
+    while (!w->queue.try_push(h)) cpu_relax();
+    wakeWorker(w);
+    return h;
+}
+
 void MPComm::Impl::wakeWorker(Worker *w) {
     w->doorbell.fetch_add(1);  // seq_cst: ordered against the worker's `sleeping` store
     if (w->sleeping.load()) {
@@ -449,10 +529,95 @@ void MPComm::Impl::postFanoutChunks(Worker *w, Transfer *t, std::vector<fabric::
     }
 }
 
+void MPComm::Impl::postPagedChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched) {
+    const size_t total = t->plan.total();
+    const size_t r = t->paged_rail;
+    while (true) {
+        size_t chunk;
+        bool from_retry = false;
+        if (!t->retry.empty()) {
+            chunk = t->retry.front();
+            from_retry = true;
+        } else if (t->next_chunk < total) {
+            chunk = t->next_chunk;
+        } else {
+            break;
+        }
+        if (rails_[r]->quarantined.load(std::memory_order_relaxed)) {
+            // Only the GPU holding the indices can run the gather.
+            t->error.store(MPCOMM_ERR_TRANSFER);
+            t->aborted = true;
+            break;
+        }
+        const Chunk c = t->plan.get(chunk);
+        QpGroup *g = t->conns[0]->group_for(r);
+        if (!g || g->qps.empty()) {
+            t->error.store(MPCOMM_ERR_CONNECTION);
+            t->aborted = true;
+            break;
+        }
+        const size_t rail_out = w->rail_posted[r] - w->rail_completed[r];
+        if (rail_out >= t->outstanding_limit * std::min(cfg_.qps_per_connection, g->qps.size())) break;
+        size_t q = SIZE_MAX, q_out = SIZE_MAX;
+        const size_t nq = std::min(g->qps.size(), kMaxQpsPerRail);
+        for (size_t i = 0; i < nq; ++i) {
+            const size_t out = w->qp_posted[r][i] - w->qp_completed[r][i];
+            if (out < t->outstanding_limit && out < q_out) {
+                q = i;
+                q_out = out;
+            }
+        }
+        if (q == SIZE_MAX) break;
+        if (!qosAllowRemoteWrite(*t->conns[0], c.remote_addr, c.length)) break;
+        fabric::PagedWrite pw;
+        pw.wr_id = WrId::encode(r, q, t->handle, chunk);
+        pw.pool = t->pool;
+        pw.pool_pages = t->pool_pages;
+        pw.indices = t->indices + chunk * t->pages_per_chunk;
+        pw.count = static_cast<uint32_t>(c.length / t->page_bytes);
+        pw.page_bytes = t->page_bytes;
+        pw.remote_addr = c.remote_addr;
+        pw.rkey = t->conns[0]->rkey_for(c.remote_addr, g->remote_rail);
+        if (pw.rkey == 0) {
+            MPCOMM_LOG_ERROR("MPComm: no rkey for remote 0x%lx on %s (query the peer's buffers first)\n",
+                             static_cast<unsigned long>(c.remote_addr), t->conns[0]->host_id.c_str());
+            t->error.store(MPCOMM_ERR_MEMORY);
+            t->aborted = true;
+            break;
+        }
+        kern::H2DWindow *win = nullptr;
+        uint32_t *wctr = nullptr;
+        if (t->host_source) acquireH2DWindow(rails_[r]->gpu, &win, &wctr);
+        pw.h2d_window = win;
+        fabric::QueuePair *qp = g->qps[q].get();
+        if (qp->post_paged(pw) != 0) {
+            if (win) __atomic_store_n(&win->armed, 0u, __ATOMIC_RELEASE);
+            t->error.store(MPCOMM_ERR_TRANSFER);
+            t->aborted = true;
+            break;
+        }
+        ++w->rail_posted[r];
+        ++w->qp_posted[r][q];
+        ++t->in_flight;
+        if (from_retry) t->retry.pop_front();
+        else ++t->next_chunk;
+        if (std::find(touched->begin(), touched->end(), qp) == touched->end()) touched->push_back(qp);
+        if (!t->first_posted) {
+            t->first_posted = true;
+            t->t_first_post = Clock::now();
+        }
+        if (t->next_chunk == total && t->retry.empty()) t->t_all_posted = Clock::now();
+    }
+}
+
 void MPComm::Impl::postChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched) {
     if (t->finished.load(std::memory_order_relaxed) || t->aborted) return;
     if (t->fanout) {
         postFanoutChunks(w, t, touched);
+        return;
+    }
+    if (t->paged) {
+        postPagedChunks(w, t, touched);
         return;
     }
     const size_t total = t->plan.total();
@@ -599,7 +764,7 @@ void MPComm::Impl::handleCompletion(Worker *w, const fabric::WorkCompletion &wc)
     const int dom = t->op == fabric::Opcode::kRead
                         ? t->local_gpu
                         : (t->remote_gpu.empty() ? -1 : t->remote_gpu[c.host_idx]);
-    if (cfg_.pcie_stat_enable && !t->fanout) pcieOnCompleted(dom, c.length);
+    if (cfg_.pcie_stat_enable && !t->fanout && !t->paged) pcieOnCompleted(dom, c.length);
     if (wc.status == fabric::kWcSuccess || cfg_.fault_tolerate) {
         // A fused broadcast chunk wrote its bytes to every destination.
         const uint64_t moved = t->fanout ? c.length * t->hosts.size() : c.length;

@@ -86,10 +86,12 @@ uint32_t crc32_host(const void *data, size_t len, uint32_t crc);
 // DRAM mapped on this GPU) into dst[i*bs ..], where dst may be a peer GPU's
 // HBM (IPC-mapped). After every store of the launch has completed, the last
 // CTA publishes `flag_value` to *done_flag (system-scope release; the flag
-// may live in the peer's memory).
+// may live in the peer's memory). `window` (optional, needs `ctr`): H2D QoS
+// window of the host pool read, opened by the first CTA, closed by the last.
 int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx, void *dst,
                        int64_t n, int64_t bs, int max_ctas, void *stream, uint32_t *status,
-                       uint64_t *done_flag, uint64_t flag_value, uint32_t *ctr, LaunchInfo *info);
+                       uint64_t *done_flag, uint64_t flag_value, uint32_t *ctr, LaunchInfo *info,
+                       H2DWindow *window = nullptr);
 
 // NVLS broadcast: multimem stores of src[0..bytes) into a multicast address
 // (every GPU bound to the multicast object receives the bytes).

@@ -597,9 +597,10 @@ int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_
 
 int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx, void *dst,
                        int64_t n, int64_t bs, int max_ctas, void *stream, uint32_t *status,
-                       uint64_t *done_flag, uint64_t flag_value, uint32_t *ctr, LaunchInfo *info) {
+                       uint64_t *done_flag, uint64_t flag_value, uint32_t *ctr, LaunchInfo *info,
+                       H2DWindow *window) {
     if (!pool || !idx || !dst || n <= 0 || bs <= 0) return cudaErrorInvalidValue;
-    if (done_flag && !ctr) return cudaErrorInvalidValue;
+    if ((done_flag || window) && !ctr) return cudaErrorInvalidValue;
     const int path = pick_path(kModeAuto, pool, dst, bs);
     GatherSrc src;
     src.pool = static_cast<const char *>(pool);
@@ -610,7 +611,7 @@ int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx
     src.pool_blocks = pool_blocks;
     src.tile_bytes = path == 1 ? kStageBytes : kVecTileBytes;
     src.tpb = (bs + src.tile_bytes - 1) / src.tile_bytes;
-    const Epilogue ep{nullptr, ctr, done_flag, flag_value,
+    const Epilogue ep{window, ctr, done_flag, flag_value,
                       trace_acquire("pxn_gather_forward", static_cast<uint64_t>(n * bs))};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     return path == 1 ? launch_bulk(src, src.n * src.tpb, max_ctas, st, status, ep, info)

@@ -52,6 +52,10 @@ TransferHandle MPComm::broadcastAsync(uintptr_t local, size_t len, const std::ve
     if (hosts.empty() || raddrs.size() != hosts.size() || len == 0) return INVALID_TRANSFER_HANDLE;
     return impl_->submit(local, hosts, raddrs, std::vector<size_t>(hosts.size(), len), Direction::kBroadcast);
 }
+TransferHandle MPComm::putPagesAsync(uintptr_t dram_dev_ptr, const int64_t *indices, int num_blocks, int block_size,
+                                     const std::string &host, uintptr_t raddr) {
+    return impl_->submitPaged(dram_dev_ptr, indices, num_blocks, block_size, host, raddr);
+}
 TransferHandle MPComm::putAsync(uintptr_t local, const std::string &host, uintptr_t raddr, size_t len) {
     if (len == 0) return INVALID_TRANSFER_HANDLE;
     return impl_->submit(local, {host}, {raddr}, {len}, Direction::kScatter);

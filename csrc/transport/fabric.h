@@ -67,6 +67,22 @@ enum class QpState { kReset, kInit, kRtr, kRts, kErr };
 
 class QueuePair;
 
+// A WRITE whose source is a list of pages of a pool (host DRAM mapped for
+// the device, or device memory): page i = pool + indices[i] * page_bytes,
+// written contiguously from remote_addr. `indices` is device memory of the
+// rail's GPU and stays valid until the completion.
+struct PagedWrite {
+    uint64_t wr_id;
+    uintptr_t pool;
+    uint64_t pool_pages;     // index bound (0 = unchecked)
+    const int64_t *indices;
+    uint32_t count;
+    uint32_t page_bytes;
+    uintptr_t remote_addr;
+    uint32_t rkey;
+    void *h2d_window;        // kern::H2DWindow of a host pool read (may be null)
+};
+
 // One destination of a one-to-many WRITE (post_fanout): the QP of that
 // destination's connection (on the same local rail as the posting QP), the
 // remote address and its rkey.
@@ -110,6 +126,10 @@ class QueuePair {
                             void * /*h2d_window*/) {
         return -7;  // MPCOMM_ERR_INVALID_ARG
     }
+    // Paged WRITE (gather from a pool + write to the peer in one device
+    // operation; one completion carrying w.wr_id). Rails without
+    // supports_paged() return MPCOMM_ERR_INVALID_ARG.
+    virtual int post_paged(const PagedWrite & /*w*/) { return -7; }
 };
 
 class Rail {
@@ -136,6 +156,8 @@ class Rail {
     }
     // Routes kernel launches (nvl) into a caller stream; others ignore it.
     virtual int set_stream(void * /*stream*/) { return 0; }
+    // True when QPs of this rail accept post_paged.
+    virtual bool supports_paged() const { return false; }
     // Largest number of destinations one post_fanout may carry (0 = none).
     virtual size_t max_fanout() const { return 0; }
     // Source and destination alignment a one-to-many WRITE needs (bytes).

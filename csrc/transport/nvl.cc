@@ -546,6 +546,7 @@ class NvlQp final : public QueuePair {
     }
     int post(const WorkRequest *wrs, size_t n) override;
     int post_fanout(const WorkRequest &wr, const FanoutTarget *targets, size_t n, void *h2d_window) override;
+    int post_paged(const PagedWrite &w) override;
     void flush() override;
     // Retires completed launches into the rail CQ. Caller holds rail mutex.
     void reap(std::deque<WorkCompletion> *cq);
@@ -578,6 +579,12 @@ class NvlQp final : public QueuePair {
         kern::H2DWindow *win;      // QoS window of a host-memory source (may be null)
     };
     std::vector<PendingFanout> pending_fanout_;
+    // Paged WRITEs queued since the last flush: one pxn_gather_forward each.
+    struct PendingPaged {
+        PagedWrite w;
+        void *dst;
+    };
+    std::vector<PendingPaged> pending_paged_;
     // Resolves a remote range of this QP's peer to a device pointer on this
     // rail's GPU (kWcSuccess or a WC error status); fills *mc if non-null.
     int resolve_remote(uint32_t rkey, uintptr_t raddr, size_t len, uintptr_t *out, bool *host, McInfo *mc);
@@ -646,6 +653,7 @@ class NvlRail final : public Rail {
         return cfg.max_outstanding_set ? cfg.max_outstanding_per_qp : cfg.nvl_outstanding_per_qp;
     }
     size_t max_fanout() const override { return kern::kMaxFanoutDsts; }
+    bool supports_paged() const override { return true; }
     size_t fanout_alignment() const override { return 16; }
     int set_multicast(const MemKey &key, uintptr_t uc, size_t len, uintptr_t mc, uint64_t token,
                       int members) override {
@@ -763,6 +771,10 @@ int NvlQp::to_err() {
     pending_.clear();
     pending_ids_.clear();
     pending_lens_.clear();
+    for (auto &pf : pending_fanout_) rail_->cq_.push_back(WorkCompletion{pf.wr_id, kWcFlushErr, 0});
+    pending_fanout_.clear();
+    for (auto &pp : pending_paged_) rail_->cq_.push_back(WorkCompletion{pp.w.wr_id, kWcFlushErr, 0});
+    pending_paged_.clear();
     for (auto &f : inflight_) f.failed = true;
     return 0;
 }
@@ -945,9 +957,37 @@ int NvlQp::post_fanout(const WorkRequest &wr, const FanoutTarget *targets, size_
     return 0;
 }
 
+// Paged WRITE: the pages are read by this rail's GPU (from mapped host DRAM
+// or device memory) into shared memory and stored straight into the peer's
+// range by one launch (the fused PXN gather + forward).
+int NvlQp::post_paged(const PagedWrite &w) {
+    if (!w.pool || !w.indices || w.count == 0 || w.page_bytes == 0) return MPCOMM_ERR_INVALID_ARG;
+    QpState s = state_.load();
+    if (s != QpState::kRts && s != QpState::kErr) return MPCOMM_ERR_CONNECTION;
+    std::lock_guard<std::mutex> g(rail_->mu_);
+    auto fail = [&](int st) {
+        rail_->cq_.push_back(WorkCompletion{w.wr_id, st, 0});
+        if (w.h2d_window) __atomic_store_n(&static_cast<kern::H2DWindow *>(w.h2d_window)->armed, 0u, __ATOMIC_RELEASE);
+        return 0;
+    };
+    if (s == QpState::kErr) return fail(kWcFlushErr);
+    if (remote_pid_ > 0 && remote_pid_ != getpid() && kill(static_cast<pid_t>(remote_pid_), 0) != 0 &&
+        errno == ESRCH) {
+        state_ = QpState::kErr;
+        return fail(kWcRetryExcErr);
+    }
+    uintptr_t dst = 0;
+    bool host = false;
+    const size_t bytes = static_cast<size_t>(w.count) * w.page_bytes;
+    const int st = resolve_remote(w.rkey, w.remote_addr, bytes, &dst, &host, nullptr);
+    if (st != kWcSuccess) return fail(st);
+    pending_paged_.push_back(PendingPaged{w, reinterpret_cast<void *>(dst)});
+    return 0;
+}
+
 void NvlQp::flush() {
     std::lock_guard<std::mutex> g(rail_->mu_);
-    if (pending_.empty() && pending_fanout_.empty()) return;
+    if (pending_.empty() && pending_fanout_.empty() && pending_paged_.empty()) return;
     nvtx::Range range("mpcomm::nvl_doorbell");
     gpu::set_device(rail_->dev_);
     void *stream = rail_->override_stream_ ? rail_->override_stream_ : stream_;
@@ -1018,6 +1058,36 @@ void NvlQp::flush() {
         }
     }
     pending_fanout_.clear();
+    for (auto &pp : pending_paged_) {
+        Inflight f;
+        f.event = nullptr;
+        f.failed = false;
+        f.seq = ++seq_;
+        f.wr_ids.assign(1, pp.w.wr_id);
+        f.lens.assign(1, pp.w.count * pp.w.page_bytes);
+        auto *win = static_cast<kern::H2DWindow *>(pp.w.h2d_window);
+        int e = done_word_ ? 0 : -1;
+        if (e == 0)
+            e = kern::pxn_gather_forward(reinterpret_cast<const void *>(pp.w.pool),
+                                         static_cast<int64_t>(pp.w.pool_pages), pp.w.indices, pp.dst, pp.w.count,
+                                         pp.w.page_bytes, 0, stream, status_, done_word_, f.seq, status_ + 4, nullptr,
+                                         win);
+        if (e == 0) {
+            f.event = rail_->take_event();
+            if (!f.event || gpu::event_record(f.event, stream) != 0) e = -1;
+        }
+        if (e != 0) {
+            MPCOMM_LOG_ERROR("MPComm[nvl]: paged launch failed on %s: %s\n", rail_->name().c_str(),
+                             e > 0 ? gpu::error_string(e) : "event");
+            rail_->cq_.push_back(WorkCompletion{pp.w.wr_id, kWcGeneralErr, 0});
+            if (f.event) rail_->give_event(f.event);
+            if (win) __atomic_store_n(&win->armed, 0u, __ATOMIC_RELEASE);
+        } else {
+            f.launched = std::chrono::steady_clock::now();
+            inflight_.push_back(std::move(f));
+        }
+    }
+    pending_paged_.clear();
 }
 
 void NvlQp::reap(std::deque<WorkCompletion> *cq) {

@@ -297,6 +297,20 @@ class MPComm {
     // cudaStream_t of the rail's device; nullptr restores the per-QP
     // internal streams). Lets callers bracket transfers with CUDA events.
     int setFabricStream(void *stream);
+    // Paged PUT, the fused PXN gather + forward as a transfer: page i =
+    // dram_dev_ptr + indices[i] * block_size (a pool mapped with
+    // mapDRAMtoGPU, or device memory) is written to remote_addr +
+    // i * block_size of `remote_host_id` (a published buffer, typically
+    // another GPU's HBM). The GPU that holds `indices` (device memory, kept
+    // valid until the transfer completes) gathers the pages into shared
+    // memory and stores them straight into the destination over NVLink, one
+    // launch per chunk of pages, on its GPU-fabric rail; with H2D QoS on,
+    // each launch reading host memory opens a QoS window on that GPU. Use a
+    // GPU close to the pool's NUMA node (the reference routes traffic
+    // through such a proxy GPU, src/mpcomm.cpp:5135-5403). Tracked like any
+    // transfer (waitTransfer, getTransferResult).
+    TransferHandle putPagesAsync(uintptr_t dram_dev_ptr, const int64_t *indices, int num_blocks,
+                                 int block_size, const std::string &remote_host_id, uintptr_t remote_addr);
     // Number of this library's GPU kernels launched so far (all objects).
     static uint64_t getKernelLaunchCount();
     // Extension: device start/end of recent data-mover launches, from the

@@ -74,6 +74,9 @@ class PyMPComm {
     }
     uint64_t put_async(uintptr_t l, const std::string &h, uintptr_t r, size_t n) { return c_.putAsync(l, h, r, n); }
     uint64_t get_async(uintptr_t l, const std::string &h, uintptr_t r, size_t n) { return c_.getAsync(l, h, r, n); }
+    uint64_t put_pages_async(uintptr_t dram, uintptr_t idx, int n, int bs, const std::string &h, uintptr_t r) {
+        return c_.putPagesAsync(dram, reinterpret_cast<const int64_t *>(idx), n, bs, h, r);
+    }
     uint64_t mp_replicate_async(const std::string &type, const std::vector<std::string> &h, uintptr_t l,
                                 const std::vector<uintptr_t> &r, const std::vector<size_t> &n) {
         if (type == "scatter") return c_.scatterAsync(l, h, r, n);
@@ -340,6 +343,10 @@ PYBIND11_MODULE(_mpcomm, m) {
              py::arg("remote_addr"), py::arg("length"))
         .def("get_async", &C::get_async, py::arg("local_addr"), py::arg("remote_host_id"),
              py::arg("remote_addr"), py::arg("length"))
+        .def("put_pages_async", &C::put_pages_async, py::arg("dram_dev_ptr"), py::arg("indices_ptr"),
+             py::arg("num_blocks"), py::arg("block_size"), py::arg("remote_host_id"), py::arg("remote_addr"),
+             "Paged PUT: the GPU holding the int64 indices gathers pool pages and writes them to the remote range "
+             "in one launch per chunk of pages (fused PXN gather + forward).")
         .def("mp_replicate_async", &C::mp_replicate_async, py::arg("comm_type"), py::arg("host_list"),
              py::arg("local_addr"), py::arg("remote_addrs"), py::arg("lengths"))
         .def("is_transfer_complete", &C::is_transfer_complete, py::arg("handle"))

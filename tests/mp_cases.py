@@ -18,6 +18,10 @@ non-zero on any mismatch.
           fused launch per chunk (bulk stores to each peer's published
           buffer), then to the other members' copies of an NVLS group
           (multicast stores); the kernel trace shows which launch ran.
+  engine_pxn  MPComm.put_pages_async: rank r gathers the pages rank
+          (r-1)%N wants from a host pool shared by all ranks and writes them
+          into that rank's published HBM buffer (fused PXN gather + forward as
+          an engine transfer).
 """
 import argparse
 import datetime
@@ -345,10 +349,54 @@ def case_engine_bcast(rank, world):
         print(f"engine_bcast case used: {used}", flush=True)
 
 
+def case_engine_pxn(rank, world):
+    bs, pages, n = 65536, 2048, 200
+    name = f"mpcomm-test-epxn-{os.environ.get('MASTER_PORT', '0')}"
+    if rank == 0:
+        pool = parallel.SharedHostPool(name, pages * bs, create=True)
+        g = torch.Generator().manual_seed(21)
+        pool.tensor.copy_(torch.randint(0, 256, (pages * bs,), dtype=torch.uint8, generator=g))
+    dist.barrier()
+    if rank != 0:
+        pool = parallel.SharedHostPool(name, pages * bs, create=False)
+    dist.barrier()
+    requester = (rank - 1) % world
+    wants = [torch.randperm(pages, generator=torch.Generator().manual_seed(30 + r))[:n] for r in range(world)]
+    idx = wants[requester].cuda()
+    inbox = torch.zeros(n * bs, dtype=torch.uint8, device="cuda")
+    comm = mpcomm.MPComm()
+    assert comm.init(f"p{rank}") == 0 and comm.start_accept_thread() == 0
+    dram = comm.map_dram_to_gpu(pool.tensor.data_ptr(), pages * bs)
+    assert dram
+    assert comm.register_memory(inbox.data_ptr(), inbox.numel()) == 0
+    assert comm.publish_buffer(inbox.data_ptr(), inbox.numel()) == 0
+    ports = [None] * world
+    dist.all_gather_object(ports, comm.get_tcp_port())
+    dist.barrier()
+    host = f"p{requester}"
+    assert comm.connect(host, "127.0.0.1", ports[requester]) == 0
+    info = comm.query_remote_buffers(host, "127.0.0.1", ports[requester])
+    raddr = info["buffers"][0]["addr"]
+    h = comm.put_pages_async(dram, idx.data_ptr(), n, bs, host, raddr)
+    assert h != mpcomm.INVALID_TRANSFER_HANDLE
+    assert comm.wait_transfer(h, 60000) == 0, "paged PUT failed"
+    res = comm.get_transfer_result(h)
+    comm.release_transfer(h)
+    assert res["bytes_transferred"] == n * bs
+    dist.barrier()  # every rank's pages have landed
+    assert torch.equal(inbox.view(n, bs).cpu(), pool.tensor.view(pages, bs)[wants[rank]]), "paged PUT mismatch"
+    dist.barrier()
+    comm.unmap_dram_from_gpu(pool.tensor.data_ptr())
+    comm.shutdown()
+    dist.barrier()
+    pool.close(unlink=(rank == 0))
+
+
 def main():
     os.environ.setdefault("MPCOMM_KERNEL_TRACE", "4096")
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=["putget", "pxn", "nvls", "gather_bcast", "peer_exit", "engine_bcast", "all"])
+    p.add_argument("case", choices=["putget", "pxn", "nvls", "gather_bcast", "peer_exit", "engine_bcast", "engine_pxn",
+                                      "all"])
     a = p.parse_args()
     rank, world, _ = parallel.init_from_env("gloo")
     if a.case == "peer_exit":
@@ -358,7 +406,8 @@ def main():
         if rank == 0:
             print("case peer_exit ok", flush=True)
         os._exit(0)
-    cases = ["putget", "pxn", "nvls", "gather_bcast", "engine_bcast"] if a.case == "all" else [a.case]
+    cases = (["putget", "pxn", "nvls", "gather_bcast", "engine_bcast", "engine_pxn"] if a.case == "all"
+             else [a.case])
     for c in cases:
         globals()[f"case_{c}"](rank, world)
         if rank == 0:

@@ -18,7 +18,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("case", ["putget", "pxn", "nvls", "gather_bcast", "peer_exit", "engine_bcast"])
+@pytest.mark.parametrize("case", ["putget", "pxn", "nvls", "gather_bcast", "peer_exit", "engine_bcast",
+                                  "engine_pxn"])
 def test_multigpu_case(case):
     n = torch.cuda.device_count()
     if n < 2:
