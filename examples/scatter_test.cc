@@ -16,6 +16,10 @@
 // --json prints one JSON line per test.
 // GB/s = bytes / 1e9 / wall seconds of the timed iterations (as the reference).
 // --gpu N puts the local (and served) buffers in HBM of GPU N (cudaMalloc).
+// --verify fills the local buffer with seeded bytes and, after the tests,
+// reads every target slot the last put/scatter/broadcast test wrote back
+// with GETs and compares it byte for byte (the reference harness verifies
+// by read-back the same way).
 #include <cuda_runtime.h>
 #include <unistd.h>
 
@@ -86,7 +90,7 @@ void usage(const char *prog) {
         "          [--target ID:ADDR:PORT]... [--size S] [--buffer-size S] [--batch-size B]\n"
         "          [--iterations N] [--warmup W] [--test-type put,get,scatter,gather,broadcast]\n"
         "          [--gpu N] [--wait-go-file PATH] [--ready-file PATH] [--hold-file PATH]\n"
-        "          [--hold-timeout S] [--done-file PATH] [--json] [--verbose]\n"
+        "          [--hold-timeout S] [--done-file PATH] [--json] [--verify] [--verbose]\n"
         "Sizes take K/M/G/T suffixes. Fabric: MPCOMM_FABRIC (auto|nvl|ib|sock|lo).\n",
         prog);
 }
@@ -97,7 +101,7 @@ int main(int argc, char **argv) {
     std::string mode = "initiator", host_id = "test:0", devices, tests = "put,get", go_file, ready_file, hold_file, done_file;
     int tcp_port = 0, iters = 10, warmup = 3, gpu = -1, hold_timeout = 600;
     size_t size = 1ull << 30, buf_size = 0, batch = 4;
-    bool verbose = false, json = false;
+    bool verbose = false, json = false, verify = false;
     std::vector<Target> targets;
     for (int i = 1; i < argc; ++i) {
         std::string a = argv[i];
@@ -123,6 +127,7 @@ int main(int argc, char **argv) {
         else if (a == "--done-file") done_file = next();
         else if (a == "--hold-timeout") hold_timeout = std::atoi(next().c_str());
         else if (a == "--json") json = true;
+        else if (a == "--verify") verify = true;
         else if (a == "--verbose" || a == "-v") verbose = true;
         else if (a == "--help" || a == "-h") return usage(argv[0]), 0;
         else return usage(argv[0]), 2;
@@ -194,6 +199,18 @@ int main(int argc, char **argv) {
     void *local = alloc_buf(local_bytes, gpu);
     if (!local || comm.registerMemory(local, local_bytes)) return std::fprintf(stderr, "local buffer failed\n"), 1;
     const uintptr_t lp = reinterpret_cast<uintptr_t>(local);
+    std::vector<unsigned char> pattern;
+    if (verify) {
+        pattern.resize(local_bytes);
+        std::mt19937_64 rng(0x5CA77E5ull);
+        for (size_t i = 0; i + 8 <= local_bytes; i += 8) {
+            const uint64_t v = rng();
+            std::memcpy(&pattern[i], &v, 8);
+        }
+        if (gpu >= 0) cudaMemcpy(local, pattern.data(), local_bytes, cudaMemcpyHostToDevice);
+        else std::memcpy(local, pattern.data(), local_bytes);
+    }
+    std::string last_write;
 
     for (const std::string &tt : split(tests, ',')) {
         auto one_round = [&]() -> int {
@@ -234,6 +251,7 @@ int main(int argc, char **argv) {
         };
         for (int w = 0; w < warmup; ++w)
             if (one_round()) return std::fprintf(stderr, "%s warm-up failed\n", tt.c_str()), 1;
+        const uint64_t launches0 = mpcomm::MPComm::getKernelLaunchCount();
         auto t0 = std::chrono::steady_clock::now();
         for (int i = 0; i < iters; ++i)
             if (one_round()) return std::fprintf(stderr, "%s failed\n", tt.c_str()), 1;
@@ -241,12 +259,42 @@ int main(int argc, char **argv) {
         const double bytes = static_cast<double>(size) * batch * targets.size() * iters;
         std::printf("--- %s Summary: size=%zu batch=%zu targets=%zu iters=%d  %.3f GB/s  (%.3f ms/round)\n",
                     tt.c_str(), size, batch, targets.size(), iters, bytes / 1e9 / s, s * 1e3 / iters);
+        const uint64_t launches = mpcomm::MPComm::getKernelLaunchCount() - launches0;
         if (json)
             std::printf("{\"tool\": \"scatter_test\", \"host\": \"%s\", \"test\": \"%s\", \"size\": %zu, "
-                        "\"batch\": %zu, \"targets\": %zu, \"iters\": %d, \"gbps\": %.4f, \"ms_per_round\": %.4f}\n",
+                        "\"batch\": %zu, \"targets\": %zu, \"iters\": %d, \"gbps\": %.4f, \"ms_per_round\": %.4f, "
+                        "\"kernel_launches\": %llu}\n",
                         host_id.c_str(), tt.c_str(), size, batch, targets.size(), iters, bytes / 1e9 / s,
-                        s * 1e3 / iters);
+                        s * 1e3 / iters, static_cast<unsigned long long>(launches));
         std::fflush(stdout);
+        if (tt == "put" || tt == "scatter" || tt == "broadcast") last_write = tt;
+    }
+    if (verify && !last_write.empty()) {
+        // Read every written slot back and compare with what was sent.
+        void *scratch = alloc_buf(size, gpu);
+        if (!scratch || comm.registerMemory(scratch, size)) return std::fprintf(stderr, "verify buffer failed\n"), 1;
+        std::vector<unsigned char> got(size);
+        size_t bad = 0;
+        for (size_t t = 0; t < targets.size(); ++t) {
+            for (size_t b = 0; b < batch; ++b) {
+                const size_t src_off = last_write == "broadcast" ? b * size : (t * batch + b) * size;
+                mpcomm::TransferHandle h =
+                    comm.getAsync(reinterpret_cast<uintptr_t>(scratch), targets[t].id, remote[t] + b * size, size);
+                if (h == mpcomm::INVALID_TRANSFER_HANDLE || comm.waitTransfer(h, 600000))
+                    return std::fprintf(stderr, "verify read-back failed\n"), 1;
+                comm.releaseTransfer(h);
+                if (gpu >= 0) cudaMemcpy(got.data(), scratch, size, cudaMemcpyDeviceToHost);
+                else std::memcpy(got.data(), scratch, size);
+                if (std::memcmp(got.data(), &pattern[src_off], size) != 0) ++bad;
+            }
+        }
+        std::printf("[scatter_test] verify %s: %zu of %zu slots differ\n", last_write.c_str(), bad,
+                    targets.size() * batch);
+        if (json)
+            std::printf("{\"tool\": \"scatter_test\", \"verify\": \"%s\", \"slots\": %zu, \"bad\": %zu}\n",
+                        last_write.c_str(), targets.size() * batch, bad);
+        std::fflush(stdout);
+        if (bad) return 1;
     }
     if (!done_file.empty())
         if (FILE *f = std::fopen(done_file.c_str(), "w")) std::fclose(f);

@@ -137,7 +137,8 @@ def _fill_kv_pool(view: torch.Tensor, dev, seed: int = 0) -> None:
     torch.cuda.synchronize()
 
 
-def pxn_forward(dev, pool_pages: int = 65536, request: int = 1024, warmup: int = 3, iters: int = 10) -> dict:
+def pxn_forward(comm, fstream: torch.cuda.Stream, dev, pool_pages: int = 65536, request: int = 1024,
+                warmup: int = 3, iters: int = 10) -> dict:
     rank, world = dist.get_rank(), dist.get_world_size()
     bs = LLAMA3_8B_KV.page_bytes
     name = f"mpcomm-bench-pxn-{os.environ.get('MASTER_PORT', '0')}"
@@ -177,6 +178,37 @@ def pxn_forward(dev, pool_pages: int = 65536, request: int = 1024, warmup: int =
     torch.cuda.synchronize()
     crc_ok = _all_true(torch.equal(got, exp) and status.item() == 0, dev)
 
+    # The same forward through the public engine API: put_pages_async on the
+    # GPU holding the indices, into the requester's published buffer (one
+    # fused launch per chunk of pages, tracked by a handle). Each proxy's
+    # transfer completes once its pages have landed, so the max over ranks
+    # of the per-rank device time is the delivery time.
+    dram = comm.map_dram_to_gpu(pool.tensor.data_ptr(), nbytes)
+    assert dram
+    inbox = torch.zeros(request * bs, dtype=torch.uint8, device=dev)
+    assert comm.register_memory(inbox.data_ptr(), inbox.numel()) == 0
+    assert comm.publish_buffer(inbox.data_ptr(), inbox.numel()) == 0
+    ports = [None] * world
+    dist.all_gather_object(ports, comm.get_tcp_port())
+    dist.barrier()
+    assert comm.connect("pxnreq", "127.0.0.1", ports[requester]) == 0
+    info = comm.query_remote_buffers("pxnreq", "127.0.0.1", ports[requester])
+    raddr = next(b["addr"] for b in info["buffers"] if b["length"] == request * bs and b["gpu_device_id"] >= 0)
+    dist.barrier()
+
+    def engine_step(_seq: int):
+        h = comm.put_pages_async(dram, fwd_idx.data_ptr(), request, bs, "pxnreq", raddr)
+        assert h != mpcomm.INVALID_TRANSFER_HANDLE
+        assert comm.wait_transfer(h, 60000) == 0, "paged PUT failed"
+        comm.release_transfer(h)
+
+    engine_ms = _timed(engine_step, fstream, warmup, iters, dev)
+    engine_ok = _all_true(torch.equal(ops.crc32_blocks(inbox, request), exp), dev)
+    dist.barrier()
+    comm.unpublish_buffer(inbox.data_ptr())
+    comm.unregister_memory(inbox.data_ptr())
+    comm.unmap_dram_from_gpu(pool.tensor.data_ptr())
+
     # Unfused two step (the reference's shape: gather into the proxy's own
     # HBM, then a separate peer copy into the requester's buffer; here both
     # steps are this library's kernels).
@@ -211,15 +243,19 @@ def pxn_forward(dev, pool_pages: int = 65536, request: int = 1024, warmup: int =
         "pxn_roofline_gbs": round(roof, 3),
         "pxn_roofline_frac": round(gbs / roof, 4),
         "pxn_two_step_gbs": round(total / (two_ms * 1e-3) / 1e9, 3),
+        "pxn_engine_gbs": round(total / (engine_ms * 1e-3) / 1e9, 3),
+        "pxn_engine_roofline_frac": round(total / (engine_ms * 1e-3) / 1e9 / roof, 4),
+        "pxn_engine_crc_ok": engine_ok,
         "pxn_crc_ok": crc_ok,
         "pxn_gpu_launches": int(launches),
         "pxn_what": f"{request} x 64 KiB KV pages per rank (seed 3+rank) from a {nbytes >> 30} GiB shared host pool, "
-                    f"gathered by rank (r+1)%N and stored into rank r's HBM by one kernel; roofline = copy-engine "
-                    f"H2D of the same bytes on every rank at once",
+                    f"gathered by rank (r+1)%N and stored into rank r's HBM by one kernel (pxn_*: the kernel "
+                    f"with a device flag; pxn_engine_*: MPComm.put_pages_async, one launch per 32 MiB of pages); "
+                    f"roofline = copy-engine H2D of the same bytes on every rank at once",
     }
 
 
-def gather_bcast_rollout(dev, warmup: int = 3, iters: int = 20) -> dict:
+def gather_bcast_rollout(comm, fstream: torch.cuda.Stream, dev, warmup: int = 3, iters: int = 20) -> dict:
     rank, world = dist.get_rank(), dist.get_world_size()
     raw, ids, lens = RolloutBatch().make(seed=4)
     pad = (-raw.numel()) % PAGE
@@ -273,6 +309,47 @@ def gather_bcast_rollout(dev, warmup: int = 3, iters: int = 20) -> dict:
     torch.cuda.synchronize()
     crc_ok = _all_true(torch.equal(got, exp_crc) and status.item() == 0, dev)
 
+    # The same broadcast through the public engine API: rank 0's
+    # broadcast_async from its pinned batch to every other rank's copy (the
+    # NVLS group's copies, registered as its members, or plain published
+    # buffers): one fused launch per chunk. Its transfer completes when the
+    # bytes have landed everywhere, so rank 0's device time is the delivery.
+    dest = grp.uc if grp is not None else bufs.local
+    dest.zero_()
+    if grp is not None:
+        grp.register(comm)
+    else:
+        assert comm.register_memory(dest.data_ptr(), dest.numel()) == 0
+    assert comm.publish_buffer(dest.data_ptr(), dest.numel(), 11) == 0
+    if rank == 0:
+        assert comm.register_memory(host.data_ptr(), nbytes) == 0
+    ports = [None] * world
+    dist.all_gather_object(ports, comm.get_tcp_port())
+    dests = [None] * world
+    dist.all_gather_object(dests, dest.data_ptr())
+    dist.barrier()
+    hosts = [f"bc{r}" for r in range(1, world)]
+    if rank == 0:
+        for r in range(1, world):
+            assert comm.connect(f"bc{r}", "127.0.0.1", ports[r]) == 0
+            assert comm.query_remote_buffers(f"bc{r}", "127.0.0.1", ports[r])
+    dist.barrier()
+
+    def engine_step(_seq: int):
+        if rank == 0:
+            h = comm.broadcast_async(host.data_ptr(), nbytes, hosts, dests[1:])
+            assert h != mpcomm.INVALID_TRANSFER_HANDLE
+            assert comm.wait_transfer(h, 60000) == 0, "engine broadcast failed"
+            comm.release_transfer(h)
+
+    engine_ms = _timed(engine_step, fstream, warmup, iters, dev)
+    engine_ok = _all_true(rank == 0 or torch.equal(ops.crc32_blocks(dest[:nbytes], pages), exp_crc), dev)
+    dist.barrier()
+    comm.unpublish_buffer(dest.data_ptr())
+    comm.unregister_memory(dest.data_ptr())
+    if rank == 0:
+        comm.unregister_memory(host.data_ptr())
+
     # Library comparator: H2D copy of the batch into rank 0's HBM, then NCCL
     # broadcast to every rank.
     staged = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -314,12 +391,16 @@ def gather_bcast_rollout(dev, warmup: int = 3, iters: int = 20) -> dict:
         "gather_bcast_roofline_ms": round(roof_ms, 4),
         "gather_bcast_roofline_frac": round(roof_ms / ms, 4),
         "gather_bcast_crc_ok": crc_ok,
+        "gather_bcast_engine_ms": round(engine_ms, 4),
+        "gather_bcast_engine_roofline_frac": round(roof_ms / engine_ms, 4),
+        "gather_bcast_engine_crc_ok": engine_ok,
         "gather_bcast_gpu_launches": int(launches),
         "bcast_nccl_ms": round(nccl_ms, 4),
         "bcast_ce_h2d_gbs": round(nbytes / (ce_ms * 1e-3) / 1e9, 3),
         "gather_bcast_what": "rollout batch (1,048,576 x 8 int32 expert IDs + 4,096 lognormal sequences, seed 4) "
                              "in rank 0's pinned DRAM, one gather_bcast launch to every GPU, device completion "
-                             "flag on each; roofline = max(copy-engine H2D of the batch, NVLink bytes / 770 GB/s); "
+                             "flag on each (gather_bcast_engine_*: MPComm.broadcast_async from rank 0, one fused launch "
+                             "per 32 MiB chunk); roofline = max(copy-engine H2D of the batch, NVLink bytes / 770 GB/s); "
                              "comparator bcast_nccl_ms = copy-engine H2D + NCCL broadcast",
     })
     return res
@@ -330,6 +411,6 @@ def run(comm, src: torch.Tensor, dst: torch.Tensor, block: int, batch: int, fstr
     dev = src.device
     out = {}
     out.update(nvlink_putget(comm, src, dst, block, batch, fstream))
-    out.update(pxn_forward(dev))
-    out.update(gather_bcast_rollout(dev))
+    out.update(pxn_forward(comm, fstream, dev))
+    out.update(gather_bcast_rollout(comm, fstream, dev))
     return out

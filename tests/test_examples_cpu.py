@@ -29,5 +29,15 @@ def test_scatter_test_both_mode():
         assert f"--- {t} Summary" in out
 
 
+def test_scatter_test_verify_reads_back_every_slot():
+    """--verify: after a broadcast (and after a put) every written slot is
+    read back with GETs and compared byte for byte."""
+    for t in ("put", "broadcast"):
+        out = _run([os.path.join(ROOT, "examples", "bin", "scatter_test"), "--mode", "both", "--size", "1M",
+                    "--batch-size", "3", "--iterations", "2", "--warmup", "1", "--test-type", t, "--verify",
+                    "--json"])
+        assert f"verify {t}: 0 of 3 slots differ" in out, out
+
+
 def test_check_install():
     assert "install check PASSED" in _run([sys.executable, "-m", "mpcomm.check_install"])

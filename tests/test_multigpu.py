@@ -1,9 +1,11 @@
 """Multi-GPU cases (cross-process NVLink PUT/GET, PXN forward, NVLS) under
 torch.distributed.run; skipped on hosts with fewer than 2 GPUs."""
+import json
 import os
 import socket
 import subprocess
 import sys
+import time
 
 import pytest
 import torch
@@ -80,3 +82,48 @@ print("pxn rails ok", len(busy))
                        text=True, cwd=ROOT, env=dict(os.environ, MPCOMM_LOG_LEVEL="1"))
     assert r.returncode == 0, f"{r.stdout[-3000:]}\n{r.stderr[-3000:]}"
     assert "pxn rails ok" in r.stdout
+
+
+def test_scatter_test_broadcast_across_gpus(tmp_path):
+    """The C++ API end to end: scatter_test serves a buffer in the HBM of
+    every GPU but 0; the initiator on GPU 0 broadcasts to all of them
+    (--test-type broadcast), reads every slot back and compares it
+    (--verify). Each request of 2 chunks is 2 fused launches whatever the
+    number of targets."""
+    n = min(torch.cuda.device_count(), 8)
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    exe = os.path.join(ROOT, "examples", "bin", "scatter_test")
+    env = dict(os.environ, MPCOMM_LOG_LEVEL="1", MPCOMM_NVL_CHUNK_SIZE=str(16 << 20))
+    procs, targets = [], []
+    try:
+        for r in range(1, n):
+            ready = tmp_path / f"t{r}.ready"
+            procs.append(subprocess.Popen([exe, "--mode", "target", "--host-id", f"t{r}", "--gpu", str(r),
+                                           "--buffer-size", "64M", "--ready-file", str(ready)],
+                                          stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL, env=env))
+        deadline = time.time() + 60
+        for r in range(1, n):
+            ready = tmp_path / f"t{r}.ready"
+            while not ready.exists():
+                assert time.time() < deadline, f"target {r} not ready"
+                assert procs[r - 1].poll() is None, f"target {r} exited"
+                time.sleep(0.1)
+            targets += ["--target", f"t{r}:127.0.0.1:{int(ready.read_text().split()[0])}"]
+        r = subprocess.run(["timeout", "-k", "10", "240", exe, "--gpu", "0", *targets, "--size", "32M",
+                            "--batch-size", "2", "--iterations", "2", "--warmup", "1", "--test-type", "broadcast",
+                            "--verify", "--json"], capture_output=True, text=True, env=env, cwd=ROOT)
+        assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+        lines = [json.loads(x) for x in r.stdout.splitlines() if x.startswith("{")]
+        bench = next(x for x in lines if x.get("test") == "broadcast")
+        check = next(x for x in lines if "verify" in x)
+        assert check["bad"] == 0 and check["slots"] == 2 * (n - 1)
+        assert bench["kernel_launches"] == 2 * 2 * 2, bench  # iterations x batch x chunks
+    finally:
+        for p in procs:
+            p.terminate()
+        for p in procs:
+            try:
+                p.wait(timeout=20)
+            except subprocess.TimeoutExpired:
+                p.kill()
