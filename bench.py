@@ -146,6 +146,10 @@ def reference_unavailable_reason() -> str:
 def main():
     args = parse()
     rank, world, local = rank_env()
+    if world > 1 and not args.no_extras:
+        # Device start/end of the broadcast launches measured after the
+        # headline (kernel trace ring; read once, outside every timed loop).
+        os.environ.setdefault("MPCOMM_KERNEL_TRACE", "4096")
     if args.impl == "reference":
         # Every rank reaches the same conclusion; rank 0 reports it.
         if rank == 0:

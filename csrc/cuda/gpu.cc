@@ -154,10 +154,48 @@ void device_free(void *p) {
     if (p) cudaFree(p);
 }
 
-int memset_device(void *p, int v, size_t bytes) { return cudaMemset(p, v, bytes); }
+namespace {
+
+// A non-blocking helper stream per device. The synchronous helpers below run
+// on it instead of the legacy default stream: work queued on the legacy
+// stream (for instance a wait on a collective that needs this very process
+// to answer a control message first) would otherwise hold them up.
+cudaStream_t helper_stream() {
+    static std::mutex mu;
+    static cudaStream_t streams[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> g(mu);
+    if (!streams[dev] && cudaStreamCreateWithFlags(&streams[dev], cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        streams[dev] = nullptr;
+    }
+    return streams[dev];
+}
+
+}  // namespace
+
+int memset_device(void *p, int v, size_t bytes) {
+    cudaStream_t s = helper_stream();
+    if (!s) return cudaMemset(p, v, bytes);
+    cudaError_t e = cudaMemsetAsync(p, v, bytes, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e;
+}
+
+int memset_device_async(void *p, int v, size_t bytes, void *stream) {
+    return cudaMemsetAsync(p, v, bytes, static_cast<cudaStream_t>(stream));
+}
 
 int copy_d2h_sync(void *dst, const void *src, size_t bytes) {
-    return cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost);
+    cudaStream_t s = helper_stream();
+    if (!s) return cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost);
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e;
 }
 
 int ipc_get_handle(void *base, unsigned char out[kIpcHandleBytes]) {

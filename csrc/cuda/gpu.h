@@ -45,7 +45,10 @@ void *host_alloc_mapped(size_t bytes);
 void host_free(void *p);
 void *device_alloc(size_t bytes);
 void device_free(void *p);
+// Synchronous memset / device-to-host copy on a non-blocking stream of the
+// current device (never queued behind work on the legacy default stream).
 int memset_device(void *p, int v, size_t bytes);
+int memset_device_async(void *p, int v, size_t bytes, void *stream);
 int copy_d2h_sync(void *dst, const void *src, size_t bytes);
 
 // CUDA IPC (legacy handles; device memory from cudaMalloc).

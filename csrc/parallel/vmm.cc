@@ -194,5 +194,53 @@ int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size
     return 0;
 }
 
+int gdr_alloc(int dev, size_t size, void **ptr, size_t *alloc_size) {
+    auto gran = sym<CUresult (*)(size_t *, const CUmemAllocationProp *, CUmemAllocationGranularity_flags)>(
+        "cuMemGetAllocationGranularity");
+    auto create = sym<CUresult (*)(CUmemGenericAllocationHandle *, size_t, const CUmemAllocationProp *,
+                                   unsigned long long)>("cuMemCreate");
+    auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
+    if (!gran || !create || !rel) return kNoDriver;
+    if (size == 0) return CUDA_ERROR_INVALID_VALUE;
+    CUmemAllocationProp p;
+    std::memset(&p, 0, sizeof(p));
+    p.type = CU_MEM_ALLOCATION_TYPE_PINNED;
+    p.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+    p.location.id = dev;
+    p.allocFlags.gpuDirectRDMACapable = 1;
+    size_t g = 0;
+    CUresult r = gran(&g, &p, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED);
+    if (r != CUDA_SUCCESS) return r;
+    if (g == 0) g = 2u << 20;
+    const size_t n = (size + g - 1) / g * g;
+    CUmemGenericAllocationHandle h = 0;
+    r = create(&h, n, &p, 0);
+    if (r != CUDA_SUCCESS) return r;
+    // The mapping holds a reference; the creation handle is released now,
+    // so unmapping frees the memory.
+    const int e = map_rw(h, n, dev, ptr);
+    rel(h);
+    if (e) return e;
+    *alloc_size = n;
+    return 0;
+}
+
+int gdr_free(void *ptr, size_t alloc_size) {
+    auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
+    auto vfree = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree");
+    if (!unmap || !vfree) return kNoDriver;
+    if (!ptr) return 0;
+    CUresult r = unmap(reinterpret_cast<CUdeviceptr>(ptr), alloc_size);
+    if (r != CUDA_SUCCESS) return r;
+    return vfree(reinterpret_cast<CUdeviceptr>(ptr), alloc_size);
+}
+
+int dmabuf_export(const void *ptr, size_t size, unsigned long long flags, int *fd) {
+    auto fn = sym<CUresult (*)(void *, CUdeviceptr, size_t, CUmemRangeHandleType, unsigned long long)>(
+        "cuMemGetHandleForAddressRange");
+    if (!fn) return kNoDriver;
+    return fn(fd, reinterpret_cast<CUdeviceptr>(ptr), size, CU_MEM_RANGE_HANDLE_TYPE_DMA_BUF_FD, flags);
+}
+
 }  // namespace vmm
 }  // namespace mpcomm

@@ -41,6 +41,16 @@ int multicast_map(uint64_t mc, size_t size, int dev, void **mc_va);
 // Unmaps/unbinds/releases everything created above (any argument may be 0).
 int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev);
 
+// HBM that a NIC can register through dma-buf (GPUDirect RDMA): a VMM
+// allocation of `dev` created with the gpuDirectRDMACapable flag, `size`
+// rounded up to the allocation granularity (*alloc_size), mapped read-write
+// for `dev`. Registering it with the ib fabric exports it as a dma-buf.
+int gdr_alloc(int dev, size_t size, void **ptr, size_t *alloc_size);
+int gdr_free(void *ptr, size_t alloc_size);
+// Exports [ptr, ptr + size) as a dma-buf file descriptor
+// (cuMemGetHandleForAddressRange, DMA_BUF_FD; flags as the driver's).
+int dmabuf_export(const void *ptr, size_t size, unsigned long long flags, int *fd);
+
 }  // namespace vmm
 }  // namespace mpcomm
 

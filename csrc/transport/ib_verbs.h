@@ -83,6 +83,13 @@ struct Sge {
     uint32_t lkey;
 };
 
+struct RdmaWr {  // the `rdma` member of ibv_send_wr's wr union, padded to the union's 32 bytes
+    uint64_t remote_addr;
+    uint32_t rkey;
+    uint32_t pad_rdma;
+    uint64_t pad_atomic[2];
+};
+
 struct SendWr {
     uint64_t wr_id;
     SendWr *next;
@@ -91,12 +98,7 @@ struct SendWr {
     uint32_t opcode;
     uint32_t send_flags;
     uint32_t imm_data;
-    struct {
-        uint64_t remote_addr;
-        uint32_t rkey;
-        uint32_t pad_rdma;
-        uint64_t pad_atomic[2];
-    } wr;
+    RdmaWr wr;
     uint32_t qp_type_xrc;
     uint32_t pad0;
     unsigned char tail[64];  // bind_mw / tso union
@@ -220,6 +222,55 @@ struct Api {
     int (*modify_qp)(Qp *, QpAttr *, int);
     int (*destroy_qp)(Qp *);
 };
+
+// Layout checks against rdma-core's infiniband/verbs.h on LP64 (x86-64 and
+// aarch64 Linux): the size and the offset of every field this library reads
+// or writes. Structs this library allocates (SendWr, QpInitAttr, QpAttr,
+// PortAttr) may be larger than the real ones; providers read only the real
+// fields.
+static_assert(offsetof(Context, ops) == 8, "ibv_context.ops");
+static_assert(sizeof(Context::ops) == 32 * sizeof(void *), "ibv_context_ops has 32 slots");
+static_assert(offsetof(Cq, context) == 0, "ibv_cq.context");
+static_assert(offsetof(Mr, addr) == 16 && offsetof(Mr, length) == 24, "ibv_mr.addr/length");
+static_assert(offsetof(Mr, handle) == 32 && offsetof(Mr, lkey) == 36 && offsetof(Mr, rkey) == 40, "ibv_mr keys");
+static_assert(sizeof(Mr) == 48, "ibv_mr size");
+static_assert(offsetof(Qp, send_cq) == 24 && offsetof(Qp, srq) == 40, "ibv_qp queues");
+static_assert(offsetof(Qp, handle) == 48 && offsetof(Qp, qp_num) == 52, "ibv_qp.qp_num");
+static_assert(offsetof(Qp, state) == 56 && offsetof(Qp, qp_type) == 60, "ibv_qp.state/qp_type");
+static_assert(sizeof(Gid) == 16, "ibv_gid size");
+static_assert(offsetof(Wc, status) == 8 && offsetof(Wc, opcode) == 12, "ibv_wc.status/opcode");
+static_assert(offsetof(Wc, byte_len) == 20 && offsetof(Wc, qp_num) == 28, "ibv_wc.byte_len/qp_num");
+static_assert(offsetof(Wc, wc_flags) == 36 && offsetof(Wc, pkey_index) == 40, "ibv_wc.wc_flags");
+static_assert(offsetof(Wc, sl) == 44 && offsetof(Wc, dlid_path_bits) == 45, "ibv_wc tail");
+static_assert(sizeof(Sge) == 16 && offsetof(Sge, length) == 8 && offsetof(Sge, lkey) == 12, "ibv_sge");
+static_assert(offsetof(SendWr, next) == 8 && offsetof(SendWr, sg_list) == 16, "ibv_send_wr list");
+static_assert(offsetof(SendWr, num_sge) == 24 && offsetof(SendWr, opcode) == 28, "ibv_send_wr.opcode");
+static_assert(offsetof(SendWr, send_flags) == 32 && offsetof(SendWr, imm_data) == 36, "ibv_send_wr flags");
+static_assert(offsetof(SendWr, wr) == 40 && sizeof(RdmaWr) == 32, "ibv_send_wr.wr union");
+static_assert(offsetof(RdmaWr, rkey) == 8, "ibv_send_wr.wr.rdma.rkey");
+static_assert(offsetof(SendWr, qp_type_xrc) == 72 && offsetof(SendWr, tail) == 80, "ibv_send_wr.qp_type");
+static_assert(sizeof(SendWr) >= 128, "ibv_send_wr size (bind_mw member is 48 bytes)");
+static_assert(sizeof(QpCap) == 20, "ibv_qp_cap size");
+static_assert(offsetof(QpInitAttr, send_cq) == 8 && offsetof(QpInitAttr, srq) == 24, "ibv_qp_init_attr queues");
+static_assert(offsetof(QpInitAttr, cap) == 32 && offsetof(QpInitAttr, qp_type) == 52, "ibv_qp_init_attr.cap");
+static_assert(offsetof(QpInitAttr, sq_sig_all) == 56 && sizeof(QpInitAttr) >= 64, "ibv_qp_init_attr size");
+static_assert(sizeof(GlobalRoute) == 24 && offsetof(GlobalRoute, flow_label) == 16, "ibv_global_route");
+static_assert(offsetof(GlobalRoute, sgid_index) == 20 && offsetof(GlobalRoute, traffic_class) == 22,
+              "ibv_global_route.traffic_class");
+static_assert(offsetof(AhAttr, dlid) == 24 && offsetof(AhAttr, is_global) == 29 && offsetof(AhAttr, port_num) == 30,
+              "ibv_ah_attr fields");
+static_assert(offsetof(QpAttr, path_mtu) == 8 && offsetof(QpAttr, rq_psn) == 20, "ibv_qp_attr psn");
+static_assert(offsetof(QpAttr, sq_psn) == 24 && offsetof(QpAttr, dest_qp_num) == 28, "ibv_qp_attr.dest_qp_num");
+static_assert(offsetof(QpAttr, qp_access_flags) == 32 && offsetof(QpAttr, cap) == 36, "ibv_qp_attr.cap");
+static_assert(offsetof(QpAttr, alt_ah_attr) == 88, "ibv_qp_attr.alt_ah_attr");
+static_assert(offsetof(QpAttr, max_rd_atomic) == 126 && offsetof(QpAttr, max_dest_rd_atomic) == 127,
+              "ibv_qp_attr rd_atomic");
+static_assert(offsetof(QpAttr, min_rnr_timer) == 128 && offsetof(QpAttr, port_num) == 129, "ibv_qp_attr.port");
+static_assert(offsetof(QpAttr, timeout) == 130 && offsetof(QpAttr, retry_cnt) == 131 &&
+                  offsetof(QpAttr, rnr_retry) == 132, "ibv_qp_attr retries");
+static_assert(offsetof(QpAttr, rate_limit) == 136 && sizeof(QpAttr) >= 144, "ibv_qp_attr size");
+static_assert(offsetof(PortAttr, gid_tbl_len) == 12 && offsetof(PortAttr, lid) == 34, "ibv_port_attr.lid");
+static_assert(offsetof(PortAttr, active_mtu) == 8 && offsetof(PortAttr, link_layer) == 46, "ibv_port_attr.link_layer");
 
 // Loads libibverbs once; nullptr if unavailable. MPCOMM_IBVERBS_LIB
 // overrides the library path (tests load a fake provider through it).

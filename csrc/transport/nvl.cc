@@ -603,10 +603,38 @@ class NvlRail final : public Rail {
         if (numa_ < 0) numa_ = 0;
         pci_path_ = topo::pci_realpath(bdf);
         sms_ = kern::sm_count(dev);
+        std::lock_guard<std::mutex> g(words_mu_);
+        grow_words();
     }
     ~NvlRail() override {
         std::lock_guard<std::mutex> g(mu_);
         for (void *e : free_events_) gpu::event_destroy(e);
+        const int prev = gpu::current_device();
+        gpu::set_device(dev_);
+        for (auto &sl : word_slabs_) {
+            gpu::device_free(sl.first);
+            gpu::host_free(sl.second);
+        }
+        if (prev >= 0) gpu::set_device(prev);
+    }
+
+    // Status words (device) and completion words (host-mapped) of this
+    // rail's QPs, 64 bytes each, carved from slabs allocated when the rail
+    // opens. A QP is created on the accept thread while the process's own
+    // device work may be queued behind a collective that waits for this very
+    // handshake; taking a slot makes no allocation call there that could
+    // wait on the device (cudaMalloc/cudaFree can).
+    bool take_words(uint32_t **status, uint64_t **done) {
+        std::lock_guard<std::mutex> g(words_mu_);
+        if (free_words_.empty() && !grow_words()) return false;
+        *status = free_words_.back().first;
+        *done = free_words_.back().second;
+        free_words_.pop_back();
+        return true;
+    }
+    void give_words(uint32_t *status, uint64_t *done) {
+        std::lock_guard<std::mutex> g(words_mu_);
+        free_words_.emplace_back(status, done);
     }
     const std::string &name() const override { return name_; }
     std::string gid() const override { return gid_; }
@@ -711,16 +739,47 @@ class NvlRail final : public Rail {
     uint32_t next_qpn_ = 1;
     std::vector<NvlQp *> qps_;
     std::vector<void *> free_events_;
+
+    static constexpr size_t kWordSlots = 256;  // QPs per slab
+    bool grow_words() {  // caller holds words_mu_
+        const int prev = gpu::current_device();
+        gpu::set_device(dev_);
+        auto *d = static_cast<char *>(gpu::device_alloc(kWordSlots * 64));
+        auto *h = static_cast<char *>(gpu::host_alloc_mapped(kWordSlots * 64));
+        bool ok = d && h && gpu::memset_device(d, 0, kWordSlots * 64) == 0;
+        if (prev >= 0) gpu::set_device(prev);
+        if (!ok) {
+            gpu::device_free(d);
+            gpu::host_free(h);
+            return false;
+        }
+        std::memset(h, 0, kWordSlots * 64);
+        word_slabs_.emplace_back(d, h);
+        for (size_t i = kWordSlots; i-- > 0;)
+            free_words_.emplace_back(reinterpret_cast<uint32_t *>(d + i * 64), reinterpret_cast<uint64_t *>(h + i * 64));
+        return true;
+    }
+    std::mutex words_mu_;
+    std::vector<std::pair<char *, char *>> word_slabs_;
+    std::vector<std::pair<uint32_t *, uint64_t *>> free_words_;
 };
 
 NvlQp::NvlQp(NvlRail *rail, uint32_t qpn) : rail_(rail), qpn_(qpn) {
     stream_ = gpu::stream_create(rail_->dev_);
+    if (!rail_->take_words(&status_, &done_word_)) {
+        status_ = nullptr;
+        done_word_ = nullptr;
+        return;
+    }
+    // A recycled slot starts from zero: the status word and last-CTA
+    // counter on the device (zeroed on this QP's own non-blocking stream,
+    // which then drains, so launches on any stream see it), the completion
+    // word on the host.
     int prev = gpu::current_device();
     gpu::set_device(rail_->dev_);
-    status_ = static_cast<uint32_t *>(gpu::device_alloc(64));
-    if (status_) gpu::memset_device(status_, 0, 64);
-    done_word_ = static_cast<uint64_t *>(gpu::host_alloc_mapped(64));
+    if (stream_ && gpu::memset_device_async(status_, 0, 64, stream_) == 0) gpu::stream_sync(stream_);
     if (prev >= 0) gpu::set_device(prev);
+    __atomic_store_n(done_word_, 0ull, __ATOMIC_RELEASE);
 }
 
 NvlQp::~NvlQp() {
@@ -737,8 +796,7 @@ NvlQp::~NvlQp() {
     }
     rail_->forget(this);
     gpu::stream_destroy(stream_);
-    gpu::device_free(status_);
-    gpu::host_free(done_word_);
+    if (status_) rail_->give_words(status_, done_word_);
 }
 
 int NvlQp::to_rtr(const EndpointInfo &remote) {

@@ -54,6 +54,26 @@ def _all_true(ok: bool, dev) -> bool:
     return bool(t.item())
 
 
+_host_barrier_seq = [0]
+
+
+def _host_barrier(timeout_s: float = 300.0) -> None:
+    """Barrier through the process group's TCP store: no device work, so a
+    rank waiting here leaves its GPU streams free while a peer's control-plane
+    handshake (connect, buffer query) reaches this process."""
+    import time
+
+    store = dist.distributed_c10d._get_default_store()
+    _host_barrier_seq[0] += 1
+    key = f"mpcomm-bench-barrier-{_host_barrier_seq[0]}"
+    store.add(key, 1)
+    deadline = time.time() + timeout_s
+    while store.add(key, 0) < dist.get_world_size():
+        if time.time() > deadline:
+            raise TimeoutError(f"host barrier {key} timed out")
+        time.sleep(0.002)
+
+
 def _timed(step: Callable[[int], None], stream: torch.cuda.Stream, warmup: int, iters: int, dev,
            seq0: int = 0) -> float:
     """Mean device ms of one step on this rank's stream, max over ranks."""
@@ -83,12 +103,12 @@ def nvlink_putget(comm, src: torch.Tensor, dst: torch.Tensor, block: int, batch:
     assert comm.publish_buffer(target.data_ptr(), total) == 0
     ports = [None] * world
     dist.all_gather_object(ports, comm.get_tcp_port())
-    dist.barrier()
+    _host_barrier()
     peer = rank ^ 1
     assert comm.connect("nvpeer", "127.0.0.1", ports[peer]) == 0
     info = comm.query_remote_buffers("nvpeer", "127.0.0.1", ports[peer])
     raddr = next(b["addr"] for b in info["buffers"] if b["gpu_device_id"] >= 0 and b["length"] == total)
-    dist.barrier()
+    _host_barrier()
     sp, dp = src.data_ptr(), dst.data_ptr()
 
     def phase(put: bool):
@@ -190,11 +210,11 @@ def pxn_forward(comm, fstream: torch.cuda.Stream, dev, pool_pages: int = 65536, 
     assert comm.publish_buffer(inbox.data_ptr(), inbox.numel()) == 0
     ports = [None] * world
     dist.all_gather_object(ports, comm.get_tcp_port())
-    dist.barrier()
+    _host_barrier()
     assert comm.connect("pxnreq", "127.0.0.1", ports[requester]) == 0
     info = comm.query_remote_buffers("pxnreq", "127.0.0.1", ports[requester])
     raddr = next(b["addr"] for b in info["buffers"] if b["length"] == request * bs and b["gpu_device_id"] >= 0)
-    dist.barrier()
+    _host_barrier()
 
     def engine_step(_seq: int):
         h = comm.put_pages_async(dram, fwd_idx.data_ptr(), request, bs, "pxnreq", raddr)
@@ -327,13 +347,13 @@ def gather_bcast_rollout(comm, fstream: torch.cuda.Stream, dev, warmup: int = 3,
     dist.all_gather_object(ports, comm.get_tcp_port())
     dests = [None] * world
     dist.all_gather_object(dests, dest.data_ptr())
-    dist.barrier()
+    _host_barrier()
     hosts = [f"bc{r}" for r in range(1, world)]
     if rank == 0:
         for r in range(1, world):
             assert comm.connect(f"bc{r}", "127.0.0.1", ports[r]) == 0
             assert comm.query_remote_buffers(f"bc{r}", "127.0.0.1", ports[r])
-    dist.barrier()
+    _host_barrier()
 
     def engine_step(_seq: int):
         if rank == 0:
@@ -406,6 +426,98 @@ def gather_bcast_rollout(comm, fstream: torch.cuda.Stream, dev, warmup: int = 3,
     return res
 
 
+def hbm_broadcast(dev, warmup: int = 3, iters: int = 20) -> dict:
+    """Broadcast of the rollout batch already in rank 0's HBM to every rank:
+    this library's all-source NVLS broadcast (every rank loads its 1/N slice
+    from rank 0 over NVLink and multicasts it) and single-source NVLS
+    broadcast, against NCCL's broadcast of the same buffer. Every iteration
+    ends with the same one-element NCCL all-reduce as a delivery barrier
+    (data is complete on every rank only once every rank's launch is done);
+    kernel_us is the device duration of the broadcast launch alone (trace
+    ring, slowest rank)."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    raw, _, _ = RolloutBatch().make(seed=4)
+    nbytes = raw.numel() - raw.numel() % 4096
+    src = parallel.PeerBuffers(nbytes)
+    if rank == 0:
+        src.local.copy_(raw[:nbytes].to(dev))
+    exp = ops.crc32_blocks(raw[:nbytes].to(dev), nbytes // 4096)
+    stream = torch.cuda.Stream(device=dev)
+    sync = torch.zeros(1, device=dev)
+    recv = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    res = {}
+    try:
+        grp: Optional[parallel.NvlsGroup] = parallel.NvlsGroup(nbytes)
+    except RuntimeError as e:
+        grp = None
+        res["hbm_bcast_nvls"] = f"unavailable: {e}"
+
+    def with_barrier(fn):
+        def step(_seq):
+            fn()
+            with torch.cuda.stream(stream):
+                dist.all_reduce(sync)
+        return step
+
+    def kernel_us():
+        d = sorted(r["duration_us"] for r in mpcomm._native.kernel_trace() if r["kind"] == "nvls_broadcast")
+        return _all_max(d[len(d) // 2] if d else 0.0, dev)
+
+    barrier_ms = _timed(with_barrier(lambda: None), stream, warmup, iters, dev)
+    tracing = mpcomm._native.kernel_trace_slots() > 0
+    if grp is not None:
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        if tracing:
+            mpcomm._native.kernel_trace_reset()
+        pull_ms = _timed(with_barrier(lambda: grp.broadcast_from(src.ptrs[0], nbytes, stream=stream)), stream,
+                         warmup, iters, dev)
+        pull_ok = _all_true(torch.equal(ops.crc32_blocks(grp.uc[:nbytes], nbytes // 4096), exp), dev)
+        res.update({"hbm_bcast_allsource_ms": round(pull_ms, 4), "hbm_bcast_allsource_crc_ok": pull_ok})
+        if tracing:
+            k = kernel_us()
+            res["hbm_bcast_allsource_kernel_us"] = round(k, 2)
+            res["hbm_bcast_allsource_kernel_frac"] = round(nbytes / (k * 1e-6) / 1e9 / NVLINK_GBS, 4)
+            mpcomm._native.kernel_trace_reset()
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        one_ms = _timed(with_barrier(lambda: rank == 0 and ops.nvls_broadcast(src.local, grp.mc_ptr, nbytes,
+                                                                               stream=stream)),
+                        stream, warmup, iters, dev)
+        one_ok = _all_true(torch.equal(ops.crc32_blocks(grp.uc[:nbytes], nbytes // 4096), exp), dev)
+        res.update({"hbm_bcast_onesource_ms": round(one_ms, 4), "hbm_bcast_onesource_crc_ok": one_ok})
+        if tracing:
+            k = kernel_us()
+            res["hbm_bcast_onesource_kernel_us"] = round(k, 2)
+            res["hbm_bcast_onesource_kernel_frac"] = round(nbytes / (k * 1e-6) / 1e9 / NVLINK_GBS, 4)
+    if rank == 0:
+        recv.copy_(src.local)
+
+    def nccl():
+        with torch.cuda.stream(stream):
+            dist.broadcast(recv, src=0)
+
+    nccl_ms = _timed(with_barrier(nccl), stream, warmup, iters, dev)
+    nccl_ok = _all_true(torch.equal(ops.crc32_blocks(recv, nbytes // 4096), exp), dev)
+    dist.barrier()
+    if grp is not None:
+        grp.close()
+    src.close()
+    res.update({
+        "hbm_bcast_bytes": nbytes,
+        "hbm_bcast_barrier_ms": round(barrier_ms, 4),
+        "hbm_bcast_nccl_ms": round(nccl_ms, 4),
+        "hbm_bcast_nccl_crc_ok": nccl_ok,
+        "hbm_bcast_what": "rollout batch in rank 0's HBM to every rank; each step = broadcast + one-element NCCL "
+                          "all-reduce (hbm_bcast_barrier_ms alone); allsource = NvlsGroup.broadcast_from, "
+                          "onesource = nvls_broadcast from rank 0, nccl = torch.distributed.broadcast; "
+                          "kernel_frac = bytes / kernel time / 770 GB/s",
+    })
+    return res
+
+
 def run(comm, src: torch.Tensor, dst: torch.Tensor, block: int, batch: int, fstream: torch.cuda.Stream) -> dict:
     """All inter-GPU paths; every rank calls it, rank 0 reports."""
     dev = src.device
@@ -413,4 +525,5 @@ def run(comm, src: torch.Tensor, dst: torch.Tensor, block: int, batch: int, fstr
     out.update(nvlink_putget(comm, src, dst, block, batch, fstream))
     out.update(pxn_forward(comm, fstream, dev))
     out.update(gather_bcast_rollout(comm, fstream, dev))
+    out.update(hbm_broadcast(dev))
     return out

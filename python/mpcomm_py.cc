@@ -6,6 +6,8 @@
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
+#include <unistd.h>
+
 #include <cstring>
 #include <string>
 #include <vector>
@@ -648,6 +650,28 @@ PYBIND11_MODULE(_mpcomm, m) {
         int e = vmm::multicast_map(mc, size, dev, &va);
         return py::make_tuple(e, reinterpret_cast<uintptr_t>(va));
     });
+    m.def(
+        "gdr_alloc",
+        [](int dev, size_t size) {
+            void *p = nullptr;
+            size_t n = 0;
+            int e = vmm::gdr_alloc(dev, size, &p, &n);
+            return py::make_tuple(e, reinterpret_cast<uintptr_t>(p), n);
+        },
+        py::arg("device"), py::arg("size"),
+        "(err, ptr, alloc_size): HBM created for GPUDirect RDMA (dma-buf exportable), mapped for `device`.");
+    m.def("gdr_free", [](uintptr_t p, size_t n) { return vmm::gdr_free(reinterpret_cast<void *>(p), n); },
+          py::arg("ptr"), py::arg("alloc_size"));
+    m.def(
+        "dmabuf_export_rc",
+        [](uintptr_t p, size_t n, unsigned long long flags) {
+            int fd = -1;
+            int e = vmm::dmabuf_export(reinterpret_cast<void *>(p), n, flags, &fd);
+            if (e == 0 && fd >= 0) ::close(fd);
+            return e;
+        },
+        py::arg("ptr"), py::arg("size"), py::arg("flags") = 0,
+        "Driver result of exporting [ptr, ptr+size) as a dma-buf (the fd is closed again).");
     m.def("multicast_teardown", [](uint64_t mc, uint64_t mem, uintptr_t uc, uintptr_t mcva, size_t size, int dev) {
         return vmm::multicast_teardown(mc, mem, reinterpret_cast<void *>(uc), reinterpret_cast<void *>(mcva), size,
                                        dev);

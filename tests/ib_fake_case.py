@@ -124,6 +124,31 @@ def main_gpu():
     a.release_transfer(h)
     torch.cuda.synchronize()
     assert torch.equal(dst[4096:], src[4096:]) and not dst[:4096].any(), "GET mismatch"
+    # HBM allocated for GPUDirect RDMA (VMM allocation with the
+    # gpuDirectRDMACapable flag): the driver's dma-buf export of it, and its
+    # registration + a PUT into it through the fake provider.
+    from mpcomm.parallel import device_view
+
+    err, gptr, gsize = mpcomm._native.gdr_alloc(0, n)
+    gdr = {"alloc_rc": err}
+    if err == 0:
+        gdr["export_rc"] = mpcomm._native.dmabuf_export_rc(gptr, gsize, 0)
+        gdr["export_pcie_rc"] = mpcomm._native.dmabuf_export_rc(gptr, gsize, 1)
+        before = lib.fake_ibv_dmabuf_registrations()
+        assert b.register_memory(gptr, n) == 0 and b.publish_buffer(gptr, n) == 0
+        gdr["dmabuf_registrations"] = lib.fake_ibv_dmabuf_registrations() - before
+        if gdr["export_rc"] == 0 or gdr["export_pcie_rc"] == 0:
+            assert gdr["dmabuf_registrations"] == len(b.get_active_devices()), gdr
+        assert a.query_remote_buffers("B", "127.0.0.1", port)
+        h = a.put_async(src.data_ptr(), "B", gptr, n)
+        assert a.wait_transfer(h, 20000) == 0, "PUT into GPUDirect HBM failed"
+        a.release_transfer(h)
+        torch.cuda.synchronize()
+        assert torch.equal(device_view(gptr, n), src), "PUT into GPUDirect HBM mismatch"
+        b.unpublish_buffer(gptr)
+        b.unregister_memory(gptr)
+        assert mpcomm._native.gdr_free(gptr, gsize) == 0
+    print(f"gdr: {gdr}", flush=True)
     a.shutdown()
     b.shutdown()
     print(f"ib fake ok (dma-buf registrations: {regs}, dma_buf_supported={sup.value}, export_rc={rc})",
