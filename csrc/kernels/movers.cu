@@ -424,6 +424,161 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     run_epilogue(ep);
 }
 
+// ---------------------------------------------------------------------------
+// Packed gather of small blocks (<= 4 KiB): a warp's stage holds up to 32
+// whole blocks of one tile, one per lane. Every lane issues the bulk load of
+// its own block into the stage (all completing on the stage's mbarrier, whose
+// expected byte count lane 0 sets first), and lane 0 writes the tile to the
+// contiguous output with ONE bulk store. A warp keeps STAGES x 32 blocks in
+// flight instead of STAGES, so a batch of small blocks is one wave of PCIe
+// reads rather than many.
+// ---------------------------------------------------------------------------
+struct PackedGather {
+    const char *pool;
+    const int64_t *idx;
+    char *out;
+    int64_t n, bs, pool_blocks;
+    int per;  // blocks per tile (<= 32, per * bs <= stage bytes)
+};
+
+// Warp copy of one landed block out of a shared-memory stage (16-byte
+// multiples, 16-byte aligned on both sides): shared-space loads, global
+// stores.
+__device__ __forceinline__ void warp_copy_from_stage(char *dst, const char *stage, uint32_t bytes) {
+    const int lane = threadIdx.x & 31;
+    for (uint32_t i = static_cast<uint32_t>(lane); i < (bytes >> 4); i += 32) {
+        int4 v;
+        asm volatile("ld.shared.v4.s32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(smem_u32(stage + (static_cast<size_t>(i) << 4))));
+        *reinterpret_cast<int4 *>(dst + (static_cast<size_t>(i) << 4)) = v;
+    }
+}
+
+template <int STAGES, uint32_t STAGE_BYTES>
+__device__ __forceinline__ void warp_packed_gather(const PackedGather &a, int64_t first, int64_t stride,
+                                                   char *stage_mem, uint64_t *bars, uint32_t *status,
+                                                   uint64_t budget) {
+    const int lane = threadIdx.x & 31;
+    const int64_t tiles = (a.n + a.per - 1) / a.per;
+    if (first >= tiles) return;
+    const int64_t n = (tiles - 1 - first) / stride + 1;
+    if (lane == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_proxy_async_smem();
+    }
+    __syncwarp();
+    // Lane-0 record of each stage: first block, block count, bad-index lanes.
+    int64_t st_b0[STAGES];
+    uint32_t st_cnt[STAGES], st_bad[STAGES];
+    int64_t issued = 0;
+    const uint32_t bs = static_cast<uint32_t>(a.bs);
+
+    auto issue = [&](int64_t j, int s) {  // warp-collective
+        const int64_t b0 = (first + j * stride) * a.per;
+        const int64_t left = a.n - b0;
+        const uint32_t cnt = static_cast<uint32_t>(left < a.per ? left : a.per);
+        int64_t p = -1;
+        bool valid = false;
+        if (static_cast<uint32_t>(lane) < cnt) {
+            p = __ldg(a.idx + b0 + lane);
+            valid = p >= 0 && (a.pool_blocks <= 0 || p < a.pool_blocks);
+        }
+        const uint32_t vmask = __ballot_sync(0xffffffffu, valid);
+        if (lane == 0) {
+            const uint32_t all = cnt >= 32 ? 0xffffffffu : ((1u << cnt) - 1u);
+            st_b0[s] = b0;
+            st_cnt[s] = cnt;
+            st_bad[s] = all & ~vmask;
+            mbar_arrive_expect_tx(&bars[s], static_cast<uint32_t>(__popc(vmask)) * bs);
+        }
+        __syncwarp();  // the expected byte count is set before any load lands
+        if (valid)
+            bulk_load(stage_mem + static_cast<size_t>(s) * STAGE_BYTES + static_cast<size_t>(lane) * bs,
+                      a.pool + p * a.bs, bs, &bars[s]);
+        ++issued;
+    };
+
+    const int64_t pro = n < STAGES ? n : STAGES;
+    for (int64_t j = 0; j < pro; ++j) issue(j, static_cast<int>(j));
+
+    int64_t j = 0;
+    bool aborted = false;
+    for (; j < n; ++j) {
+        const int s = static_cast<int>(j % STAGES);
+        const uint32_t parity = static_cast<uint32_t>((j / STAGES) & 1);
+        char *stage = stage_mem + static_cast<size_t>(s) * STAGE_BYTES;
+        int ok = 1;
+        uint32_t bad = 0, cnt = 0;
+        int64_t b0 = 0;
+        if (lane == 0) {
+            if (!mbar_wait_bounded(&bars[s], parity, budget)) {
+                ok = 0;
+                atomicOr(status, kStatusLoadTimeout);
+            } else {
+                bad = st_bad[s];
+                cnt = st_cnt[s];
+                b0 = st_b0[s];
+                if (!bad) bulk_store(a.out + b0 * a.bs, stage, cnt * bs);
+                else atomicOr(status, kStatusBadIndex);
+            }
+            bulk_commit();
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            aborted = true;
+            break;
+        }
+        bad = __shfl_sync(0xffffffffu, bad, 0);
+        if (bad) {
+            // Slow path: the valid blocks one by one (a bad index leaves its
+            // output block untouched, as in the tiled pipeline).
+            __syncwarp();  // lane 0 saw the stage land before the lanes read it
+            cnt = __shfl_sync(0xffffffffu, cnt, 0);
+            b0 = static_cast<int64_t>(__shfl_sync(0xffffffffu, static_cast<long long>(b0), 0));
+            for (uint32_t k = 0; k < cnt; ++k)
+                if (!((bad >> k) & 1u)) warp_copy_from_stage(a.out + (b0 + k) * a.bs, stage + k * bs, bs);
+            __syncwarp();
+            if (lane == 0) fence_proxy_async_smem();  // generic reads before the next async fill
+        }
+        if (j >= 1) {
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            const int64_t t = j - 1 + STAGES;
+            if (t < n) issue(t, static_cast<int>((j - 1) % STAGES));
+        }
+    }
+    if (lane == 0) {
+        if (aborted) {
+            for (int64_t t = j; t < issued; ++t) {
+                if (!mbar_wait_bounded(&bars[t % STAGES], static_cast<uint32_t>((t / STAGES) & 1), budget)) {
+                    atomicOr(status, kStatusDrainTimeout);
+                    break;
+                }
+            }
+        }
+        bulk_wait_all();
+    }
+    __syncwarp();
+}
+
+template <int WARPS, int STAGES, uint32_t STAGE_BYTES>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    packed_gather_kernel(const __grid_constant__ PackedGather a, uint32_t *status, uint64_t budget,
+                         const Epilogue ep) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int warp = threadIdx.x >> 5;
+    char *stage_mem = reinterpret_cast<char *>(smem_raw) + static_cast<size_t>(warp) * STAGES * STAGE_BYTES;
+    uint64_t *bars =
+        reinterpret_cast<uint64_t *>(smem_raw + static_cast<size_t>(WARPS) * STAGES * STAGE_BYTES) + warp * STAGES;
+    trace_begin(ep.stamp);
+    window_open(ep.win);
+    warp_packed_gather<STAGES, STAGE_BYTES>(a, static_cast<int64_t>(blockIdx.x) * WARPS + warp,
+                                            static_cast<int64_t>(gridDim.x) * WARPS, stage_mem, bars, status, budget);
+    trace_end(ep.stamp);
+    run_epilogue(ep);
+}
+
 template <class Src>
 __global__ void __launch_bounds__(kVecWarps * 32)
     vector_mover_kernel(const __grid_constant__ Src src, uint32_t *status, const Epilogue ep) {
@@ -504,6 +659,38 @@ int launch_vector(const Src &src, int64_t tiles, int max_ctas, cudaStream_t st, 
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Largest block the packed gather kernel takes (a stage holds >= 4 blocks).
+constexpr int64_t kPackedMaxBlock = kStageBytes / 4;
+
+int launch_packed_gather(const PackedGather &a, int max_ctas, cudaStream_t st, uint32_t *status,
+                         const Epilogue &ep, LaunchInfo *info) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::mutex mu;
+    static uint64_t configured = 0;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (dev < 64 && !(configured & (1ull << dev))) {
+            cudaError_t e = cudaFuncSetAttribute(packed_gather_kernel<kWarps, kStages, kStageBytes>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kBulkSmem));
+            if (e != cudaSuccess) return e;
+            configured |= 1ull << dev;
+        }
+    }
+    const int64_t tiles = (a.n + a.per - 1) / a.per;
+    const int cap = max_ctas > 0 ? max_ctas : sm_count(dev);
+    const int64_t need = (tiles + kWarps - 1) / kWarps;
+    int ctas = static_cast<int>(need < cap ? need : cap);
+    if (ctas < 1) ctas = 1;
+    if (!status) status = default_status_word(dev);
+    packed_gather_kernel<kWarps, kStages, kStageBytes><<<ctas, kWarps * 32, kBulkSmem, st>>>(a, status,
+                                                                                           wait_budget_ns(), ep);
+    note_launch();
+    if (info) *info = LaunchInfo{ctas, kWarps * 32, kBulkSmem, 3};
+    return cudaGetLastError();
+}
+
 // AUTO: the bulk pipeline needs 16-byte aligned spans; tiny blocks are
 // better served one warp per block.
 int pick_path(int mode, const void *a, const void *b, int64_t bs) {
@@ -523,6 +710,22 @@ int h2d_gather(const void *pool, int64_t pool_blocks, const int64_t *idx, void *
     const int path = pick_path(mode, pool, out, bs);
     if (path < 0) return cudaErrorMisalignedAddress;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Packed kernel: small blocks on the bulk path (TMA mode up to 4 KiB;
+    // AUTO from 1 KiB, below which the vector kernel measures faster).
+    const bool packed = path == 1 && bs <= kPackedMaxBlock && (mode == kModeTma || bs >= 1024);
+    if (packed) {
+        PackedGather a;
+        a.pool = static_cast<const char *>(pool);
+        a.idx = idx;
+        a.out = static_cast<char *>(out);
+        a.n = n;
+        a.bs = bs;
+        a.pool_blocks = pool_blocks;
+        a.per = static_cast<int>(std::min<int64_t>(32, kStageBytes / bs));
+        const Epilogue ep{window, window_ctr, nullptr, 0,
+                          trace_acquire("h2d_gather", static_cast<uint64_t>(n * bs))};
+        return launch_packed_gather(a, max_ctas, st, status, ep, info);
+    }
     GatherSrc src;
     src.pool = static_cast<const char *>(pool);
     src.idx = idx;
