@@ -5,6 +5,8 @@ per-kernel timing (single GPU, a few hundred MB at most).
 
 Cases (inputs larger than the 126 MB L2 where DRAM/PCIe traffic matters):
   gather_tma / gather_sm   1,024 x 64 KiB pages from a 2,048-page pinned pool
+  gather_1k                10,240 x 1 KiB blocks from a 40,960-block pinned pool
+                           (the packed small-block gather kernel)
   scatter_tma              the reverse
   copy_d2d                 GPU-fabric WR batch, 4 x 40 MiB HBM -> HBM
   copy_h2d                 GPU-fabric WR batch, 2 x 32 MiB pinned DRAM -> HBM
@@ -31,7 +33,7 @@ import mpcomm
 from mpcomm import ops
 
 PAGE = 65536
-ALL = ["gather_tma", "gather_sm", "scatter_tma", "copy_d2d", "copy_h2d", "crc32", "crc32_noalloc",
+ALL = ["gather_tma", "gather_sm", "gather_1k", "scatter_tma", "copy_d2d", "copy_h2d", "crc32", "crc32_noalloc",
        "pxn_local", "fanout_local", "gather_bcast_p2p", "nvls", "wait_flag"]
 
 
@@ -44,6 +46,9 @@ def build_cases():
     big2 = torch.empty_like(big)
     host = torch.randint(0, 256, (64 << 20,), dtype=torch.uint8, generator=g).pin_memory()
     crc_out = torch.empty(4, dtype=torch.int32, device="cuda")
+    pool1k = torch.randint(0, 256, (40960, 1024), dtype=torch.uint8, generator=g).pin_memory()
+    idx1k = torch.randperm(40960, generator=g)[:10240].cuda()
+    out1k = torch.empty((10240, 1024), dtype=torch.uint8, device="cuda")
     flag = torch.ones(1, dtype=torch.int64, device="cuda")
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
@@ -55,6 +60,7 @@ def build_cases():
     cases = {
         "gather_tma": (lambda: ops.paged_gather(pool, idx, out=out, mode=ops.MODE_TMA), nb),
         "gather_sm": (lambda: ops.paged_gather(pool, idx, out=out, mode=ops.MODE_SM), nb),
+        "gather_1k": (lambda: ops.paged_gather(pool1k, idx1k, out=out1k), 10240 * 1024),
         "scatter_tma": (lambda: ops.paged_scatter(out, idx, pool, mode=ops.MODE_TMA), nb),
         "copy_d2d": (lambda: ops.copy_spans([big.data_ptr() + i * q for i in range(4)],
                                             [big2.data_ptr() + i * q for i in range(4)], [q] * 4), 4 * q),
@@ -72,7 +78,7 @@ def build_cases():
                              512 * PAGE),
         "wait_flag": (lambda: ops.wait_flag(flag.data_ptr(), 1, 1_000_000, status.data_ptr()), 8),
     }
-    keep = (pool, idx, out, big, big2, host, crc_out, flag, status, ctr)
+    keep = (pool, idx, out, big, big2, host, crc_out, flag, status, ctr, pool1k, idx1k, out1k)
     return cases, keep
 
 
