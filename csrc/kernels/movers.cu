@@ -610,9 +610,11 @@ __global__ void __launch_bounds__(kVecWarps * 32)
 // ---------------------------------------------------------------------------
 namespace {
 
-template <class Src>
-int launch_bulk(const Src &src, int64_t tiles, int max_ctas, cudaStream_t st, uint32_t *status,
-                const Epilogue &ep, LaunchInfo *info) {
+template <int WARPS, int STAGES, uint32_t STAGE_BYTES, class Src>
+int launch_bulk_cfg(const Src &src, int64_t tiles, int max_ctas, cudaStream_t st, uint32_t *status,
+                    const Epilogue &ep, LaunchInfo *info) {
+    constexpr size_t smem = static_cast<size_t>(WARPS) * STAGES * STAGE_BYTES +
+                            static_cast<size_t>(WARPS) * STAGES * sizeof(uint64_t);
     int dev = 0;
     cudaGetDevice(&dev);
     static std::mutex mu;
@@ -620,24 +622,41 @@ int launch_bulk(const Src &src, int64_t tiles, int max_ctas, cudaStream_t st, ui
     {
         std::lock_guard<std::mutex> g(mu);
         if (dev < 64 && !(configured & (1ull << dev))) {
-            cudaError_t e = cudaFuncSetAttribute(
-                bulk_mover_kernel<kWarps, kStages, kStageBytes, Src>,
-                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kBulkSmem));
+            cudaError_t e = cudaFuncSetAttribute(bulk_mover_kernel<WARPS, STAGES, STAGE_BYTES, Src>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
             if (e != cudaSuccess) return e;
             configured |= 1ull << dev;
         }
     }
     const int sms = sm_count(dev);
     int cap = max_ctas > 0 ? max_ctas : sms;
-    int64_t need = (tiles + kWarps - 1) / kWarps;
+    int64_t need = (tiles + WARPS - 1) / WARPS;
     int ctas = static_cast<int>(need < cap ? need : cap);
     if (ctas < 1) ctas = 1;
     if (!status) status = default_status_word(dev);
-    bulk_mover_kernel<kWarps, kStages, kStageBytes, Src>
-        <<<ctas, kWarps * 32, kBulkSmem, st>>>(src, status, wait_budget_ns(), ep);
+    bulk_mover_kernel<WARPS, STAGES, STAGE_BYTES, Src><<<ctas, WARPS * 32, smem, st>>>(src, status,
+                                                                                       wait_budget_ns(), ep);
     note_launch();
-    if (info) *info = LaunchInfo{ctas, kWarps * 32, kBulkSmem, 1};
+    if (info) *info = LaunchInfo{ctas, WARPS * 32, smem, 1};
     return cudaGetLastError();
+}
+
+template <class Src>
+int launch_bulk(const Src &src, int64_t tiles, int max_ctas, cudaStream_t st, uint32_t *status,
+                const Epilogue &ep, LaunchInfo *info) {
+    return launch_bulk_cfg<kWarps, kStages, kStageBytes>(src, tiles, max_ctas, st, status, ep, info);
+}
+
+// Stage size of the fabric batch copies (MPCOMM_BULK_STAGE_KB = 16, 32 or
+// 64; the shared memory per CTA stays ~192 KiB: 4, 2 or 1 pipelines).
+uint32_t batch_stage_bytes() {
+    static const uint32_t v = [] {
+        const char *e = std::getenv("MPCOMM_BULK_STAGE_KB");
+        const long kb = e ? std::atol(e) : 16;
+        return static_cast<uint32_t>(kb == 32 || kb == 64 ? kb << 10 : kStageBytes);
+    }();
+    return v;
 }
 
 template <class Src>
@@ -769,7 +788,8 @@ int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_
     if (done_flag && !done_ctr) return cudaErrorInvalidValue;
     const bool vec = mode == kModeSm;
     BatchSrc src;
-    src.tile_bytes = vec ? kVecTileBytes : kStageBytes;
+    const uint32_t stage = batch_stage_bytes();
+    src.tile_bytes = vec ? kVecTileBytes : stage;
     src.gate = gate_budget_ns ? gate : nullptr;
     src.gate_budget = gate_budget_ns;
     int k = 0;
@@ -794,8 +814,10 @@ int copy_batch(const CopyDesc *descs, int n, int max_ctas, void *stream, uint32_
     for (int i = 0; i < n; ++i) total += descs[i].bytes;
     const Epilogue ep{nullptr, done_ctr, done_flag, done_value, trace_acquire("copy_batch", total)};
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return vec ? launch_vector(src, tiles, max_ctas, st, status, ep, info)
-               : launch_bulk(src, tiles, max_ctas, st, status, ep, info);
+    if (vec) return launch_vector(src, tiles, max_ctas, st, status, ep, info);
+    if (stage == 32768) return launch_bulk_cfg<2, kStages, 32768>(src, tiles, max_ctas, st, status, ep, info);
+    if (stage == 65536) return launch_bulk_cfg<1, kStages, 65536>(src, tiles, max_ctas, st, status, ep, info);
+    return launch_bulk(src, tiles, max_ctas, st, status, ep, info);
 }
 
 int pxn_gather_forward(const void *pool, int64_t pool_blocks, const int64_t *idx, void *dst,
