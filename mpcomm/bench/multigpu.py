@@ -480,6 +480,22 @@ def hbm_broadcast(dev, warmup: int = 3, iters: int = 20) -> dict:
             res["hbm_bcast_allsource_kernel_us"] = round(k, 2)
             res["hbm_bcast_allsource_kernel_frac"] = round(nbytes / (k * 1e-6) / 1e9 / NVLINK_GBS, 4)
             mpcomm._native.kernel_trace_reset()
+        # The same all-source broadcast with bulk copies of the slice into
+        # shared memory (gather_bcast) instead of per-thread loads.
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        bulk_ms = _timed(with_barrier(lambda: grp.broadcast_from(src.ptrs[0], nbytes, stream=stream,
+                                                                 method="bulk")), stream, warmup, iters, dev)
+        bulk_ok = _all_true(torch.equal(ops.crc32_blocks(grp.uc[:nbytes], nbytes // 4096), exp), dev)
+        res.update({"hbm_bcast_allsource_bulk_ms": round(bulk_ms, 4), "hbm_bcast_allsource_bulk_crc_ok": bulk_ok})
+        if tracing:
+            d = sorted(r["duration_us"] for r in mpcomm._native.kernel_trace() if r["kind"] == "gather_bcast_nvls")
+            k = _all_max(d[len(d) // 2] if d else 0.0, dev)
+            res["hbm_bcast_allsource_bulk_kernel_us"] = round(k, 2)
+            if k:
+                res["hbm_bcast_allsource_bulk_kernel_frac"] = round(nbytes / (k * 1e-6) / 1e9 / NVLINK_GBS, 4)
+            mpcomm._native.kernel_trace_reset()
         grp.uc.zero_()
         torch.cuda.synchronize()
         dist.barrier()

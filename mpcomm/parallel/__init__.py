@@ -229,7 +229,7 @@ class NvlsGroup:
         dist.barrier()
 
     def broadcast_from(self, root_ptr: int, nbytes: int, max_ctas: int = 0,
-                       stream: Optional[torch.cuda.Stream] = None) -> None:
+                       stream: Optional[torch.cuda.Stream] = None, method: str = "load") -> None:
         """All-source broadcast of ``nbytes`` that sit in the root's HBM at
         ``root_ptr`` (an address this rank can load from: the root's own
         pointer on the root, its CUDA-IPC mapping elsewhere, e.g.
@@ -241,6 +241,12 @@ class NvlsGroup:
         root issuing it alone (8 B200s: 104 us instead of 134 us for 57.9 MB).
         Completion is stream-ordered per rank; the data is complete on every
         rank once every rank's launch has finished (a barrier, or a flag).
+
+        ``method``: "load" reads the slice with 16-byte loads from every
+        thread (nvls_broadcast); "bulk" pulls it into shared memory with bulk
+        copies (cp.async.bulk, no multicast qualifier) and multicasts from
+        there (gather_bcast with one page), keeping more bytes in flight per
+        SM across NVLink.
         """
         if nbytes > self.size or nbytes % 16:
             raise ValueError("nbytes must be a multiple of 16 within the group's size")
@@ -250,9 +256,15 @@ class NvlsGroup:
         if ln == 0:
             return
         s = stream if stream is not None else torch.cuda.current_stream()
-        err = _native.nvls_broadcast(root_ptr + off, self.mc_ptr + off, ln, max_ctas, int(s.cuda_stream))
+        if method == "bulk":
+            if not hasattr(self, "_page0"):
+                self._page0 = torch.zeros(1, dtype=torch.int64, device="cuda")
+            err = _native.gather_bcast(root_ptr + off, 0, self._page0.data_ptr(), 1, ln, self.mc_ptr + off, [], 0, [],
+                                       1, 0, max_ctas, int(s.cuda_stream), 0)
+        else:
+            err = _native.nvls_broadcast(root_ptr + off, self.mc_ptr + off, ln, max_ctas, int(s.cuda_stream))
         if err:
-            raise RuntimeError(f"nvls_broadcast failed with CUDA error {err}")
+            raise RuntimeError(f"broadcast_from ({method}) failed with CUDA error {err}")
 
     def register(self, comm) -> None:
         """Registers this rank's copy with an ``MPComm`` (GPU fabric) as a

@@ -144,6 +144,15 @@ def case_nvls(rank, world):
         dist.barrier()
         assert torch.equal(grp.uc[:nbytes], torch.flip(src, [0])), "all-source NVLS broadcast mismatch"
         dist.barrier()
+        # The same with bulk copies of each slice into shared memory.
+        grp.uc.zero_()
+        torch.cuda.synchronize()
+        dist.barrier()
+        grp.broadcast_from(root.ptrs[0], nbytes, method="bulk")
+        torch.cuda.synchronize()
+        dist.barrier()
+        assert torch.equal(grp.uc[:nbytes], torch.flip(src, [0])), "all-source bulk NVLS broadcast mismatch"
+        dist.barrier()
         root.close()
         grp.close()
     bufs = parallel.PeerBuffers(nbytes)
