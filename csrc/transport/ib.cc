@@ -99,12 +99,55 @@ bool gid_zero(const ibv::Gid &g) {
 }
 
 using UdpSportFn = int (*)(ibv::Qp *, uint16_t);
-UdpSportFn udp_sport_fn() {
-    static UdpSportFn fn = [] {
-        void *h = dlopen("libmlx5.so.1", RTLD_NOW | RTLD_GLOBAL);
-        return h ? reinterpret_cast<UdpSportFn>(dlsym(h, "mlx5dv_modify_qp_udp_sport")) : nullptr;
+
+// UDP source port of a RoCE v2 QP (ECMP spreading across fabric paths),
+// set through the NIC vendor's direct-verbs call: mlx5dv_modify_qp_udp_sport
+// for mlx5 devices, bnxt_re_dv_modify_qp_udp_sport for Broadcom bnxt_re
+// devices (the reference calls one or the other depending on its build,
+// src/mpcomm.cpp:3954-3967). MPCOMM_IBV_DV_LIB names one library to look
+// both symbols up in instead of the vendors' own.
+UdpSportFn udp_sport_fn(const std::string &device) {
+    struct Fns {
+        UdpSportFn mlx5 = nullptr, bnxt = nullptr;
+    };
+    static const Fns fns = [] {
+        Fns f;
+        auto look = [](const char *lib, const char *sym) -> UdpSportFn {
+            void *h = dlopen(lib, RTLD_NOW | RTLD_GLOBAL);
+            return h ? reinterpret_cast<UdpSportFn>(dlsym(h, sym)) : nullptr;
+        };
+        const char *over = std::getenv("MPCOMM_IBV_DV_LIB");
+        if (over && *over) {
+            f.mlx5 = look(over, "mlx5dv_modify_qp_udp_sport");
+            f.bnxt = look(over, "bnxt_re_dv_modify_qp_udp_sport");
+            return f;
+        }
+        f.mlx5 = look("libmlx5.so.1", "mlx5dv_modify_qp_udp_sport");
+        for (const char *lib : {"libbnxt_re.so.1", "libbnxt_re.so", "libbnxt_re-rdmav34.so"})
+            if (!f.bnxt) f.bnxt = look(lib, "bnxt_re_dv_modify_qp_udp_sport");
+        return f;
     }();
-    return fn;
+    return device.compare(0, 7, "bnxt_re") == 0 ? fns.bnxt : fns.mlx5;
+}
+
+// Source port of the i-th QP: MPCOMM_UDP_SPORTS (comma list) cycled in QP
+// order, else spread over the dynamic range 49152-65535 by a multiplicative
+// hash so consecutive QPs land far apart.
+uint16_t udp_sport_for(uint32_t i) {
+    static const std::vector<uint16_t> list = [] {
+        std::vector<uint16_t> v;
+        const char *e = std::getenv("MPCOMM_UDP_SPORTS");
+        for (const char *p = e; p && *p;) {
+            char *end = nullptr;
+            const long x = std::strtol(p, &end, 10);
+            if (end == p) break;
+            if (x > 0 && x < 65536) v.push_back(static_cast<uint16_t>(x));
+            p = *end == ',' ? end + 1 : end;
+        }
+        return v;
+    }();
+    if (!list.empty()) return list[i % list.size()];
+    return static_cast<uint16_t>(49152 + (i * 40503u) % 16384);
 }
 
 class IbRail;
@@ -338,10 +381,10 @@ int IbQp::to_rts() {
                                ibv::kQpState | ibv::kQpTimeout | ibv::kQpRetryCnt | ibv::kQpRnrRetry |
                                    ibv::kQpSqPsn | ibv::kQpMaxQpRdAtomic))
         return MPCOMM_ERR_CONNECTION;
-    if (UdpSportFn fn = udp_sport_fn()) {
+    if (UdpSportFn fn = udp_sport_fn(rail_->name())) {
         static std::atomic<uint32_t> k{0};
-        const uint32_t i = k.fetch_add(1);
-        fn(qp_, static_cast<uint16_t>(49152 + (i * 40503u) % 16384));
+        if (fn(qp_, udp_sport_for(k.fetch_add(1))) != 0)
+            MPCOMM_LOG_DEBUG("MPComm[ib]: UDP source port not set on %s\n", rail_->name().c_str());
     }
     state_ = QpState::kRts;
     return 0;

@@ -23,7 +23,8 @@ def main():
     a, b = mpcomm.MPComm(), mpcomm.MPComm()
     assert a.init("A") == 0 and b.init("B") == 0
     assert a.get_fabric_name() == "ib", a.get_fabric_name()
-    assert a.get_active_devices() == ["mlx5_0", "mlx5_1"], a.get_active_devices()
+    prefix = os.environ.get("FAKE_IBV_DEVICE_PREFIX", "mlx5_")
+    assert a.get_active_devices() == [prefix + "0", prefix + "1"], a.get_active_devices()
     gid = a.get_gid(0)
     assert gid.startswith("fe:80:") and len(gid) == 47, gid
     t = ctypes.create_string_buffer(n)
@@ -55,9 +56,31 @@ def main():
     a.release_transfer(h)
     for i in range(3):
         assert t.raw[(2 - i) * seg:(3 - i) * seg] == s.raw[i * seg:(i + 1) * seg]
+    sport_check(a)
     a.shutdown()
     b.shutdown()
     print("ib fake ok", flush=True)
+
+
+def sport_check(comm):
+    """With MPCOMM_IBV_DV_LIB pointing at this provider, every RTS transition
+    set a UDP source port through the device vendor's call."""
+    want = os.environ.get("EXPECT_SPORT_VENDOR")
+    if not want:
+        return
+    lib = ctypes.CDLL(os.environ["MPCOMM_IBVERBS_LIB"])
+    calls = [lib.fake_ibv_sport_calls(0), lib.fake_ibv_sport_calls(1)]
+    vendor = {"mlx5": 0, "bnxt_re": 1}[want]
+    assert calls[vendor] > 0 and calls[1 - vendor] == 0, calls
+    ports = (ctypes.c_uint16 * 256)()
+    n = lib.fake_ibv_sports(ports, 256)
+    got = {ports[i] for i in range(min(n, 256))}
+    allowed = {int(x) for x in os.environ.get("MPCOMM_UDP_SPORTS", "").split(",") if x}
+    if allowed:
+        assert got <= allowed and len(got) == len(allowed), (got, allowed)
+    else:
+        assert all(49152 <= p <= 65535 for p in got) and len(got) > 1, got
+    print(f"sport calls {calls} ports {sorted(got)}", flush=True)
 
 
 def main_gpu():

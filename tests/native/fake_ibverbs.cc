@@ -16,6 +16,7 @@
 // system ABI.
 #include <cuda.h>
 #include <dlfcn.h>
+#include <cstdio>
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -64,6 +65,26 @@ struct FakeMr {
 
 std::mutex g_mu;
 FakeDevice g_devs[2] = {{"mlx5_0", 0}, {"mlx5_1", 1}};
+// FAKE_IBV_DEVICE_PREFIX renames the devices (e.g. "bnxt_re" -> bnxt_re0/1).
+void name_devices() {
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char *p = std::getenv("FAKE_IBV_DEVICE_PREFIX");
+        if (!p || !*p) return;
+        for (int i = 0; i < 2; ++i) std::snprintf(g_devs[i].name, sizeof(g_devs[i].name), "%s%d", p, i);
+    });
+}
+// Vendor UDP source-port calls (0 = mlx5dv, 1 = bnxt_re_dv) and their ports.
+std::atomic<int> g_sport_calls[2];
+std::mutex g_sport_mu;
+std::vector<uint16_t> g_sports;
+int record_sport(int vendor, Qp *qp, uint16_t port) {
+    if (!qp || port == 0) return 22;
+    g_sport_calls[vendor].fetch_add(1);
+    std::lock_guard<std::mutex> g(g_sport_mu);
+    g_sports.push_back(port);
+    return 0;
+}
 std::map<uint32_t, FakeQp *> g_qps;
 std::map<uint32_t, FakeMr *> g_mrs;  // key -> region (lkey == rkey)
 uint32_t g_next_qpn = 0x300, g_next_key = 0x4000;
@@ -190,6 +211,7 @@ int fake_poll_cq(Cq *cq, int n, Wc *wc) {
 extern "C" {
 
 Device **ibv_get_device_list(int *n) {
+    name_devices();
     Device **l = static_cast<Device **>(std::calloc(3, sizeof(Device *)));
     l[0] = reinterpret_cast<Device *>(&g_devs[0]);
     l[1] = reinterpret_cast<Device *>(&g_devs[1]);
@@ -277,6 +299,15 @@ Mr *ibv_reg_dmabuf_mr(Pd *pd, uint64_t offset, size_t len, uint64_t iova, int fd
     return &m->mr;
 }
 int fake_ibv_dmabuf_registrations() { return g_dmabuf_regs.load(); }
+int mlx5dv_modify_qp_udp_sport(Qp *qp, uint16_t port) { return record_sport(0, qp, port); }
+int bnxt_re_dv_modify_qp_udp_sport(Qp *qp, uint16_t port) { return record_sport(1, qp, port); }
+int fake_ibv_sport_calls(int vendor) { return vendor == 0 || vendor == 1 ? g_sport_calls[vendor].load() : -1; }
+// Copies up to `max` recorded ports into `out`; returns how many were recorded.
+int fake_ibv_sports(uint16_t *out, int max) {
+    std::lock_guard<std::mutex> g(g_sport_mu);
+    for (int i = 0; i < max && i < static_cast<int>(g_sports.size()); ++i) out[i] = g_sports[i];
+    return static_cast<int>(g_sports.size());
+}
 int ibv_dereg_mr(Mr *mr) {
     std::lock_guard<std::mutex> g(g_mu);
     g_mrs.erase(mr->lkey);

@@ -23,6 +23,20 @@ def test_ib_fabric_put_get_scatter():
     _run({})
 
 
+@pytest.mark.parametrize("vendor,ports", [("mlx5", ""), ("bnxt_re", "60000,60051,57663,57804")])
+def test_ib_udp_source_port_per_vendor(vendor, ports):
+    """RTS sets each QP's RoCE UDP source port through the device vendor's
+    direct-verbs call (mlx5dv or bnxt_re_dv): spread over the dynamic port
+    range by default, or cycled through MPCOMM_UDP_SPORTS."""
+    extra = {"MPCOMM_IBV_DV_LIB": LIB, "EXPECT_SPORT_VENDOR": vendor}
+    if vendor == "bnxt_re":
+        extra["FAKE_IBV_DEVICE_PREFIX"] = "bnxt_re"
+    if ports:
+        extra["MPCOMM_UDP_SPORTS"] = ports
+    r = _run(extra)
+    assert "sport calls" in r.stdout
+
+
 @pytest.mark.parametrize("mode", ["single_qp", "all_qp"])
 def test_ib_fault_injection_reposts_on_healthy_rail(mode):
     r = _run({"MPCOMM_FAULT_INJECT_AFTER_SEC": "0", "MPCOMM_FAULT_INJECT_NIC": "0",
