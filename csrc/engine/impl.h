@@ -265,6 +265,7 @@ class MPComm::Impl {
     int numaNodeForAddr(void *addr) const;
     std::vector<size_t> localNicsForNuma(int numa) const;
     int gpuNumaNode(int gpu) const;
+    std::vector<MPComm::PcieAffinityCheck> pcieAffinitySelfCheck() const;
     std::string fabricName() const { return fabric_name_; }
     const Config &config() const { return cfg_; }
     RailSlot *rail(size_t i) { return rails_[i].get(); }

@@ -293,14 +293,42 @@ void MPComm::Impl::discoverTopology() {
     }
     nic_topology_.clear();
     for (auto &r : rails_) nic_topology_.push_back(NicTopologyInfo{r->name, r->numa});
-    // Self-check table (reference :3192-3251): sysfs affinity vs the
-    // name-suffix heuristic (suffix N serves GPU N).
-    for (auto &r : rails_) {
-        int suffix = topo::name_suffix(r->name);
-        MPCOMM_LOG_DEBUG("MPComm: rail %-10s numa=%d gpu(sysfs)=%d gpu(suffix)=%d %s\n",
-                         r->name.c_str(), r->numa, r->gpu, suffix,
-                         (r->gpu < 0 || r->gpu == suffix) ? "ok" : "MISMATCH");
+    const auto rows = pcieAffinitySelfCheck();
+    if (rows.empty()) return;
+    size_t mismatches = 0;
+    MPCOMM_LOG_INFO("MPComm: GPU <-> rail PCIe affinity (sysfs, used for accounting) vs name-suffix heuristic:\n");
+    for (const auto &row : rows) {
+        std::string sys;
+        for (const auto &n : row.sysfs_rails) sys += (sys.empty() ? "" : ",") + n;
+        if (!row.agrees) ++mismatches;
+        MPCOMM_LOG_INFO("MPComm:   GPU%-2d sysfs=[%s] suffix=[%s] %s\n", row.gpu_device_id,
+                        sys.empty() ? "-" : sys.c_str(), row.suffix_rail.empty() ? "-" : row.suffix_rail.c_str(),
+                        row.agrees ? "match" : "MISMATCH");
     }
+    if (mismatches)
+        MPCOMM_LOG_INFO("MPComm:   %zu GPU(s) disagree with the suffix heuristic; accounting follows sysfs\n",
+                        mismatches);
+}
+
+std::vector<MPComm::PcieAffinityCheck> MPComm::Impl::pcieAffinitySelfCheck() const {
+    std::vector<MPComm::PcieAffinityCheck> out;
+    const int ngpu = gpu::device_count();
+    for (int g = 0; g < ngpu && g < static_cast<int>(kMaxGpuDomains); ++g) {
+        MPComm::PcieAffinityCheck row;
+        row.gpu_device_id = g;
+        const auto affine = affineRailsForGpu(g);
+        for (size_t r : affine) row.sysfs_rails.push_back(rails_[r]->name);
+        size_t heur = SIZE_MAX;
+        for (size_t r = 0; r < rails_.size(); ++r)
+            if (topo::name_suffix(rails_[r]->name) == g) {
+                heur = r;
+                break;
+            }
+        if (heur != SIZE_MAX) row.suffix_rail = rails_[heur]->name;
+        row.agrees = !affine.empty() && heur != SIZE_MAX && affine[0] == heur;
+        out.push_back(std::move(row));
+    }
+    return out;
 }
 
 void MPComm::Impl::writeConfigFile() const {

@@ -142,6 +142,9 @@ std::vector<MPComm::KernelTraceRecord> MPComm::getKernelTrace() {
     return out;
 }
 std::string MPComm::getFabricName() const { return impl_->fabricName(); }
+std::vector<MPComm::PcieAffinityCheck> MPComm::getPcieAffinitySelfCheck() const {
+    return impl_->pcieAffinitySelfCheck();
+}
 int MPComm::registerMulticastMemory(void *uc_addr, size_t length, void *mc_addr, uint64_t group_token,
                                     int group_size) {
     return impl_->registerMulticastMemory(uc_addr, length, mc_addr, group_token, group_size);

@@ -265,6 +265,19 @@ class MPComm {
     static const char *getQpsPerConnectionEnvVarName();
 
     // ---- topology ------------------------------------------------------
+    // GPU <-> rail PCIe affinity self-check (extension; the reference prints
+    // it at init, src/mpcomm.cpp:3192-3251): for every visible GPU, the
+    // rails sysfs places under the same PCIe switch (used for PCIe-domain
+    // accounting and rail choice) beside the rail the name-suffix heuristic
+    // would pick (suffix N serves GPU N), and whether they agree. Logged at
+    // INFO by init(); empty without GPUs.
+    struct PcieAffinityCheck {
+        int gpu_device_id;
+        std::vector<std::string> sysfs_rails;
+        std::string suffix_rail;  // empty when no rail has suffix N
+        bool agrees;
+    };
+    std::vector<PcieAffinityCheck> getPcieAffinitySelfCheck() const;
     const std::vector<NumaTopology> &getNumaTopology() const;
     const std::vector<NicTopologyInfo> &getNicTopology() const;
     int getNicNumaNode(const std::string &nic_name) const;

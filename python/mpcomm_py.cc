@@ -39,6 +39,18 @@ class PyMPComm {
         return c_.registerMemory(reinterpret_cast<void *>(a), l);
     }
     int unregister_memory(uintptr_t a) { return c_.unregisterMemory(reinterpret_cast<void *>(a)); }
+    py::list get_pcie_affinity_self_check() const {
+        py::list out;
+        for (const auto &r : c_.getPcieAffinitySelfCheck()) {
+            py::dict d;
+            d["gpu"] = r.gpu_device_id;
+            d["sysfs_rails"] = r.sysfs_rails;
+            d["suffix_rail"] = r.suffix_rail;
+            d["agrees"] = r.agrees;
+            out.append(d);
+        }
+        return out;
+    }
     int register_multicast_memory(uintptr_t uc, size_t l, uintptr_t mc, uint64_t token, int members) {
         py::gil_scoped_release r;
         return c_.registerMulticastMemory(reinterpret_cast<void *>(uc), l, reinterpret_cast<void *>(mc), token,
@@ -323,6 +335,8 @@ PYBIND11_MODULE(_mpcomm, m) {
         .def("shutdown", &C::shutdown)
         .def("register_memory", &C::register_memory, py::arg("addr"), py::arg("length"))
         .def("unregister_memory", &C::unregister_memory, py::arg("addr"))
+        .def("get_pcie_affinity_self_check", &C::get_pcie_affinity_self_check,
+             "Per GPU: rails under the same PCIe switch (sysfs) vs the name-suffix heuristic.")
         .def("register_multicast_memory", &C::register_multicast_memory, py::arg("uc_addr"), py::arg("length"),
              py::arg("mc_addr"), py::arg("group_token"), py::arg("group_size"),
              "Registers this process's copy of an NVLS multicast group buffer; broadcast_async to the group's "

@@ -139,6 +139,14 @@ def test_scatter_gather_broadcast(pair):
         assert t.bytes(i * seg, seg) == s.bytes(0, seg)
 
 
+def test_pcie_affinity_self_check_without_gpus(lo_env):
+    """The GPU <-> rail affinity table has a row per visible GPU; none here."""
+    c = mpcomm.MPComm()
+    assert c.init("aff") == 0
+    assert c.get_pcie_affinity_self_check() == []
+    c.shutdown()
+
+
 def test_staging_refuses_unmapped_local_range(pair):
     """An unregistered local range that is neither device memory nor mapped
     host memory is refused at submit (no handle, nothing touched)."""

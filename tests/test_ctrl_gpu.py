@@ -35,3 +35,17 @@ def test_connect_while_default_stream_is_busy(monkeypatch):
     torch.cuda.synchronize()
     c.shutdown()
     assert took < 1.0, f"connect waited {took:.2f} s behind the default stream"
+
+
+def test_pcie_affinity_self_check_gpu_fabric(monkeypatch):
+    """On the GPU fabric every rail is a GPU: the sysfs affinity of GPU g is
+    its own rail nvl_g, which the suffix heuristic also picks."""
+    monkeypatch.setenv("MPCOMM_LOG_LEVEL", "1")
+    c = mpcomm.MPComm()
+    assert c.init("affinity") == 0 and c.get_fabric_name() == "nvl"
+    rows = c.get_pcie_affinity_self_check()
+    assert len(rows) == torch.cuda.device_count()
+    row0 = rows[0]
+    assert row0["gpu"] == 0 and "nvl_0" in row0["sysfs_rails"], row0
+    assert row0["suffix_rail"] == "nvl_0" and row0["agrees"], row0
+    c.shutdown()
