@@ -419,7 +419,6 @@ void MPComm::Impl::workerLoop(Worker *w) {
 
 void MPComm::Impl::postFanoutChunks(Worker *w, Transfer *t, std::vector<fabric::QueuePair *> *touched) {
     const size_t total = t->plan.total();
-    const size_t r = t->fanout_rail;
     const size_t nh = t->hosts.size();
     std::vector<fabric::FanoutTarget> targets(nh);
     while (true) {
@@ -433,11 +432,33 @@ void MPComm::Impl::postFanoutChunks(Worker *w, Transfer *t, std::vector<fabric::
         } else {
             break;
         }
+        const size_t r = t->fanout_rail;
         if (rails_[r]->quarantined.load(std::memory_order_relaxed)) {
-            // A fused WRITE has no other rail that reaches every destination.
-            t->error.store(MPCOMM_ERR_TRANSFER);
-            t->aborted = true;
-            break;
+            // Move the rest of the broadcast to another healthy rail that
+            // reaches every destination in one operation (the re-post rule
+            // of plain WRs); fail only when there is none.
+            size_t alt = SIZE_MAX;
+            for (size_t c2 : t->candidates) {
+                if (c2 == r || rails_[c2]->quarantined.load(std::memory_order_relaxed) ||
+                    rails_[c2]->rail->max_fanout() < nh)
+                    continue;
+                bool all = true;
+                for (size_t i = 0; all && i < nh; ++i) all = t->conns[i]->group_for(c2) != nullptr;
+                if (all) {
+                    alt = c2;
+                    break;
+                }
+            }
+            if (alt == SIZE_MAX) {
+                t->error.store(MPCOMM_ERR_TRANSFER);
+                t->aborted = true;
+                break;
+            }
+            MPCOMM_LOG_WARN("MPComm: fused broadcast #%lu moves from %s to %s\n",
+                            static_cast<unsigned long>(t->handle), rails_[r]->name.c_str(),
+                            rails_[alt]->name.c_str());
+            t->fanout_rail = alt;
+            continue;
         }
         const Chunk c = t->plan.get(chunk);
         QpGroup *g0 = t->conns[0]->group_for(r);

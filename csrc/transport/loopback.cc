@@ -20,6 +20,7 @@
 #include <shared_mutex>
 #include <thread>
 #include <unordered_map>
+#include <vector>
 
 #include "mpcomm.h"
 #include "mpcomm_log.h"
@@ -53,6 +54,7 @@ struct Directory {
 struct PendingWr {
     WorkRequest wr;
     LoQp *qp;
+    std::vector<FanoutTarget> fan;  // one-to-many WRITE (empty: a plain WR)
 };
 
 class LoRail final : public Rail {
@@ -107,6 +109,8 @@ class LoRail final : public Rail {
     }
 
     std::unique_ptr<QueuePair> create_qp() override;
+    // One-to-many WRITEs: one completion after the bytes reached every target.
+    size_t max_fanout() const override { return 8; }
 
     int poll(WorkCompletion *out, int max) override {
         std::lock_guard<std::mutex> g(cqmu_);
@@ -121,7 +125,14 @@ class LoRail final : public Rail {
     void enqueue(const WorkRequest *wrs, size_t n, LoQp *qp) {
         {
             std::lock_guard<std::mutex> g(qmu_);
-            for (size_t i = 0; i < n; ++i) work_.push_back(PendingWr{wrs[i], qp});
+            for (size_t i = 0; i < n; ++i) work_.push_back(PendingWr{wrs[i], qp, {}});
+        }
+        qcv_.notify_one();
+    }
+    void enqueue_fanout(const WorkRequest &wr, const FanoutTarget *t, size_t n, LoQp *qp) {
+        {
+            std::lock_guard<std::mutex> g(qmu_);
+            work_.push_back(PendingWr{wr, qp, std::vector<FanoutTarget>(t, t + n)});
         }
         qcv_.notify_one();
     }
@@ -195,9 +206,21 @@ class LoQp final : public QueuePair {
         rail_->enqueue(wrs, n, this);
         return 0;
     }
+    int post_fanout(const WorkRequest &wr, const FanoutTarget *targets, size_t n, void *) override {
+        QpState s = state_.load();
+        if (s != QpState::kRts && s != QpState::kErr) return MPCOMM_ERR_CONNECTION;
+        if (n == 0 || n > 8 || wr.op != Opcode::kWrite) return MPCOMM_ERR_INVALID_ARG;
+        for (size_t i = 0; i < n; ++i) {
+            auto *q = dynamic_cast<LoQp *>(targets[i].qp);
+            if (!q || q->rail_ != rail_) return MPCOMM_ERR_INVALID_ARG;
+        }
+        rail_->enqueue_fanout(wr, targets, n, this);
+        return 0;
+    }
     const EndpointInfo &remote() const { return remote_; }
 
  private:
+    friend class LoRail;
     LoRail *rail_;
     uint32_t qpn_;
     std::atomic<QpState> state_{QpState::kReset};
@@ -245,6 +268,26 @@ void LoRail::run() {
         }
         if (!check(wr.lkey, wr.local_addr, wr.length)) {
             complete(wr.wr_id, kWcLocProtErr, 0);
+            continue;
+        }
+        if (!p.fan.empty()) {
+            int st = kWcSuccess;
+            for (const auto &t : p.fan) {
+                auto *q = static_cast<LoQp *>(t.qp);
+                LoRail *peer = nullptr;
+                {
+                    std::lock_guard<std::mutex> g(Directory::get().mu);
+                    auto it = Directory::get().rails.find(q->remote().gid);
+                    if (it != Directory::get().rails.end()) peer = it->second;
+                }
+                if (q->state() == QpState::kErr) st = kWcFlushErr;
+                else if (!peer || !peer->port_active()) st = kWcRetryExcErr;
+                else if (!peer->check(t.rkey, t.remote_addr, wr.length)) st = kWcRemAccessErr;
+                if (st != kWcSuccess) break;
+                std::memmove(reinterpret_cast<void *>(t.remote_addr), reinterpret_cast<const void *>(wr.local_addr),
+                             wr.length);
+            }
+            complete(wr.wr_id, st, st == kWcSuccess ? wr.length : 0);
             continue;
         }
         LoRail *peer = nullptr;

@@ -139,6 +139,38 @@ def test_scatter_gather_broadcast(pair):
         assert t.bytes(i * seg, seg) == s.bytes(0, seg)
 
 
+@pytest.mark.parametrize("fused", ["1", "0"])
+def test_broadcast_fused_and_per_destination(lo_env, monkeypatch, fused):
+    """broadcast_async gives the same bytes at every destination whether the
+    rail writes all of them in one operation per chunk (fused) or one WR per
+    destination; a rail that fails a fused chunk is quarantined and the rest
+    of the broadcast moves to a healthy rail."""
+    monkeypatch.setenv("MPCOMM_FUSED_BROADCAST", fused)
+    monkeypatch.setenv("MPCOMM_MAX_RDMA_TRANSFER_SIZE", str(64 << 10))
+    a, b = mpcomm.MPComm(), mpcomm.MPComm()
+    assert a.init("A") == 0 and b.init("B") == 0 and b.start_accept_thread() == 0
+    try:
+        seg, hosts = 300_000, 4
+        t = Buf(seg * hosts)
+        connect(a, b, t, seg * hosts)
+        s = Buf(seg, os.urandom(seg))
+        assert a.register_memory(s.ptr, seg) == 0
+        rails = a.get_active_devices()
+        # One completion error on every rail but the last.
+        for i in range(len(rails) - 1):
+            assert mpcomm._native._lo_inject_wc_errors(a.get_gid(i), 1) == 0
+        h = a.broadcast_async(s.ptr, seg, ["B"] * hosts, [t.ptr + i * seg for i in range(hosts)])
+        assert a.wait_transfer(h, 30000) == 0
+        r = a.get_transfer_result(h)
+        a.release_transfer(h)
+        assert r["bytes_transferred"] == seg * hosts
+        for i in range(hosts):
+            assert t.bytes(i * seg, seg) == s.bytes(), i
+    finally:
+        a.shutdown()
+        b.shutdown()
+
+
 def test_pcie_affinity_self_check_without_gpus(lo_env):
     """The GPU <-> rail affinity table has a row per visible GPU; none here."""
     c = mpcomm.MPComm()
