@@ -135,3 +135,38 @@ def test_peer_drops_mid_handshake(initiator):
     assert initiator.connect("flaky", "127.0.0.1", port) == int(mpcomm.MPCommError.ERR_CONNECTION)
     t.join(10)
     srv.close()
+
+
+HOST_BARRIER = r"""
+import os, sys, time
+import torch.distributed as dist
+sys.path.insert(0, os.environ["ROOT"])
+from mpcomm.bench.multigpu import _host_barrier
+dist.init_process_group("gloo")
+rank = dist.get_rank()
+if rank == 1:
+    time.sleep(1.0)  # arrives late
+t0 = time.time()
+_host_barrier(timeout_s=30)
+_host_barrier(timeout_s=30)
+waited = time.time() - t0
+print(f"rank {rank} waited {waited:.2f}", flush=True)
+assert rank == 1 or waited > 0.8, waited
+dist.destroy_process_group()
+"""
+
+
+def test_bench_host_barrier_two_ranks(tmp_path):
+    """The benchmark's store-based barrier (no device work) holds an early
+    rank until the late one arrives, call after call."""
+    script = tmp_path / "hb.py"
+    script.write_text(HOST_BARRIER)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, ROOT=ROOT, MPCOMM_LOG_LEVEL="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr=127.0.0.1", f"--master-port={port}", str(script)],
+                       capture_output=True, text=True, env=env, timeout=180)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert r.stdout.count("waited") == 2
