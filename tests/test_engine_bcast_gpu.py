@@ -124,3 +124,65 @@ def test_engine_paged_put_one_gpu():
                        cwd=ROOT, env=env)
     assert r.returncode == 0, f"{r.stdout[-3000:]}\n{r.stderr[-3000:]}"
     assert "paged put ok" in r.stdout
+
+
+MIXED = r"""
+import os, torch, mpcomm
+torch.cuda.set_device(0)
+n = 24 << 20
+src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+dsts = [torch.zeros(n, dtype=torch.uint8, device="cuda") for _ in range(3)]
+host = torch.zeros(n, dtype=torch.uint8).pin_memory()
+back = torch.zeros(n, dtype=torch.uint8, device="cuda")
+bs, pages, k = 16384, 8192, 4096
+pool = torch.randint(0, 256, (pages, bs), dtype=torch.uint8).pin_memory()
+idx_cpu = torch.randperm(pages, generator=torch.Generator().manual_seed(9))[:k]
+idx = idx_cpu.cuda()
+out = torch.empty(k * bs, dtype=torch.uint8, device="cuda")
+c = mpcomm.MPComm()
+assert c.init("mix") == 0 and c.start_accept_thread() == 0 and c.get_fabric_name() == "nvl"
+for t in [src, back, host] + dsts:
+    assert c.register_memory(t.data_ptr(), n) == 0
+for t in dsts + [host]:
+    assert c.publish_buffer(t.data_ptr(), n) == 0
+port = c.get_tcp_port()
+assert c.connect("self", "127.0.0.1", port) == 0 and c.query_remote_buffers("self", "127.0.0.1", port)
+dram = c.map_dram_to_gpu(pool.data_ptr(), pool.numel())
+assert dram
+c.enable_h2d_qos(0, 0)  # READ posts pause while an H2D window is open
+gs = torch.cuda.Stream()
+assert c.tma_gather(dram, idx.data_ptr(), out.data_ptr(), k, bs, 0, 0, gs.cuda_stream) == 0
+half = n // 2
+hs = [c.broadcast_async(src.data_ptr(), n, ["self"] * 3, [d.data_ptr() for d in dsts]),
+      c.scatter_async(src.data_ptr(), ["self", "self"], [host.data_ptr(), host.data_ptr() + half], [half, n - half])]
+for h in hs:
+    assert h != mpcomm.INVALID_TRANSFER_HANDLE
+    assert c.wait_transfer(h, 60000) == 0
+    c.release_transfer(h)
+h = c.get_async(back.data_ptr(), "self", host.data_ptr(), n)  # READ over PCIe, gated by the QoS engine
+assert c.wait_transfer(h, 60000) == 0
+c.release_transfer(h)
+torch.cuda.synchronize()
+for d in dsts:
+    assert torch.equal(d, src)
+assert torch.equal(host.cuda(), src) and torch.equal(back, src)
+assert torch.equal(out.view(k, bs).cpu(), pool[idx_cpu])
+w = c.get_last_h2d_window(0)
+assert w is not None and w["end_ns"] > w["begin_ns"] > 0, w
+c.disable_h2d_qos()
+c.unmap_dram_from_gpu(pool.data_ptr())
+c.shutdown()
+print("mixed ok")
+"""
+
+
+def test_broadcast_and_scatter_under_qos_window_with_pxn_rails():
+    """broadcast_async to three destinations and scatter_async to two, with
+    MPCOMM_PXN_ENABLE=1 (a rail per visible GPU) and H2D QoS on while a
+    tmaGather's window is open on the same GPU, then a GET the QoS engine
+    gates: every transfer completes bit-exact and the window is recorded."""
+    env = dict(os.environ, MPCOMM_PXN_ENABLE="1", MPCOMM_NVL_CHUNK_SIZE=str(4 << 20), MPCOMM_LOG_LEVEL="1")
+    r = subprocess.run(["timeout", "-k", "30", "240", sys.executable, "-c", MIXED], capture_output=True, text=True,
+                       cwd=ROOT, env=env)
+    assert r.returncode == 0, f"{r.stdout[-3000:]}\n{r.stderr[-3000:]}"
+    assert "mixed ok" in r.stdout
