@@ -316,6 +316,61 @@ def main():
         e2e = {"value": round(world * 2 * total / wall.item() / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": req_host.numel() * 8, "d2h_bytes_per_step": batch * 4}
 
+    # Paged KV gather / scatter on every rank at once:
+    # the 4 GiB host pool is 65,536 Llama-3-8B KV pages of 64 KiB; 4,096 of
+    # them (seed 1) are gathered into HBM with tmaGather and scattered back
+    # with tmaScatter (the same bytes, so the pool is unchanged), checked
+    # against torch indexing of the pool.
+    kv = {}
+    if not args.no_extras:
+        from mpcomm.models import LLAMA3_8B_KV
+
+        pbytes = LLAMA3_8B_KV.page_bytes
+        npages, nreq = total // pbytes, 4096
+        kv_idx_cpu = LLAMA3_8B_KV.sample_pages(npages, nreq, seed=1)
+        kv_idx = kv_idx_cpu.to(dev)
+        kv_out = torch.empty(nreq * pbytes, dtype=torch.uint8, device=dev)
+        dram = comm.map_dram_to_gpu(pp, total)
+        assert dram, "map_dram_to_gpu failed"
+        fs = fstream.cuda_stream
+        kv_ms = []
+        for gather in (True, False):
+            def one():
+                if gather:
+                    rc = comm.tma_gather(dram, kv_idx.data_ptr(), kv_out.data_ptr(), nreq, pbytes, 0, 0, fs)
+                else:
+                    rc = comm.tma_scatter(kv_out.data_ptr(), kv_idx.data_ptr(), dram, nreq, pbytes, 0, 0, fs)
+                assert rc == 0
+            for _ in range(2):
+                one()
+            torch.cuda.synchronize()
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(fstream)
+            for _ in range(5):
+                one()
+            b.record(fstream)
+            torch.cuda.synchronize()
+            t = torch.tensor([a.elapsed_time(b) / 5], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            kv_ms.append(t.item())
+        ok = torch.equal(kv_out.view(nreq, pbytes).cpu(), pool.view(npages, pbytes)[kv_idx_cpu])
+        okt = torch.tensor([1 if ok else 0], device=dev)
+        if world > 1:
+            dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+        comm.unmap_dram_from_gpu(pp)
+        kv_bytes = world * nreq * pbytes
+        kv = {"kv_gather_gbs": round(kv_bytes / (kv_ms[0] * 1e-3) / 1e9, 3),
+              "kv_scatter_gbs": round(kv_bytes / (kv_ms[1] * 1e-3) / 1e9, 3),
+              "kv_gather_roofline_frac": round(kv_bytes / (kv_ms[0] * 1e-3) / 1e9 / ce[1], 4),
+              "kv_scatter_roofline_frac": round(kv_bytes / (kv_ms[1] * 1e-3) / 1e9 / ce[0], 4),
+              "kv_bitexact": bool(okt.item()),
+              "kv_what": "4,096 x 64 KiB Llama-3-8B KV pages (seed 1) of a 65,536-page pinned pool per rank, "
+                         "tmaGather into HBM / tmaScatter back, all ranks at once; roofline = concurrent "
+                         "copy-engine H2D / D2H of the pool"}
+        del kv_out
+
     # Staging (non-zero-copy) PUT/GET: the same 4 x 1 GiB from and into HBM
     # that was never registered; the library stages it through slabs in the
     # same GPU's HBM (device-to-device stage copies, then the zero-copy
@@ -444,6 +499,7 @@ def main():
                 "put_frac_of_host_cpu_write": round(put_gbs / host_bw["write_gbs"], 4),
                 "get_frac_of_host_cpu_read": round(get_gbs / host_bw["read_gbs"], 4),
             }
+        out.update(kv)
         out.update(staging)
         out.update(extras)
         print(json.dumps(out), flush=True)
