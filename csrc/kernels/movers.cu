@@ -579,6 +579,116 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     run_epilogue(ep);
 }
 
+// Packed scatter of small blocks, the gather's mirror: lane 0 loads a tile
+// of up to 32 consecutive source blocks with ONE bulk load, then every lane
+// stores its own block to its pool slot (one bulk store per lane, tracked by
+// that lane's own bulk groups; every lane commits each round so the groups
+// stay aligned across the warp).
+struct PackedScatter {
+    const char *src;
+    const int64_t *idx;
+    char *pool;
+    int64_t n, bs, pool_blocks;
+    int per;
+};
+
+template <int STAGES, uint32_t STAGE_BYTES>
+__device__ __forceinline__ void warp_packed_scatter(const PackedScatter &a, int64_t first, int64_t stride,
+                                                    char *stage_mem, uint64_t *bars, uint32_t *status,
+                                                    uint64_t budget) {
+    const int lane = threadIdx.x & 31;
+    const int64_t tiles = (a.n + a.per - 1) / a.per;
+    if (first >= tiles) return;
+    const int64_t n = (tiles - 1 - first) / stride + 1;
+    if (lane == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_proxy_async_smem();
+    }
+    __syncwarp();
+    const uint32_t bs = static_cast<uint32_t>(a.bs);
+    int64_t issued = 0;
+
+    auto tile_count = [&](int64_t j) -> uint32_t {
+        const int64_t left = a.n - (first + j * stride) * a.per;
+        return static_cast<uint32_t>(left < a.per ? left : a.per);
+    };
+    auto issue = [&](int64_t j, int s) {  // lane 0 loads; the others only count
+        if (lane == 0) {
+            const int64_t b0 = (first + j * stride) * a.per;
+            const uint32_t bytes = tile_count(j) * bs;
+            mbar_arrive_expect_tx(&bars[s], bytes);
+            bulk_load(stage_mem + static_cast<size_t>(s) * STAGE_BYTES, a.src + b0 * a.bs, bytes, &bars[s]);
+        }
+        ++issued;
+    };
+
+    const int64_t pro = n < STAGES ? n : STAGES;
+    for (int64_t j = 0; j < pro; ++j) issue(j, static_cast<int>(j));
+
+    int64_t j = 0;
+    bool aborted = false;
+    for (; j < n; ++j) {
+        const int s = static_cast<int>(j % STAGES);
+        const uint32_t parity = static_cast<uint32_t>((j / STAGES) & 1);
+        int ok = 1;
+        if (lane == 0 && !mbar_wait_bounded(&bars[s], parity, budget)) {
+            ok = 0;
+            atomicOr(status, kStatusLoadTimeout);
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) {
+            aborted = true;
+            break;
+        }
+        __syncwarp();  // lane 0 saw the tile land before any lane stores from it
+        const uint32_t cnt = tile_count(j);
+        if (static_cast<uint32_t>(lane) < cnt) {
+            const int64_t b = (first + j * stride) * a.per + lane;
+            const int64_t p = __ldg(a.idx + b);
+            if (p < 0 || (a.pool_blocks > 0 && p >= a.pool_blocks))
+                atomicOr(status, kStatusBadIndex);
+            else
+                bulk_store(a.pool + p * a.bs,
+                           stage_mem + static_cast<size_t>(s) * STAGE_BYTES + static_cast<size_t>(lane) * bs, bs);
+        }
+        bulk_commit();
+        if (j >= 1) {
+            bulk_wait_read<1>();  // this lane's stores of tile j-1 have read their stage
+            __syncwarp();
+            const int64_t t = j - 1 + STAGES;
+            if (t < n) issue(t, static_cast<int>((j - 1) % STAGES));
+        }
+    }
+    if (lane == 0 && aborted) {
+        for (int64_t t = j; t < issued; ++t) {
+            if (!mbar_wait_bounded(&bars[t % STAGES], static_cast<uint32_t>((t / STAGES) & 1), budget)) {
+                atomicOr(status, kStatusDrainTimeout);
+                break;
+            }
+        }
+    }
+    bulk_wait_all();
+    __syncwarp();
+}
+
+template <int WARPS, int STAGES, uint32_t STAGE_BYTES>
+__global__ void __launch_bounds__(WARPS * 32, 1)
+    packed_scatter_kernel(const __grid_constant__ PackedScatter a, uint32_t *status, uint64_t budget,
+                          const Epilogue ep) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int warp = threadIdx.x >> 5;
+    char *stage_mem = reinterpret_cast<char *>(smem_raw) + static_cast<size_t>(warp) * STAGES * STAGE_BYTES;
+    uint64_t *bars =
+        reinterpret_cast<uint64_t *>(smem_raw + static_cast<size_t>(WARPS) * STAGES * STAGE_BYTES) + warp * STAGES;
+    trace_begin(ep.stamp);
+    window_open(ep.win);
+    warp_packed_scatter<STAGES, STAGE_BYTES>(a, static_cast<int64_t>(blockIdx.x) * WARPS + warp,
+                                             static_cast<int64_t>(gridDim.x) * WARPS, stage_mem, bars, status,
+                                             budget);
+    trace_end(ep.stamp);
+    run_epilogue(ep);
+}
+
 template <class Src>
 __global__ void __launch_bounds__(kVecWarps * 32)
     vector_mover_kernel(const __grid_constant__ Src src, uint32_t *status, const Epilogue ep) {
@@ -681,6 +791,35 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // Largest block the packed gather kernel takes (a stage holds >= 4 blocks).
 constexpr int64_t kPackedMaxBlock = kStageBytes / 4;
 
+int launch_packed_scatter(const PackedScatter &a, int max_ctas, cudaStream_t st, uint32_t *status,
+                          const Epilogue &ep, LaunchInfo *info) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::mutex mu;
+    static uint64_t configured = 0;
+    {
+        std::lock_guard<std::mutex> g(mu);
+        if (dev < 64 && !(configured & (1ull << dev))) {
+            cudaError_t e = cudaFuncSetAttribute(packed_scatter_kernel<kWarps, kStages, kStageBytes>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(kBulkSmem));
+            if (e != cudaSuccess) return e;
+            configured |= 1ull << dev;
+        }
+    }
+    const int64_t tiles = (a.n + a.per - 1) / a.per;
+    const int cap = max_ctas > 0 ? max_ctas : sm_count(dev);
+    const int64_t need = (tiles + kWarps - 1) / kWarps;
+    int ctas = static_cast<int>(need < cap ? need : cap);
+    if (ctas < 1) ctas = 1;
+    if (!status) status = default_status_word(dev);
+    packed_scatter_kernel<kWarps, kStages, kStageBytes><<<ctas, kWarps * 32, kBulkSmem, st>>>(a, status,
+                                                                                            wait_budget_ns(), ep);
+    note_launch();
+    if (info) *info = LaunchInfo{ctas, kWarps * 32, kBulkSmem, 4};
+    return cudaGetLastError();
+}
+
 int launch_packed_gather(const PackedGather &a, int max_ctas, cudaStream_t st, uint32_t *status,
                          const Epilogue &ep, LaunchInfo *info) {
     int dev = 0;
@@ -767,6 +906,20 @@ int h2d_scatter(const void *srcp, const int64_t *idx, void *pool, int64_t pool_b
     const int path = pick_path(mode, pool, srcp, bs);
     if (path < 0) return cudaErrorMisalignedAddress;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Packed kernel for small blocks on the bulk path, as for the gather.
+    if (path == 1 && bs <= kPackedMaxBlock && (mode == kModeTma || bs >= 1024)) {
+        PackedScatter a;
+        a.src = static_cast<const char *>(srcp);
+        a.idx = idx;
+        a.pool = static_cast<char *>(pool);
+        a.n = n;
+        a.bs = bs;
+        a.pool_blocks = pool_blocks;
+        a.per = static_cast<int>(std::min<int64_t>(32, kStageBytes / bs));
+        const Epilogue ep{window, window_ctr, nullptr, 0,
+                          trace_acquire("h2d_scatter", static_cast<uint64_t>(n * bs))};
+        return launch_packed_scatter(a, max_ctas, st, status, ep, info);
+    }
     ScatterSrc src;
     src.src = static_cast<const char *>(srcp);
     src.idx = idx;

@@ -15,7 +15,8 @@ both implementations against torch indexing):
   b272    2,048 x 272 B blocks (the reference tool's default,
           user_examples/qos_bench/run-bench-h2d.sh:13-17), reference TMA mode
   b1k     10,240 x 1 KiB blocks (its QoS bench's gather), reference TMA mode
-Ours: MPComm.tma_gather / tma_scatter in AUTO mode on the same stream.
+Ours: MPComm.tma_gather / tma_scatter (AUTO mode unless --ours-mode) on the
+same stream.
 
 Timing: per launch, CUDA events on the legacy default stream (where the
 reference launches), the start event queued behind a short device sleep so
@@ -96,7 +97,7 @@ def _device_ms(launch, iters: int, warmup: int) -> float:
     return times[len(times) // 2]
 
 
-def run_case(name, comm, ref, pool_blocks, n, bs, ref_mode, seed, iters, warmup, kv=False):
+def run_case(name, comm, ref, pool_blocks, n, bs, ref_mode, seed, iters, warmup, kv=False, ours_mode=0):
     if kv:
         pool = LLAMA3_8B_KV.make_pool(pool_blocks, seed=0)
         idx_cpu = LLAMA3_8B_KV.sample_pages(pool_blocks, n, seed=seed)
@@ -114,10 +115,10 @@ def run_case(name, comm, ref, pool_blocks, n, bs, ref_mode, seed, iters, warmup,
            "reference_mode": {REF_SM: "sm", REF_TMA: "tma"}[ref_mode]}
 
     def ours_gather():
-        assert comm.tma_gather(dram, idx.data_ptr(), out.data_ptr(), n, bs, 0, 0, 0) == 0
+        assert comm.tma_gather(dram, idx.data_ptr(), out.data_ptr(), n, bs, 0, ours_mode, 0) == 0
 
     def ours_scatter():
-        assert comm.tma_scatter(out.data_ptr(), idx.data_ptr(), dram, n, bs, 0, 0, 0) == 0
+        assert comm.tma_scatter(out.data_ptr(), idx.data_ptr(), dram, n, bs, 0, ours_mode, 0) == 0
 
     def ref_gather():
         ref.gather(dram, idx.data_ptr(), out.data_ptr(), bs, n, 0, ref_mode)
@@ -148,6 +149,8 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cases", default="kv64k,b272,b1k")
+    ap.add_argument("--ours-mode", choices=["auto", "sm", "tma"], default="auto",
+                    help="this library's H2D mode (the reference's is fixed per case)")
     a = ap.parse_args(argv)
     torch.cuda.set_device(0)
     ref = RefKernels(build_reference())
@@ -156,14 +159,16 @@ def main(argv=None):
            "device": torch.cuda.get_device_name(0),
            "reference_build": "src/mpcomm_tma_kernels.cu unmodified, nvcc -gencode compute_90 (sm_90 + PTX, "
                               "JIT-compiled for sm_100 by the driver)",
-           "timing": "median per-launch CUDA-event time, host launch excluded", "cases": {}}
+           "timing": "median per-launch CUDA-event time, host launch excluded", "ours_mode": a.ours_mode,
+           "cases": {}}
     specs = {
         "kv64k": dict(pool_blocks=65536, n=4096, bs=LLAMA3_8B_KV.page_bytes, ref_mode=REF_SM, seed=1, kv=True),
         "b272": dict(pool_blocks=8192, n=2048, bs=272, ref_mode=REF_TMA, seed=5),
         "b1k": dict(pool_blocks=40960, n=10240, bs=1024, ref_mode=REF_TMA, seed=6),
     }
     for c in a.cases.split(","):
-        name, row = run_case(c, comm, ref, iters=a.iters, warmup=a.warmup, **specs[c])
+        name, row = run_case(c, comm, ref, iters=a.iters, warmup=a.warmup,
+                             ours_mode={"auto": 0, "sm": 1, "tma": 2}[a.ours_mode], **specs[c])
         res["cases"][name] = row
     # The reference prints a line per launch through C stdio: flush it first
     # so the JSON line is the last one.
