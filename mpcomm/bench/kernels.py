@@ -7,6 +7,7 @@ Cases (inputs larger than the 126 MB L2 where DRAM/PCIe traffic matters):
   gather_tma / gather_sm   1,024 x 64 KiB pages from a 2,048-page pinned pool
   gather_1k                10,240 x 1 KiB blocks from a 40,960-block pinned pool
                            (the packed small-block gather kernel)
+  scatter_1k               the reverse (the packed small-block scatter kernel)
   scatter_tma              the reverse
   copy_d2d                 GPU-fabric WR batch, 4 x 40 MiB HBM -> HBM
   copy_h2d                 GPU-fabric WR batch, 2 x 32 MiB pinned DRAM -> HBM
@@ -33,7 +34,7 @@ import mpcomm
 from mpcomm import ops
 
 PAGE = 65536
-ALL = ["gather_tma", "gather_sm", "gather_1k", "scatter_tma", "copy_d2d", "copy_h2d", "crc32", "crc32_noalloc",
+ALL = ["gather_tma", "gather_sm", "gather_1k", "scatter_1k", "scatter_tma", "copy_d2d", "copy_h2d", "crc32", "crc32_noalloc",
        "pxn_local", "fanout_local", "gather_bcast_p2p", "nvls", "wait_flag"]
 
 
@@ -61,6 +62,7 @@ def build_cases():
         "gather_tma": (lambda: ops.paged_gather(pool, idx, out=out, mode=ops.MODE_TMA), nb),
         "gather_sm": (lambda: ops.paged_gather(pool, idx, out=out, mode=ops.MODE_SM), nb),
         "gather_1k": (lambda: ops.paged_gather(pool1k, idx1k, out=out1k), 10240 * 1024),
+        "scatter_1k": (lambda: ops.paged_scatter(out1k, idx1k, pool1k), 10240 * 1024),
         "scatter_tma": (lambda: ops.paged_scatter(out, idx, pool, mode=ops.MODE_TMA), nb),
         "copy_d2d": (lambda: ops.copy_spans([big.data_ptr() + i * q for i in range(4)],
                                             [big2.data_ptr() + i * q for i in range(4)], [q] * 4), 4 * q),
