@@ -129,6 +129,7 @@ Config Config::from_env() {
     }
     read_flag("MPCOMM_REPOST_ON_FAILURE", &c.repost_on_failure);
     read_flag("MPCOMM_FUSED_BROADCAST", &c.fused_broadcast);
+    read_int("MPCOMM_PAGED_CHUNK_SIZE", 4096, 1ll << 30, &c.paged_chunk_size);
     read_str("MPCOMM_CONFIG_FILE", &c.config_file);
     return c;
 }

@@ -64,6 +64,7 @@ struct Config {
     std::string nic_pairing = "suffix";      // MPCOMM_NIC_PAIRING suffix|index
     bool repost_on_failure = true;           // MPCOMM_REPOST_ON_FAILURE
     bool fused_broadcast = true;             // MPCOMM_FUSED_BROADCAST
+    size_t paged_chunk_size = 1ull << 30;    // MPCOMM_PAGED_CHUNK_SIZE (bytes of pages per launch)
     std::string config_file;                 // MPCOMM_CONFIG_FILE (version json)
 
     // Reads all variables from the process environment.

@@ -232,7 +232,11 @@ TransferHandle MPComm::Impl::submitPaged(uintptr_t pool, const int64_t *indices,
     t->candidates = {rail};
     t->local_gpu = gpu;
     t->host_source = gpu::device_of(reinterpret_cast<const void *>(pool)) < 0;
-    t->pages_per_chunk = std::max<size_t>(1, effectiveChunk({rail}) / static_cast<size_t>(bs));
+    // Pages per launch: MPCOMM_PAGED_CHUNK_SIZE bytes (default the 1 GiB WR
+    // limit). Launches of one stream run one after another anyway, so fewer,
+    // larger ones only save launch and completion latency.
+    t->pages_per_chunk =
+        std::max<size_t>(1, std::min(cfg_.paged_chunk_size, kMaxChunk) / static_cast<size_t>(bs));
     t->plan.build(0, {raddr}, {total}, t->pages_per_chunk * static_cast<size_t>(bs), false);
     size_t ol = throttle_outstanding_.load(std::memory_order_relaxed);
     if (ol == 0) ol = rails_[rail]->rail->preferred_outstanding(cfg_);

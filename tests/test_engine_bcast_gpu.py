@@ -80,7 +80,7 @@ def test_engine_broadcast_one_gpu(fused):
 PAGED = r"""
 import os, torch, mpcomm
 torch.cuda.set_device(0)
-bs, pages, n = 65536, 96, 40  # MPCOMM_NVL_CHUNK_SIZE=1 MiB: 16 pages per chunk, 3 chunks
+bs, pages, n = 65536, 96, 40  # MPCOMM_PAGED_CHUNK_SIZE=1 MiB: 16 pages per launch, 3 launches
 pool = torch.randint(0, 256, (pages, bs), dtype=torch.uint8).pin_memory()
 idx_cpu = torch.randperm(pages, generator=torch.Generator().manual_seed(3))[:n]
 idx = idx_cpu.cuda()
@@ -119,7 +119,7 @@ print("paged put ok")
 def test_engine_paged_put_one_gpu():
     """put_pages_async: the fused PXN gather + forward as an engine transfer
     (one pxn_gather_forward launch per chunk of pages, with an H2D window)."""
-    env = dict(os.environ, MPCOMM_KERNEL_TRACE="1024", MPCOMM_NVL_CHUNK_SIZE=str(1 << 20), MPCOMM_LOG_LEVEL="1")
+    env = dict(os.environ, MPCOMM_KERNEL_TRACE="1024", MPCOMM_PAGED_CHUNK_SIZE=str(1 << 20), MPCOMM_LOG_LEVEL="1")
     r = subprocess.run(["timeout", "-k", "30", "240", sys.executable, "-c", PAGED], capture_output=True, text=True,
                        cwd=ROOT, env=env)
     assert r.returncode == 0, f"{r.stdout[-3000:]}\n{r.stderr[-3000:]}"
