@@ -73,8 +73,13 @@ int main() {
             const uintptr_t r = raddr + static_cast<uintptr_t>(t) * per;
             for (int k = 0; k < rounds; ++k) {
                 for (auto &x : src) x = static_cast<unsigned char>(rng());
+                // k % 3: 0 PUT, 1 broadcast of the first half to both halves
+                // (a fused one-to-many WRITE on loopback rails), 2 scatter.
+                const bool bcast = k % 3 == 1;
                 auto h = (k % 3 == 2) ? a.scatterAsync(reinterpret_cast<uintptr_t>(src.data()), {"B", "B"},
                                                        {r, r + per / 2}, {per / 2, per / 2})
+                         : bcast      ? a.broadcastAsync(reinterpret_cast<uintptr_t>(src.data()), per / 2, {"B", "B"},
+                                                         {r, r + per / 2})
                                       : a.putAsync(reinterpret_cast<uintptr_t>(src.data()), "B", r, per);
                 if (h == mpcomm::INVALID_TRANSFER_HANDLE || a.waitTransfer(h, 30000) != 0) ++failures;
                 auto res = a.getTransferResult(h);
@@ -88,7 +93,13 @@ int main() {
                     ++failures;
                 }
                 a.releaseTransfer(h);
-                if (std::memcmp(src.data(), back.data(), per) != 0) ++failures;
+                if (bcast) {
+                    if (std::memcmp(src.data(), back.data(), per / 2) != 0 ||
+                        std::memcmp(src.data(), back.data() + per / 2, per / 2) != 0)
+                        ++failures;
+                } else if (std::memcmp(src.data(), back.data(), per) != 0) {
+                    ++failures;
+                }
             }
         });
     }
