@@ -4,6 +4,7 @@
 
 #include "engine/impl.h"
 #include "kernels/launch.h"
+#include "parallel/mcgroup.h"
 
 namespace mpcomm {
 
@@ -148,6 +149,48 @@ std::vector<MPComm::PcieAffinityCheck> MPComm::getPcieAffinitySelfCheck() const 
 int MPComm::registerMulticastMemory(void *uc_addr, size_t length, void *mc_addr, uint64_t group_token,
                                     int group_size) {
     return impl_->registerMulticastMemory(uc_addr, length, mc_addr, group_token, group_size);
+}
+int MPComm::registerMulticastGroup(const MulticastGroup &g) {
+    return impl_->registerMulticastMemory(g.uc_addr, g.length, g.mc_addr, g.token, g.members);
+}
+
+namespace {
+int group_result(int rc, const vmm::McGroup &g, MulticastGroup *out) {
+    if (rc != 0) return rc < 0 ? MPCOMM_ERR_CONNECTION : MPCOMM_ERR_DEVICE;
+    out->uc_addr = g.uc;
+    out->mc_addr = g.mcva;
+    out->length = g.size;
+    out->token = g.token;
+    out->members = g.members;
+    out->device = g.dev;
+    out->mc_handle = g.mc;
+    out->mem_handle = g.mem;
+    return MPCOMM_SUCCESS;
+}
+}  // namespace
+
+int createMulticastGroup(const std::string &name, size_t bytes, int members, MulticastGroup *out, int timeout_ms) {
+    if (!out || name.empty() || members < 2 || bytes == 0 || timeout_ms <= 0) return MPCOMM_ERR_INVALID_ARG;
+    vmm::McGroup g;
+    return group_result(vmm::mc_group_create(name, bytes, members, timeout_ms, &g), g, out);
+}
+int joinMulticastGroup(const std::string &name, size_t bytes, int members, MulticastGroup *out, int timeout_ms) {
+    if (!out || name.empty() || members < 2 || bytes == 0 || timeout_ms <= 0) return MPCOMM_ERR_INVALID_ARG;
+    vmm::McGroup g;
+    return group_result(vmm::mc_group_join(name, bytes, members, timeout_ms, &g), g, out);
+}
+int releaseMulticastGroup(MulticastGroup *out) {
+    if (!out) return MPCOMM_ERR_INVALID_ARG;
+    vmm::McGroup g;
+    g.mc = out->mc_handle;
+    g.mem = out->mem_handle;
+    g.uc = out->uc_addr;
+    g.mcva = out->mc_addr;
+    g.size = out->length;
+    g.dev = out->device;
+    const int e = vmm::mc_group_release(&g);
+    *out = MulticastGroup{};
+    return e ? MPCOMM_ERR_DEVICE : MPCOMM_SUCCESS;
 }
 
 }  // namespace mpcomm

@@ -176,6 +176,50 @@ int multicast_bind_local(uint64_t mc, size_t size, int dev, uint64_t *mem, void 
 
 int multicast_map(uint64_t mc, size_t size, int dev, void **mc_va) { return map_rw(mc, size, dev, mc_va); }
 
+int vmm_export(const void *ptr, uintptr_t *base, size_t *size, int *fd) {
+    auto retain = sym<CUresult (*)(CUmemGenericAllocationHandle *, void *)>("cuMemRetainAllocationHandle");
+    auto range = sym<CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr)>("cuMemGetAddressRange");
+    auto exp = sym<CUresult (*)(void *, CUmemGenericAllocationHandle, CUmemAllocationHandleType,
+                                unsigned long long)>("cuMemExportToShareableHandle");
+    auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
+    if (!retain || !range || !exp || !rel) return kNoDriver;
+    CUdeviceptr b = 0;
+    size_t n = 0;
+    CUresult r = range(&b, &n, reinterpret_cast<CUdeviceptr>(ptr));
+    if (r != CUDA_SUCCESS) return r;
+    CUmemGenericAllocationHandle h = 0, last = 0;
+    r = retain(&h, reinterpret_cast<void *>(b));
+    if (r != CUDA_SUCCESS) return r;
+    // The whole range must be one allocation: its last byte has the same one.
+    r = retain(&last, reinterpret_cast<void *>(b + n - 1));
+    if (r == CUDA_SUCCESS) rel(last);
+    if (r != CUDA_SUCCESS || last != h) {
+        rel(h);
+        return r != CUDA_SUCCESS ? static_cast<int>(r) : -1;
+    }
+    int f = -1;
+    r = exp(&f, h, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0);
+    rel(h);
+    if (r != CUDA_SUCCESS) return r;
+    *base = static_cast<uintptr_t>(b);
+    *size = n;
+    *fd = f;
+    return 0;
+}
+
+int vmm_import_map(int fd, size_t size, int dev, void **va) {
+    auto imp = sym<CUresult (*)(CUmemGenericAllocationHandle *, void *, CUmemAllocationHandleType)>(
+        "cuMemImportFromShareableHandle");
+    auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
+    if (!imp || !rel) return kNoDriver;
+    CUmemGenericAllocationHandle h = 0;
+    CUresult r = imp(&h, reinterpret_cast<void *>(static_cast<uintptr_t>(fd)), CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+    if (r != CUDA_SUCCESS) return r;
+    const int e = map_rw(h, size, dev, va);
+    rel(h);  // the mapping holds the allocation from here on
+    return e;
+}
+
 int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev) {
     auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
     auto vfree = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree");
@@ -208,6 +252,7 @@ int gdr_alloc(int dev, size_t size, void **ptr, size_t *alloc_size) {
     p.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
     p.location.id = dev;
     p.allocFlags.gpuDirectRDMACapable = 1;
+    p.requestedHandleTypes = CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR;  // reachable by peer processes
     size_t g = 0;
     CUresult r = gran(&g, &p, CU_MEM_ALLOC_GRANULARITY_RECOMMENDED);
     if (r != CUDA_SUCCESS) return r;

@@ -41,6 +41,16 @@ int multicast_map(uint64_t mc, size_t size, int dev, void **mc_va);
 // Unmaps/unbinds/releases everything created above (any argument may be 0).
 int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev);
 
+// VMM (cuMemCreate) memory across processes, where CUDA IPC cannot go:
+// vmm_export: the allocation mapped at `ptr` as a POSIX file descriptor
+// (*fd, owned by the caller) with the mapped range [*base, *base + *size).
+// Fails (non-zero) for memory that is not a VMM allocation, one created
+// without a POSIX-fd handle type, or a range made of several allocations.
+int vmm_export(const void *ptr, uintptr_t *base, size_t *size, int *fd);
+// vmm_import_map: imports `fd` (not consumed) and maps its `size` bytes at
+// a new address readable and writable by device `dev`.
+int vmm_import_map(int fd, size_t size, int dev, void **va);
+
 // HBM that a NIC can register through dma-buf (GPUDirect RDMA): a VMM
 // allocation of `dev` created with the gpuDirectRDMACapable flag, `size`
 // rounded up to the allocation granularity (*alloc_size), mapped read-write

@@ -16,7 +16,11 @@
 //   * this process's host memory (pinned + mapped at registration; UVA),
 //   * another process's device memory on the same host: registrations are
 //     published in /dev/shm/mpcomm-nvl.<boot>.<pid> (key, range, CUDA IPC
-//     handle) and opened with cudaIpcOpenMemHandle on first use,
+//     handle) and opened with cudaIpcOpenMemHandle on first use; VMM
+//     (cuMemCreate) memory, which CUDA IPC cannot export (NVLS group copies,
+//     GPUDirect buffers), is offered instead as the allocation's POSIX
+//     handle on the owner's descriptor server (abstract Unix socket
+//     mpcomm-fd.<boot>.<pid>) and imported + mapped by the peer on first use,
 //   * another process's host memory when it is a shared file mapping
 //     (/dev/shm, hugetlbfs, any MAP_SHARED file): the record carries the
 //     file path and offset; the peer maps the same pages, pins them and
@@ -43,10 +47,12 @@
 
 #include "core/core.h"
 #include "core/nvtx.h"
+#include "ctrl/fdshare.h"
 #include "cuda/gpu.h"
 #include "kernels/launch.h"
 #include "mpcomm.h"
 #include "mpcomm_log.h"
+#include "parallel/vmm.h"
 #include "topo/topology.h"
 #include "transport/fabric.h"
 
@@ -65,7 +71,7 @@ struct DirRecord {
     uint64_t base;
     uint64_t alloc_size;
     int32_t device;
-    int32_t kind;  // 0 device memory, 1 host memory
+    int32_t kind;  // 0 device memory (CUDA IPC), 1 host memory, 2 device memory (VMM, descriptor server)
     unsigned char ipc[gpu::kIpcHandleBytes];
     uint64_t file_off;  // host memory: offset of `addr` in the backing file
     char path[160];     // host memory: backing file ("" = private, unreachable)
@@ -129,6 +135,9 @@ std::string dir_path(long pid) {
     return "/dev/shm/mpcomm-nvl." + boot_tag() + "." + std::to_string(pid);
 }
 
+// Abstract socket of process `pid`'s descriptor server (VMM handles).
+std::string fd_service(long pid) { return "mpcomm-fd." + boot_tag() + "." + std::to_string(pid); }
+
 struct Region {
     uint32_t key;
     uintptr_t addr;
@@ -145,6 +154,7 @@ struct Region {
     uint64_t mc_token = 0;    // NVLS group of which [addr, addr+len) is this process's copy
     uintptr_t mc_addr = 0;    // this process's multicast mapping of the group's offset 0
     int mc_members = 0;
+    bool vmm = false;         // device memory offered as a VMM handle (kind 2)
 };
 
 // Multicast identity of a registration, as seen by a process posting to it.
@@ -184,8 +194,25 @@ class Registry {
             r.base = info.base ? info.base : r.addr;
             r.alloc_size = info.size ? info.size : len;
             if (gpu::ipc_get_handle(reinterpret_cast<void *>(r.base), ipc) != 0) {
-                // Not exportable (e.g. VMM allocation): usable in-process only.
+                // Not a cudaMalloc allocation: offer it as a VMM handle, else
+                // it stays usable in-process only.
                 std::memset(ipc, 0, sizeof(ipc));
+                uintptr_t vb = 0;
+                size_t vn = 0;
+                int fd = -1;
+                if (vmm::vmm_export(addr, &vb, &vn, &fd) != 0) {
+                    MPCOMM_LOG_DEBUG("MPComm[nvl]: device range %p+%zu is not exportable; other processes "
+                                     "will not reach it\n", addr, len);
+                } else if (r.addr < vb || r.addr + len > vb + vn) {
+                    // A peer maps exactly [vb, vb + vn): the range must lie inside.
+                    MPCOMM_LOG_DEBUG("MPComm[nvl]: %p+%zu spans several VMM allocations; other processes "
+                                     "will not reach it\n", addr, len);
+                    close(fd);
+                } else if (ctrl::fd_offer(fd_service(getpid()), next_key_, fd) == 0) {
+                    r.vmm = true;  // offered under the key assigned below
+                    r.base = vb;
+                    r.alloc_size = vn;
+                }
             }
         } else {
             void *dptr = nullptr;
@@ -223,6 +250,7 @@ class Registry {
         if (it == regions_.end()) return MPCOMM_ERR_INVALID_ARG;
         if (--it->second.refs > 0) return 0;
         if (it->second.pinned_by_us) gpu::host_unpin(reinterpret_cast<void *>(it->second.addr));
+        if (it->second.vmm) ctrl::fd_withdraw(key);
         if (dir_ && it->second.slot < kDirSlots) {
             DirRecord *rec = records() + it->second.slot;
             __atomic_store_n(&rec->state, 0u, __ATOMIC_RELEASE);
@@ -315,7 +343,7 @@ class Registry {
             recs[i].base = r.base;
             recs[i].alloc_size = r.alloc_size;
             recs[i].device = r.dev;
-            recs[i].kind = r.device ? 0 : 1;
+            recs[i].kind = !r.device ? 1 : r.vmm ? 2 : 0;
             std::memcpy(recs[i].ipc, ipc, gpu::kIpcHandleBytes);
             recs[i].file_off = r.file_off;
             std::memset(recs[i].path, 0, sizeof(recs[i].path));
@@ -364,7 +392,7 @@ class RemoteMaps {
         const int prev = gpu::current_device();
         if (prev != dev) gpu::set_device(dev);
         int st;
-        if (rec.kind != 0) {
+        if (rec.kind == 1) {
             *host = true;
             st = resolve_host(pid, rec, addr, out);
         } else {
@@ -466,7 +494,35 @@ class RemoteMaps {
         return 0;
     }
 
+    // VMM allocation of `pid`: fetch its handle from the owner's descriptor
+    // server and map it for `dev`, once per (pid, key, dev) (keys are never
+    // reused, so a re-registered range is mapped afresh).
+    int resolve_vmm(long pid, const DirRecord &rec, uintptr_t addr, int dev, uintptr_t *out) {
+        auto mk = std::make_tuple(pid, rec.key, dev);
+        auto it = vmm_opened_.find(mk);
+        if (it == vmm_opened_.end()) {
+            int fd = -1;
+            const int fr = ctrl::fd_fetch(fd_service(pid), rec.key, 5000, &fd);
+            if (fr != 0) {
+                MPCOMM_LOG_ERROR("MPComm[nvl]: VMM handle of pid %ld's buffer 0x%lx: %s\n", pid,
+                                 static_cast<unsigned long>(rec.addr), fr == 1 ? "withdrawn" : "server unreachable");
+                return kWcRemAccessErr;
+            }
+            void *p = nullptr;
+            const int e = vmm::vmm_import_map(fd, rec.alloc_size, dev, &p);
+            close(fd);
+            if (e != 0) {
+                MPCOMM_LOG_ERROR("MPComm[nvl]: mapping pid %ld's VMM buffer failed (%d)\n", pid, e);
+                return kWcRemAccessErr;
+            }
+            it = vmm_opened_.emplace(mk, reinterpret_cast<uintptr_t>(p)).first;
+        }
+        *out = it->second + (addr - rec.base);
+        return 0;
+    }
+
     int resolve_device(long pid, const DirRecord &rec, uintptr_t addr, int dev, uintptr_t *out) {
+        if (rec.kind == 2) return resolve_vmm(pid, rec, addr, dev, out);
         auto mk = std::make_tuple(pid, rec.base, dev);
         auto it = opened_.find(mk);
         if (it == opened_.end()) {
@@ -489,6 +545,7 @@ class RemoteMaps {
     std::mutex mu_;
     std::unordered_map<long, const DirRecord *> dirs_;
     std::map<std::tuple<long, uintptr_t, int>, uintptr_t> opened_;  // (pid, base, local dev)
+    std::map<std::tuple<long, uint32_t, int>, uintptr_t> vmm_opened_;  // (pid, key, local dev)
     std::map<std::pair<long, uint32_t>, uintptr_t> host_ranges_;  // portable pinned: any device
 };
 

@@ -20,8 +20,19 @@
 // reads every target slot the last put/scatter/broadcast test wrote back
 // with GETs and compares it byte for byte (the reference harness verifies
 // by read-back the same way).
+// --nvls NAME:MEMBERS (with --gpu) makes this process one member of an NVLS
+// multicast group of MEMBERS GPUs (exactly one process also passes
+// --nvls-create): a target serves its copy of the group buffer, an
+// initiator registers its own copy, and a broadcast to all the other
+// members then goes out as multicast stores through the NVSwitch (one
+// launch per chunk; --verify also checks the initiator's own copy). Every
+// process needs the same --buffer-size (default --size x --batch-size).
+// A target leaves cleanly on SIGTERM/SIGINT (unregisters, releases its copy).
+// With MPCOMM_KERNEL_TRACE set, --json adds the timed launches by kind.
 #include <cuda_runtime.h>
 #include <unistd.h>
+
+#include <csignal>
 
 #include <algorithm>
 #include <chrono>
@@ -29,6 +40,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <map>
 #include <random>
 #include <sstream>
 #include <string>
@@ -38,6 +50,9 @@
 #include "mpcomm.h"
 
 namespace {
+
+volatile std::sig_atomic_t g_stop = 0;
+void on_signal(int) { g_stop = 1; }
 
 struct Target {
     std::string id, addr;
@@ -91,6 +106,7 @@ void usage(const char *prog) {
         "          [--iterations N] [--warmup W] [--test-type put,get,scatter,gather,broadcast]\n"
         "          [--gpu N] [--wait-go-file PATH] [--ready-file PATH] [--hold-file PATH]\n"
         "          [--hold-timeout S] [--done-file PATH] [--json] [--verify] [--verbose]\n"
+        "          [--nvls NAME:MEMBERS [--nvls-create]]\n"
         "Sizes take K/M/G/T suffixes. Fabric: MPCOMM_FABRIC (auto|nvl|ib|sock|lo).\n",
         prog);
 }
@@ -101,7 +117,9 @@ int main(int argc, char **argv) {
     std::string mode = "initiator", host_id = "test:0", devices, tests = "put,get", go_file, ready_file, hold_file, done_file;
     int tcp_port = 0, iters = 10, warmup = 3, gpu = -1, hold_timeout = 600;
     size_t size = 1ull << 30, buf_size = 0, batch = 4;
-    bool verbose = false, json = false, verify = false;
+    bool verbose = false, json = false, verify = false, nvls_create = false;
+    std::string nvls_name;
+    int nvls_members = 0;
     std::vector<Target> targets;
     for (int i = 1; i < argc; ++i) {
         std::string a = argv[i];
@@ -128,6 +146,12 @@ int main(int argc, char **argv) {
         else if (a == "--hold-timeout") hold_timeout = std::atoi(next().c_str());
         else if (a == "--json") json = true;
         else if (a == "--verify") verify = true;
+        else if (a == "--nvls") {
+            auto f = split(next(), ':');
+            if (f.size() != 2) return usage(argv[0]), 2;
+            nvls_name = f[0];
+            nvls_members = std::atoi(f[1].c_str());
+        } else if (a == "--nvls-create") nvls_create = true;
         else if (a == "--verbose" || a == "-v") verbose = true;
         else if (a == "--help" || a == "-h") return usage(argv[0]), 0;
         else return usage(argv[0]), 2;
@@ -138,13 +162,40 @@ int main(int argc, char **argv) {
     if (comm.init(host_id, devices, tcp_port) != 0) return std::fprintf(stderr, "init failed\n"), 1;
     std::printf("[scatter_test] host %s fabric %s rails %zu tcp %d\n", host_id.c_str(),
                 comm.getFabricName().c_str(), comm.getNumNics(), comm.getTcpPort());
+    std::signal(SIGTERM, on_signal);
+    std::signal(SIGINT, on_signal);
+
+    // NVLS group membership: this process's copy of the group buffer.
+    mpcomm::MulticastGroup grp;
+    if (!nvls_name.empty()) {
+        if (gpu < 0 || nvls_members < 2) return std::fprintf(stderr, "--nvls needs --gpu and MEMBERS >= 2\n"), 2;
+        const size_t want = buf_size ? buf_size : size * batch;
+        const int rc = nvls_create ? mpcomm::createMulticastGroup(nvls_name, want, nvls_members, &grp)
+                                   : mpcomm::joinMulticastGroup(nvls_name, want, nvls_members, &grp);
+        if (rc) return std::fprintf(stderr, "NVLS group %s: %d\n", nvls_name.c_str(), rc), 1;
+        cudaMemset(grp.uc_addr, 0x5A, grp.length);
+        cudaDeviceSynchronize();
+        if (comm.registerMulticastGroup(grp))
+            return std::fprintf(stderr, "registerMulticastGroup failed\n"), mpcomm::releaseMulticastGroup(&grp), 1;
+        std::printf("[scatter_test] NVLS group %s: copy %p (%zu bytes), %d members\n", nvls_name.c_str(),
+                    grp.uc_addr, grp.length, grp.members);
+    }
+    auto finish = [&](int rc) {
+        if (grp.uc_addr) {
+            comm.unpublishBuffer(grp.uc_addr);
+            comm.unregisterMemory(grp.uc_addr);
+        }
+        comm.shutdown();
+        mpcomm::releaseMulticastGroup(&grp);
+        return rc;
+    };
 
     void *served = nullptr;
     if (mode == "target" || mode == "both") {
         if (!buf_size) buf_size = size * batch;
-        served = alloc_buf(buf_size, gpu);
-        if (!served || comm.registerMemory(served, buf_size) || comm.publishBuffer(served, buf_size))
-            return std::fprintf(stderr, "serving buffer failed\n"), 1;
+        served = grp.uc_addr ? grp.uc_addr : alloc_buf(buf_size, gpu);
+        if (!served || (!grp.uc_addr && comm.registerMemory(served, buf_size)) || comm.publishBuffer(served, buf_size))
+            return std::fprintf(stderr, "serving buffer failed\n"), finish(1);
         comm.startAcceptThread();
         std::printf("[scatter_test] serving %zu bytes at %p (ready)\n", buf_size, served);
         std::fflush(stdout);
@@ -157,19 +208,22 @@ int main(int argc, char **argv) {
             }
         }
         if (mode == "target") {
-            for (;;) {
-                std::this_thread::sleep_for(std::chrono::seconds(verbose ? 5 : 60));
-                if (verbose) std::printf("[scatter_test] published=%zu\n", comm.getPublishedBufferCount());
+            for (int tick = 1; !g_stop; ++tick) {
+                std::this_thread::sleep_for(std::chrono::milliseconds(50));
+                if (verbose && tick % 100 == 0)
+                    std::printf("[scatter_test] published=%zu\n", comm.getPublishedBufferCount());
             }
+            std::printf("[scatter_test] target %s stopping\n", host_id.c_str());
+            return finish(0);
         }
         if (targets.empty()) targets.push_back(Target{"self", "127.0.0.1", comm.getTcpPort()});
     }
-    if (targets.empty()) return usage(argv[0]), 2;
+    if (targets.empty()) return usage(argv[0]), finish(2);
     if (!go_file.empty()) {
         const auto until = std::chrono::steady_clock::now() + std::chrono::seconds(hold_timeout);
         while (access(go_file.c_str(), F_OK) != 0) {
             if (std::chrono::steady_clock::now() >= until)
-                return std::fprintf(stderr, "no go file %s after %d s\n", go_file.c_str(), hold_timeout), 1;
+                return std::fprintf(stderr, "no go file %s after %d s\n", go_file.c_str(), hold_timeout), finish(1);
             std::this_thread::sleep_for(std::chrono::milliseconds(50));
         }
     }
@@ -191,13 +245,13 @@ int main(int argc, char **argv) {
         }
         mpcomm::RemoteBufferEntry e;
         if (rc || comm.queryRemoteBufferByNuma(t.id, t.addr, t.port, -1, e))
-            return std::fprintf(stderr, "connect/query %s failed\n", t.id.c_str()), 1;
-        if (e.length < size * batch) return std::fprintf(stderr, "remote buffer too small\n"), 1;
+            return std::fprintf(stderr, "connect/query %s failed\n", t.id.c_str()), finish(1);
+        if (e.length < size * batch) return std::fprintf(stderr, "remote buffer too small\n"), finish(1);
         remote.push_back(e.addr);
     }
     const size_t local_bytes = size * batch * targets.size();
     void *local = alloc_buf(local_bytes, gpu);
-    if (!local || comm.registerMemory(local, local_bytes)) return std::fprintf(stderr, "local buffer failed\n"), 1;
+    if (!local || comm.registerMemory(local, local_bytes)) return std::fprintf(stderr, "local buffer failed\n"), finish(1);
     const uintptr_t lp = reinterpret_cast<uintptr_t>(local);
     std::vector<unsigned char> pattern;
     if (verify) {
@@ -250,29 +304,44 @@ int main(int argc, char **argv) {
             return rc;
         };
         for (int w = 0; w < warmup; ++w)
-            if (one_round()) return std::fprintf(stderr, "%s warm-up failed\n", tt.c_str()), 1;
+            if (one_round()) return std::fprintf(stderr, "%s warm-up failed\n", tt.c_str()), finish(1);
+        // Kernel trace (MPCOMM_KERNEL_TRACE): launches of the timed rounds by kind.
+        const bool traced = std::getenv("MPCOMM_KERNEL_TRACE") != nullptr;
+        uint64_t seq0 = 0;
+        if (traced)
+            for (const auto &r : mpcomm::MPComm::getKernelTrace()) seq0 = std::max(seq0, r.seq);
         const uint64_t launches0 = mpcomm::MPComm::getKernelLaunchCount();
         auto t0 = std::chrono::steady_clock::now();
         for (int i = 0; i < iters; ++i)
-            if (one_round()) return std::fprintf(stderr, "%s failed\n", tt.c_str()), 1;
+            if (one_round()) return std::fprintf(stderr, "%s failed\n", tt.c_str()), finish(1);
         const double s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         const double bytes = static_cast<double>(size) * batch * targets.size() * iters;
         std::printf("--- %s Summary: size=%zu batch=%zu targets=%zu iters=%d  %.3f GB/s  (%.3f ms/round)\n",
                     tt.c_str(), size, batch, targets.size(), iters, bytes / 1e9 / s, s * 1e3 / iters);
         const uint64_t launches = mpcomm::MPComm::getKernelLaunchCount() - launches0;
+        std::string kinds;
+        if (traced) {
+            std::map<std::string, int> by_kind;
+            for (const auto &r : mpcomm::MPComm::getKernelTrace())
+                if (r.seq > seq0) ++by_kind[r.kind];
+            for (const auto &kv : by_kind)
+                kinds += (kinds.empty() ? "" : ", ") + ("\"" + kv.first + "\": ") + std::to_string(kv.second);
+            kinds = ", \"kernel_kinds\": {" + kinds + "}";
+        }
         if (json)
             std::printf("{\"tool\": \"scatter_test\", \"host\": \"%s\", \"test\": \"%s\", \"size\": %zu, "
                         "\"batch\": %zu, \"targets\": %zu, \"iters\": %d, \"gbps\": %.4f, \"ms_per_round\": %.4f, "
-                        "\"kernel_launches\": %llu}\n",
+                        "\"kernel_launches\": %llu, \"nvls_member\": %s%s}\n",
                         host_id.c_str(), tt.c_str(), size, batch, targets.size(), iters, bytes / 1e9 / s,
-                        s * 1e3 / iters, static_cast<unsigned long long>(launches));
+                        s * 1e3 / iters, static_cast<unsigned long long>(launches), grp.uc_addr ? "true" : "false",
+                        kinds.c_str());
         std::fflush(stdout);
         if (tt == "put" || tt == "scatter" || tt == "broadcast") last_write = tt;
     }
     if (verify && !last_write.empty()) {
         // Read every written slot back and compare with what was sent.
         void *scratch = alloc_buf(size, gpu);
-        if (!scratch || comm.registerMemory(scratch, size)) return std::fprintf(stderr, "verify buffer failed\n"), 1;
+        if (!scratch || comm.registerMemory(scratch, size)) return std::fprintf(stderr, "verify buffer failed\n"), finish(1);
         std::vector<unsigned char> got(size);
         size_t bad = 0;
         for (size_t t = 0; t < targets.size(); ++t) {
@@ -281,20 +350,27 @@ int main(int argc, char **argv) {
                 mpcomm::TransferHandle h =
                     comm.getAsync(reinterpret_cast<uintptr_t>(scratch), targets[t].id, remote[t] + b * size, size);
                 if (h == mpcomm::INVALID_TRANSFER_HANDLE || comm.waitTransfer(h, 600000))
-                    return std::fprintf(stderr, "verify read-back failed\n"), 1;
+                    return std::fprintf(stderr, "verify read-back failed\n"), finish(1);
                 comm.releaseTransfer(h);
                 if (gpu >= 0) cudaMemcpy(got.data(), scratch, size, cudaMemcpyDeviceToHost);
                 else std::memcpy(got.data(), scratch, size);
                 if (std::memcmp(got.data(), &pattern[src_off], size) != 0) ++bad;
             }
         }
-        std::printf("[scatter_test] verify %s: %zu of %zu slots differ\n", last_write.c_str(), bad,
-                    targets.size() * batch);
+        size_t slots = targets.size() * batch;
+        if (last_write == "broadcast" && grp.uc_addr && !served) {
+            // An NVLS member's own copy receives every multicast broadcast too.
+            for (size_t b = 0; b < batch; ++b, ++slots) {
+                cudaMemcpy(got.data(), static_cast<char *>(grp.uc_addr) + b * size, size, cudaMemcpyDeviceToHost);
+                if (std::memcmp(got.data(), &pattern[b * size], size) != 0) ++bad;
+            }
+        }
+        std::printf("[scatter_test] verify %s: %zu of %zu slots differ\n", last_write.c_str(), bad, slots);
         if (json)
             std::printf("{\"tool\": \"scatter_test\", \"verify\": \"%s\", \"slots\": %zu, \"bad\": %zu}\n",
-                        last_write.c_str(), targets.size() * batch, bad);
+                        last_write.c_str(), slots, bad);
         std::fflush(stdout);
-        if (bad) return 1;
+        if (bad) return finish(1);
     }
     if (!done_file.empty())
         if (FILE *f = std::fopen(done_file.c_str(), "w")) std::fclose(f);
@@ -304,6 +380,5 @@ int main(int argc, char **argv) {
         while (access(hold_file.c_str(), F_OK) != 0 && std::chrono::steady_clock::now() < until)
             std::this_thread::sleep_for(std::chrono::milliseconds(50));
     }
-    comm.shutdown();
-    return 0;
+    return finish(0);
 }

@@ -45,6 +45,7 @@ enum MPCommError {
 };
 
 using TransferHandle = uint64_t;
+struct MulticastGroup;  // defined after MPComm
 static constexpr TransferHandle INVALID_TRANSFER_HANDLE = 0;
 
 // H2D kernel selection for tmaGather/tmaScatter (values as reference
@@ -354,12 +355,43 @@ class MPComm {
     // aligned addresses and lengths; MPCOMM_FUSED_BROADCAST=0 turns them off.
     int registerMulticastMemory(void *uc_addr, size_t length, void *mc_addr, uint64_t group_token,
                                 int group_size);
+    // registerMulticastMemory for a group formed by createMulticastGroup /
+    // joinMulticastGroup (below).
+    int registerMulticastGroup(const MulticastGroup &group);
 
     class Impl;  // opaque implementation type
 
  private:
     std::unique_ptr<Impl> impl_;
 };
+
+// ---------------------------------------------------------------------------
+// NVLS multicast groups between processes of one box (B200 extension; no
+// launcher or collective library needed). One process creates the group,
+// `members - 1` others join it under the same name, in any order and each on
+// its current CUDA device; both calls return once every member has bound a
+// copy of `bytes` (rounded up to the multicast granularity) and mapped the
+// group's multicast address, or fail after `timeout_ms` (the group object is
+// handed over an abstract Unix socket named after the group, so every member
+// must share the creator's network namespace). Returns MPCOMM_SUCCESS,
+// MPCOMM_ERR_DEVICE (a driver call failed, e.g. no multicast support) or
+// MPCOMM_ERR_CONNECTION (a member did not arrive, or left, in time).
+// ---------------------------------------------------------------------------
+struct MulticastGroup {
+    void *uc_addr = nullptr;  // this member's copy (publish it like any buffer)
+    void *mc_addr = nullptr;  // multicast address: a store here reaches every copy
+    size_t length = 0;        // bytes of each copy
+    uint64_t token = 0;       // group identity (the same in every member)
+    int members = 0;
+    int device = -1;
+    uint64_t mc_handle = 0, mem_handle = 0;  // driver handles (released by releaseMulticastGroup)
+};
+int createMulticastGroup(const std::string &name, size_t bytes, int members, MulticastGroup *out,
+                         int timeout_ms = 60000);
+int joinMulticastGroup(const std::string &name, size_t bytes, int members, MulticastGroup *out,
+                       int timeout_ms = 60000);
+// Unmaps and releases this member's part (unregister the copy first).
+int releaseMulticastGroup(MulticastGroup *group);
 
 }  // namespace mpcomm
 

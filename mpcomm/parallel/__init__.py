@@ -228,6 +228,29 @@ class NvlsGroup:
         self.uc = device_view(self.uc_ptr, self.size)
         dist.barrier()
 
+    @classmethod
+    def from_name(cls, name: str, nbytes: int, members: int, create: bool, rank: Optional[int] = None,
+                  timeout_ms: int = 60000) -> "NvlsGroup":
+        """Joins (or, with ``create``, creates) the multicast group ``name`` of
+        ``members`` processes on this box without torch.distributed: the
+        creator hands the group object to the others over an abstract Unix
+        socket named after the group (native ``createMulticastGroup`` /
+        ``joinMulticastGroup``). ``rank`` (default: 0 for the creator, else
+        unset) only selects the slice ``broadcast_from`` pulls."""
+        err, g = _native.multicast_group(name, nbytes, members, create, timeout_ms)
+        if err:
+            raise RuntimeError(f"multicast group {name!r}: error {err}")
+        self = cls.__new__(cls)
+        self.world = members
+        self.rank = (0 if create else -1) if rank is None else rank
+        self.dev = g["device"]
+        self.size = g["length"]
+        self.token = g["token"]
+        self.mc, self.mem = g["mc_handle"], g["mem_handle"]
+        self.uc_ptr, self.mc_ptr = g["uc_addr"], g["mc_addr"]
+        self.uc = device_view(self.uc_ptr, self.size)
+        return self
+
     def broadcast_from(self, root_ptr: int, nbytes: int, max_ctas: int = 0,
                        stream: Optional[torch.cuda.Stream] = None, method: str = "load") -> None:
         """All-source broadcast of ``nbytes`` that sit in the root's HBM at
@@ -250,6 +273,8 @@ class NvlsGroup:
         """
         if nbytes > self.size or nbytes % 16:
             raise ValueError("nbytes must be a multiple of 16 within the group's size")
+        if not 0 <= self.rank < self.world:
+            raise ValueError("broadcast_from needs this member's rank (NvlsGroup.from_name(..., rank=r))")
         sl = (nbytes // self.world + 4095) // 4096 * 4096
         off = min(self.rank * sl, nbytes)
         ln = max(0, min(sl, nbytes - off))

@@ -686,6 +686,33 @@ PYBIND11_MODULE(_mpcomm, m) {
         },
         py::arg("ptr"), py::arg("size"), py::arg("flags") = 0,
         "Driver result of exporting [ptr, ptr+size) as a dma-buf (the fd is closed again).");
+    m.def(
+        "multicast_group",
+        [](const std::string &name, size_t bytes, int members, bool create, int timeout_ms) {
+            mpcomm::MulticastGroup g;
+            int e;
+            {
+                py::gil_scoped_release r;
+                e = create ? mpcomm::createMulticastGroup(name, bytes, members, &g, timeout_ms)
+                           : mpcomm::joinMulticastGroup(name, bytes, members, &g, timeout_ms);
+            }
+            py::dict d;
+            if (e == 0) {
+                d["uc_addr"] = reinterpret_cast<uintptr_t>(g.uc_addr);
+                d["mc_addr"] = reinterpret_cast<uintptr_t>(g.mc_addr);
+                d["length"] = g.length;
+                d["token"] = g.token;
+                d["members"] = g.members;
+                d["device"] = g.device;
+                d["mc_handle"] = g.mc_handle;
+                d["mem_handle"] = g.mem_handle;
+            }
+            return py::make_tuple(e, d);
+        },
+        py::arg("name"), py::arg("bytes"), py::arg("members"), py::arg("create"), py::arg("timeout_ms") = 60000,
+        "(err, group): create (create=True, one process) or join an NVLS multicast group of `members` GPUs by "
+        "name, on the current device, without a launcher; err is an MPCOMM_ERR_* code. Release with "
+        "multicast_teardown(mc_handle, mem_handle, uc_addr, mc_addr, length, device).");
     m.def("multicast_teardown", [](uint64_t mc, uint64_t mem, uintptr_t uc, uintptr_t mcva, size_t size, int dev) {
         return vmm::multicast_teardown(mc, mem, reinterpret_cast<void *>(uc), reinterpret_cast<void *>(mcva), size,
                                        dev);

@@ -3,12 +3,18 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <string>
 #include <set>
 #include <thread>
 #include <vector>
 
+#include <sys/mman.h>
+#include <unistd.h>
+
 #include "core/core.h"
+#include "ctrl/fdshare.h"
 #include "ctrl/wire.h"
+#include "parallel/mcgroup.h"
 #include "topo/topology.h"
 
 using namespace mpcomm;
@@ -141,6 +147,29 @@ static void test_wire_layout() {
           kQosControlFrameMagic == 0x4D505146);
 }
 
+// Descriptor hand-off (VMM handles between processes): an offered fd is
+// fetched back by key through the server's socket as a new descriptor of
+// the same file; unknown and withdrawn keys answer 1, a missing server -1.
+static void test_fd_share() {
+    const std::string name = "mpcomm-test-fd." + std::to_string(getpid());
+    int f = memfd_create("fdshare", 0);
+    CHECK(f >= 0 && ftruncate(f, 4096) == 0);
+    CHECK(pwrite(f, "B200", 4, 0) == 4);
+    CHECK(ctrl::fd_offer(name, 7, f) == 0);
+    int g = -1;
+    CHECK(ctrl::fd_fetch(name, 7, 2000, &g) == 0 && g >= 0 && g != f);
+    char buf[4] = {0};
+    CHECK(pread(g, buf, 4, 0) == 4 && std::memcmp(buf, "B200", 4) == 0);
+    close(g);
+    CHECK(ctrl::fd_fetch(name, 8, 2000, &g) == 1);
+    ctrl::fd_withdraw(7);
+    CHECK(ctrl::fd_fetch(name, 7, 2000, &g) == 1);
+    CHECK(ctrl::fd_fetch(name + ".absent", 7, 200, &g) == -1);
+    // Multicast group names map to one non-zero identity in every process.
+    CHECK(vmm::mc_group_token("grp") == vmm::mc_group_token("grp"));
+    CHECK(vmm::mc_group_token("grp") != vmm::mc_group_token("grp2") && vmm::mc_group_token("") != 0);
+}
+
 int main() {
     test_wrid();
     test_handle_pool();
@@ -149,6 +178,7 @@ int main() {
     test_token_bucket();
     test_topology_parsers();
     test_wire_layout();
+    test_fd_share();
     std::printf("native core tests passed (%d checks)\n", g_checks);
     return 0;
 }

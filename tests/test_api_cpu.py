@@ -467,3 +467,22 @@ print("drain ok", grown)
     env = dict(os.environ, MPCOMM_FABRIC="sock", MPCOMM_LOG_LEVEL="1", PYTHONPATH=ROOT)
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=120)
     assert r.returncode == 0 and "drain ok" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+def test_multicast_group_bounded_without_peers():
+    """createMulticastGroup / joinMulticastGroup fail within their timeout:
+    a joiner with no creator gets MPCOMM_ERR_CONNECTION, a creator on a
+    host without a multicast-capable GPU MPCOMM_ERR_DEVICE (with one, it
+    times out waiting for the second member), bad arguments INVALID_ARG."""
+    import time
+
+    from mpcomm import _native
+    name = f"mpcomm-cpu-test-{os.getpid()}"
+    t0 = time.monotonic()
+    err, g = _native.multicast_group(name, 1 << 20, 2, False, 300)
+    assert err == -4 and g == {} and time.monotonic() - t0 < 10
+    err, g = _native.multicast_group(name, 1 << 20, 2, True, 300)
+    assert err in (-1, -4) and g == {}
+    assert _native.multicast_group(name, 1 << 20, 1, True, 300)[0] == -7
+    assert _native.multicast_group(name, 0, 2, False, 300)[0] == -7
+    assert _native.multicast_group("", 1 << 20, 2, False, 300)[0] == -7

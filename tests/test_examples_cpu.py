@@ -41,3 +41,11 @@ def test_scatter_test_verify_reads_back_every_slot():
 
 def test_check_install():
     assert "install check PASSED" in _run([sys.executable, "-m", "mpcomm.check_install"])
+
+
+def test_scatter_test_nvls_needs_a_gpu():
+    """--nvls makes the process a member of a multicast group of GPU copies:
+    without --gpu it is refused before any group is formed."""
+    r = subprocess.run([os.path.join(ROOT, "examples", "bin", "scatter_test"), "--mode", "both", "--size", "1M",
+                        "--nvls", "g:2"], capture_output=True, text=True, env=ENV, cwd=ROOT, timeout=60)
+    assert r.returncode == 2 and "--nvls needs --gpu" in r.stderr, r.stdout + r.stderr

@@ -127,3 +127,53 @@ def test_scatter_test_broadcast_across_gpus(tmp_path):
                 p.wait(timeout=20)
             except subprocess.TimeoutExpired:
                 p.kill()
+
+
+def test_scatter_test_nvls_broadcast_across_gpus():
+    """scatter_test --nvls: the initiator on GPU 0 creates an NVLS multicast
+    group (native createMulticastGroup, no launcher) that a target process
+    on every other GPU joins and serves its copy of; a broadcast to all the
+    targets then goes out as multicast stores, one gather_bcast_nvls launch
+    per chunk, and every copy (the initiator's own included) reads back
+    bit-exact: the targets' copies are VMM memory, reached by the GETs
+    through their descriptor servers. Targets leave on SIGTERM after
+    releasing their copies."""
+    n = min(torch.cuda.device_count(), 8)
+    if n < 2:
+        pytest.skip("needs >= 2 GPUs")
+    from mpcomm import _native
+    if not all(_native.multicast_supported(d) for d in range(n)):
+        pytest.skip("no NVLS multicast on these GPUs")
+    exe = os.path.join(ROOT, "examples", "bin", "scatter_test")
+    env = dict(os.environ, MPCOMM_LOG_LEVEL="1", MPCOMM_NVL_CHUNK_SIZE=str(16 << 20), MPCOMM_KERNEL_TRACE="256")
+    group = f"scatter-test-{os.getpid()}"
+    procs, targets, outs = [], [], []
+    try:
+        for r in range(1, n):
+            port = _free_port()
+            procs.append(subprocess.Popen([exe, "--mode", "target", "--host-id", f"t{r}", "--gpu", str(r),
+                                           "--tcp-port", str(port), "--buffer-size", "64M",
+                                           "--nvls", f"{group}:{n}"],
+                                          stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, env=env))
+            targets += ["--target", f"t{r}:127.0.0.1:{port}"]
+        r = subprocess.run(["timeout", "-k", "10", "240", exe, "--gpu", "0", *targets, "--size", "32M",
+                            "--batch-size", "2", "--iterations", "2", "--warmup", "1", "--test-type", "broadcast",
+                            "--nvls", f"{group}:{n}", "--nvls-create", "--verify", "--json"],
+                           capture_output=True, text=True, env=env, cwd=ROOT)
+        assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+        lines = [json.loads(x) for x in r.stdout.splitlines() if x.startswith("{")]
+        bench = next(x for x in lines if x.get("test") == "broadcast")
+        check = next(x for x in lines if "verify" in x)
+        assert check["bad"] == 0 and check["slots"] == 2 * n, check  # n - 1 targets + own copy
+        assert bench["nvls_member"] and bench["kernel_kinds"] == {"gather_bcast_nvls": 8}, bench
+    finally:
+        for p in procs:
+            p.terminate()
+        for p in procs:
+            try:
+                outs.append(p.communicate(timeout=30)[0])
+            except subprocess.TimeoutExpired:
+                p.kill()
+                outs.append(p.communicate()[0])
+    for p, out in zip(procs, outs):
+        assert p.returncode == 0 and "stopping" in out, out[-2000:]

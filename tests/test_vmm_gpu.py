@@ -1,0 +1,97 @@
+"""VMM (cuMemCreate) memory between processes over the GPU fabric.
+
+CUDA IPC cannot export VMM allocations (NVLS group copies, GPUDirect
+buffers from gdr_alloc, allocator pools built on cuMemMap), so the nvl
+fabric offers such a registration as the allocation's POSIX handle on the
+owner's descriptor server; a peer fetches it over the Unix socket, maps it
+and its kernels then PUT/GET it like cudaMalloc memory. Two processes on
+one GPU: the target serves a gdr_alloc buffer, the initiator writes it,
+reads it back, and the target checks its own bytes.
+"""
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+TARGET = r"""
+import os, sys, time, zlib, torch, mpcomm
+from mpcomm import parallel
+d = sys.argv[1]
+torch.cuda.set_device(0)
+n = 24 << 20
+err, ptr, size = mpcomm._native.gdr_alloc(0, n)
+assert err == 0 and size >= n, (err, size)
+buf = parallel.device_view(ptr, n)
+buf.zero_(); torch.cuda.synchronize()
+c = mpcomm.MPComm()
+assert c.init("vt") == 0 and c.get_fabric_name() == "nvl"
+assert c.register_memory(ptr, n) == 0 and c.publish_buffer(ptr, n) == 0
+assert c.start_accept_thread() == 0
+open(os.path.join(d, "port.tmp"), "w").write(str(c.get_tcp_port()))
+os.rename(os.path.join(d, "port.tmp"), os.path.join(d, "port"))
+deadline = time.time() + 120
+while not os.path.exists(os.path.join(d, "crc")):
+    assert time.time() < deadline, "initiator never finished"
+    time.sleep(0.05)
+want = int(open(os.path.join(d, "crc")).read())
+torch.cuda.synchronize()
+got = zlib.crc32(buf.cpu().numpy().tobytes())
+c.unpublish_buffer(ptr); c.unregister_memory(ptr)
+c.shutdown()
+mpcomm._native.gdr_free(ptr, size)
+assert got == want, (got, want)
+print("target bytes ok")
+"""
+
+INITIATOR = r"""
+import os, sys, time, zlib, torch, mpcomm
+d = sys.argv[1]
+torch.cuda.set_device(0)
+n = 24 << 20
+deadline = time.time() + 120
+while not os.path.exists(os.path.join(d, "port")):
+    assert time.time() < deadline, "target never served"
+    time.sleep(0.05)
+port = int(open(os.path.join(d, "port")).read())
+src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+back = torch.zeros(n, dtype=torch.uint8, device="cuda")
+c = mpcomm.MPComm()
+assert c.init("vi") == 0 and c.get_fabric_name() == "nvl"
+for t in (src, back):
+    assert c.register_memory(t.data_ptr(), n) == 0
+assert c.connect("vt", "127.0.0.1", port) == 0
+raddr = c.query_remote_buffers("vt", "127.0.0.1", port)["buffers"][0]["addr"]
+h = c.put_async(src.data_ptr(), "vt", raddr, n)
+assert h != mpcomm.INVALID_TRANSFER_HANDLE and c.wait_transfer(h, 60000) == 0
+c.release_transfer(h)
+h = c.get_async(back.data_ptr(), "vt", raddr, n)
+assert h != mpcomm.INVALID_TRANSFER_HANDLE and c.wait_transfer(h, 60000) == 0
+c.release_transfer(h)
+torch.cuda.synchronize()
+assert torch.equal(back, src), "GET of the VMM buffer differs from the PUT"
+crc = zlib.crc32(src.cpu().numpy().tobytes())
+open(os.path.join(d, "crc.tmp"), "w").write(str(crc))
+os.rename(os.path.join(d, "crc.tmp"), os.path.join(d, "crc"))
+c.shutdown()
+print("initiator vmm ok")
+"""
+
+
+def test_put_get_vmm_buffer_of_another_process(tmp_path):
+    env = dict(os.environ, MPCOMM_LOG_LEVEL="1", MPCOMM_FABRIC="nvl")
+    t = subprocess.Popen(["timeout", "-k", "10", "180", sys.executable, "-c", TARGET, str(tmp_path)], cwd=ROOT,
+                         env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    try:
+        r = subprocess.run(["timeout", "-k", "10", "180", sys.executable, "-c", INITIATOR, str(tmp_path)], cwd=ROOT,
+                           env=env, capture_output=True, text=True)
+        assert r.returncode == 0 and "initiator vmm ok" in r.stdout, r.stdout[-3000:] + r.stderr[-3000:]
+        out, _ = t.communicate(timeout=120)
+        assert t.returncode == 0 and "target bytes ok" in out, out[-3000:]
+    finally:
+        if t.poll() is None:
+            t.kill()
+            t.wait()
