@@ -176,48 +176,100 @@ int multicast_bind_local(uint64_t mc, size_t size, int dev, uint64_t *mem, void 
 
 int multicast_map(uint64_t mc, size_t size, int dev, void **mc_va) { return map_rw(mc, size, dev, mc_va); }
 
-int vmm_export(const void *ptr, uintptr_t *base, size_t *size, int *fd) {
+int vmm_segments(const void *ptr, size_t len, size_t max_segments, std::vector<VmmSegment> *out) {
     auto retain = sym<CUresult (*)(CUmemGenericAllocationHandle *, void *)>("cuMemRetainAllocationHandle");
     auto range = sym<CUresult (*)(CUdeviceptr *, size_t *, CUdeviceptr)>("cuMemGetAddressRange");
+    auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
+    if (!retain || !range || !rel) return kNoDriver;
+    out->clear();
+    const CUdeviceptr end = reinterpret_cast<CUdeviceptr>(ptr) + len;
+    CUdeviceptr p = reinterpret_cast<CUdeviceptr>(ptr);
+    while (p < end) {
+        CUdeviceptr b = 0;
+        size_t n = 0;
+        CUresult r = range(&b, &n, p);
+        if (r != CUDA_SUCCESS) return r;
+        // Contiguous: after the first, each allocation starts where the
+        // previous one ended.
+        if (n == 0 || (!out->empty() && b != p) || out->size() >= max_segments) return -1;
+        // One allocation per range: its first and last bytes share a handle.
+        CUmemGenericAllocationHandle h = 0, last = 0;
+        r = retain(&h, reinterpret_cast<void *>(b));
+        if (r != CUDA_SUCCESS) return r;
+        r = retain(&last, reinterpret_cast<void *>(b + n - 1));
+        if (r == CUDA_SUCCESS) rel(last);
+        rel(h);
+        if (r != CUDA_SUCCESS) return r;
+        if (last != h) return -1;
+        out->push_back(VmmSegment{static_cast<uintptr_t>(b), n});
+        p = b + n;
+    }
+    return out->empty() ? -1 : 0;
+}
+
+int vmm_export_fd(uintptr_t base, int *fd) {
+    auto retain = sym<CUresult (*)(CUmemGenericAllocationHandle *, void *)>("cuMemRetainAllocationHandle");
     auto exp = sym<CUresult (*)(void *, CUmemGenericAllocationHandle, CUmemAllocationHandleType,
                                 unsigned long long)>("cuMemExportToShareableHandle");
     auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
-    if (!retain || !range || !exp || !rel) return kNoDriver;
-    CUdeviceptr b = 0;
-    size_t n = 0;
-    CUresult r = range(&b, &n, reinterpret_cast<CUdeviceptr>(ptr));
+    if (!retain || !exp || !rel) return kNoDriver;
+    CUmemGenericAllocationHandle h = 0;
+    CUresult r = retain(&h, reinterpret_cast<void *>(base));
     if (r != CUDA_SUCCESS) return r;
-    CUmemGenericAllocationHandle h = 0, last = 0;
-    r = retain(&h, reinterpret_cast<void *>(b));
-    if (r != CUDA_SUCCESS) return r;
-    // The whole range must be one allocation: its last byte has the same one.
-    r = retain(&last, reinterpret_cast<void *>(b + n - 1));
-    if (r == CUDA_SUCCESS) rel(last);
-    if (r != CUDA_SUCCESS || last != h) {
-        rel(h);
-        return r != CUDA_SUCCESS ? static_cast<int>(r) : -1;
-    }
     int f = -1;
     r = exp(&f, h, CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR, 0);
     rel(h);
     if (r != CUDA_SUCCESS) return r;
-    *base = static_cast<uintptr_t>(b);
-    *size = n;
     *fd = f;
     return 0;
 }
 
-int vmm_import_map(int fd, size_t size, int dev, void **va) {
+int vmm_import_map(const int *fds, const size_t *sizes, size_t n, int dev, void **va) {
     auto imp = sym<CUresult (*)(CUmemGenericAllocationHandle *, void *, CUmemAllocationHandleType)>(
         "cuMemImportFromShareableHandle");
+    auto reserve = sym<CUresult (*)(CUdeviceptr *, size_t, size_t, CUdeviceptr, unsigned long long)>(
+        "cuMemAddressReserve");
+    auto map = sym<CUresult (*)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long)>(
+        "cuMemMap");
+    auto access = sym<CUresult (*)(CUdeviceptr, size_t, const CUmemAccessDesc *, size_t)>("cuMemSetAccess");
+    auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
+    auto vfree = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree");
     auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
-    if (!imp || !rel) return kNoDriver;
-    CUmemGenericAllocationHandle h = 0;
-    CUresult r = imp(&h, reinterpret_cast<void *>(static_cast<uintptr_t>(fd)), CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+    if (!imp || !reserve || !map || !access || !unmap || !vfree || !rel) return kNoDriver;
+    if (n == 0) return CUDA_ERROR_INVALID_VALUE;
+    size_t total = 0;
+    for (size_t i = 0; i < n; ++i) total += sizes[i];
+    CUdeviceptr p = 0;
+    CUresult r = reserve(&p, total, 0, 0, 0);
     if (r != CUDA_SUCCESS) return r;
-    const int e = map_rw(h, size, dev, va);
-    rel(h);  // the mapping holds the allocation from here on
-    return e;
+    size_t mapped = 0;  // bytes mapped so far, from p
+    for (size_t i = 0; i < n && r == CUDA_SUCCESS; ++i) {
+        CUmemGenericAllocationHandle h = 0;
+        r = imp(&h, reinterpret_cast<void *>(static_cast<uintptr_t>(fds[i])), CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+        if (r != CUDA_SUCCESS) break;
+        r = map(p + mapped, sizes[i], 0, h, 0);
+        rel(h);  // the mapping holds the allocation from here on
+        if (r == CUDA_SUCCESS) mapped += sizes[i];
+    }
+    if (r == CUDA_SUCCESS) {
+        CUmemAccessDesc a;
+        std::memset(&a, 0, sizeof(a));
+        a.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
+        a.location.id = dev;
+        a.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
+        r = access(p, total, &a, 1);
+    }
+    if (r != CUDA_SUCCESS) {
+        size_t off = 0;
+        for (size_t i = 0; i < n && off < mapped; ++i) {
+            unmap(p + off, sizes[i]);
+            off += sizes[i];
+        }
+        vfree(p, total);
+        return r;
+    }
+    *va = reinterpret_cast<void *>(p);
+    return 0;
 }
 
 int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev) {

@@ -13,6 +13,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <vector>
 
 namespace mpcomm {
 namespace vmm {
@@ -41,15 +42,26 @@ int multicast_map(uint64_t mc, size_t size, int dev, void **mc_va);
 // Unmaps/unbinds/releases everything created above (any argument may be 0).
 int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev);
 
-// VMM (cuMemCreate) memory across processes, where CUDA IPC cannot go:
-// vmm_export: the allocation mapped at `ptr` as a POSIX file descriptor
-// (*fd, owned by the caller) with the mapped range [*base, *base + *size).
-// Fails (non-zero) for memory that is not a VMM allocation, one created
-// without a POSIX-fd handle type, or a range made of several allocations.
-int vmm_export(const void *ptr, uintptr_t *base, size_t *size, int *fd);
-// vmm_import_map: imports `fd` (not consumed) and maps its `size` bytes at
-// a new address readable and writable by device `dev`.
-int vmm_import_map(int fd, size_t size, int dev, void **va);
+// VMM (cuMemCreate) memory across processes, where CUDA IPC cannot go.
+// One allocation of the range a caller registers; a range may be backed by
+// several (an allocator that grows a reserved range page by page, e.g.
+// PyTorch's expandable segments), mapped back to back.
+struct VmmSegment {
+    uintptr_t base;
+    size_t size;
+};
+// vmm_segments: the allocations backing [ptr, ptr + len), contiguous and in
+// address order, at most `max_segments`. Non-zero for memory that is not
+// VMM-mapped or has a hole.
+int vmm_segments(const void *ptr, size_t len, size_t max_segments, std::vector<VmmSegment> *out);
+// vmm_export_fd: the allocation mapped at `base` as a POSIX file descriptor
+// (owned by the caller); fails for allocations created without that handle
+// type.
+int vmm_export_fd(uintptr_t base, int *fd);
+// vmm_import_map: imports `n` allocations (fds[i] of sizes[i] bytes; the
+// descriptors are not consumed) and maps them back to back at a new address
+// readable and writable by device `dev`.
+int vmm_import_map(const int *fds, const size_t *sizes, size_t n, int dev, void **va);
 
 // HBM that a NIC can register through dma-buf (GPUDirect RDMA): a VMM
 // allocation of `dev` created with the gpuDirectRDMACapable flag, `size`

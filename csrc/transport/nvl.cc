@@ -18,9 +18,10 @@
 //     published in /dev/shm/mpcomm-nvl.<boot>.<pid> (key, range, CUDA IPC
 //     handle) and opened with cudaIpcOpenMemHandle on first use; VMM
 //     (cuMemCreate) memory, which CUDA IPC cannot export (NVLS group copies,
-//     GPUDirect buffers), is offered instead as the allocation's POSIX
-//     handle on the owner's descriptor server (abstract Unix socket
-//     mpcomm-fd.<boot>.<pid>) and imported + mapped by the peer on first use,
+//     GPUDirect buffers, PyTorch expandable segments), is offered instead as
+//     the POSIX handles of its allocations on the owner's descriptor server
+//     (abstract Unix socket mpcomm-fd.<boot>.<pid>) and imported + mapped
+//     back to back by the peer on first use,
 //   * another process's host memory when it is a shared file mapping
 //     (/dev/shm, hugetlbfs, any MAP_SHARED file): the record carries the
 //     file path and offset; the peer maps the same pages, pins them and
@@ -44,6 +45,7 @@
 #include <mutex>
 #include <tuple>
 #include <unordered_map>
+#include <vector>
 
 #include "core/core.h"
 #include "core/nvtx.h"
@@ -197,21 +199,34 @@ class Registry {
                 // Not a cudaMalloc allocation: offer it as a VMM handle, else
                 // it stays usable in-process only.
                 std::memset(ipc, 0, sizeof(ipc));
-                uintptr_t vb = 0;
-                size_t vn = 0;
+                std::vector<vmm::VmmSegment> segs;
                 int fd = -1;
-                if (vmm::vmm_export(addr, &vb, &vn, &fd) != 0) {
+                if (vmm::vmm_segments(addr, len, ctrl::kFdMaxSegments, &segs) != 0 ||
+                    vmm::vmm_export_fd(segs[0].base, &fd) != 0) {
                     MPCOMM_LOG_DEBUG("MPComm[nvl]: device range %p+%zu is not exportable; other processes "
                                      "will not reach it\n", addr, len);
-                } else if (r.addr < vb || r.addr + len > vb + vn) {
-                    // A peer maps exactly [vb, vb + vn): the range must lie inside.
-                    MPCOMM_LOG_DEBUG("MPComm[nvl]: %p+%zu spans several VMM allocations; other processes "
-                                     "will not reach it\n", addr, len);
-                    close(fd);
-                } else if (ctrl::fd_offer(fd_service(getpid()), next_key_, fd) == 0) {
-                    r.vmm = true;  // offered under the key assigned below
-                    r.base = vb;
-                    r.alloc_size = vn;
+                } else {
+                    close(fd);  // exportable; the server exports afresh per request
+                    const uintptr_t vb = segs[0].base;
+                    auto provide = [segs, vb](std::vector<ctrl::FdSegment> *out) {
+                        for (const auto &g : segs) {
+                            ctrl::FdSegment f;
+                            f.offset = g.base - vb;
+                            f.size = g.size;
+                            if (vmm::vmm_export_fd(g.base, &f.fd) != 0) {
+                                for (auto &o : *out) close(o.fd);
+                                out->clear();
+                                return false;
+                            }
+                            out->push_back(f);
+                        }
+                        return true;
+                    };
+                    if (ctrl::fd_offer(fd_service(getpid()), next_key_, provide) == 0) {
+                        r.vmm = true;  // offered under the key assigned below
+                        r.base = vb;
+                        r.alloc_size = segs.back().base + segs.back().size - vb;
+                    }
                 }
             }
         } else {
@@ -494,25 +509,39 @@ class RemoteMaps {
         return 0;
     }
 
-    // VMM allocation of `pid`: fetch its handle from the owner's descriptor
-    // server and map it for `dev`, once per (pid, key, dev) (keys are never
-    // reused, so a re-registered range is mapped afresh).
+    // VMM memory of `pid`: fetch the handles of the allocations behind the
+    // registration from the owner's descriptor server and map them back to
+    // back for `dev`, once per (pid, key, dev) (keys are never reused, so a
+    // re-registered range is mapped afresh).
     int resolve_vmm(long pid, const DirRecord &rec, uintptr_t addr, int dev, uintptr_t *out) {
         auto mk = std::make_tuple(pid, rec.key, dev);
         auto it = vmm_opened_.find(mk);
         if (it == vmm_opened_.end()) {
-            int fd = -1;
-            const int fr = ctrl::fd_fetch(fd_service(pid), rec.key, 5000, &fd);
+            std::vector<ctrl::FdSegment> segs;
+            const int fr = ctrl::fd_fetch(fd_service(pid), rec.key, 5000, &segs);
             if (fr != 0) {
-                MPCOMM_LOG_ERROR("MPComm[nvl]: VMM handle of pid %ld's buffer 0x%lx: %s\n", pid,
+                MPCOMM_LOG_ERROR("MPComm[nvl]: VMM handles of pid %ld's buffer 0x%lx: %s\n", pid,
                                  static_cast<unsigned long>(rec.addr), fr == 1 ? "withdrawn" : "server unreachable");
                 return kWcRemAccessErr;
             }
+            // The owner's layout, back to back from offset 0 to alloc_size.
+            std::vector<int> fds;
+            std::vector<size_t> sizes;
+            uint64_t next = 0;
+            bool shaped = true;
+            for (const auto &g : segs) {
+                shaped &= g.offset == next;
+                next = g.offset + g.size;
+                fds.push_back(g.fd);
+                sizes.push_back(static_cast<size_t>(g.size));
+            }
+            shaped &= next == rec.alloc_size;
             void *p = nullptr;
-            const int e = vmm::vmm_import_map(fd, rec.alloc_size, dev, &p);
-            close(fd);
+            const int e = shaped ? vmm::vmm_import_map(fds.data(), sizes.data(), fds.size(), dev, &p) : -1;
+            for (int f : fds) close(f);
             if (e != 0) {
-                MPCOMM_LOG_ERROR("MPComm[nvl]: mapping pid %ld's VMM buffer failed (%d)\n", pid, e);
+                MPCOMM_LOG_ERROR("MPComm[nvl]: mapping pid %ld's VMM buffer (%zu allocations) failed (%d)\n", pid,
+                                 segs.size(), e);
                 return kWcRemAccessErr;
             }
             it = vmm_opened_.emplace(mk, reinterpret_cast<uintptr_t>(p)).first;

@@ -687,6 +687,18 @@ PYBIND11_MODULE(_mpcomm, m) {
         py::arg("ptr"), py::arg("size"), py::arg("flags") = 0,
         "Driver result of exporting [ptr, ptr+size) as a dma-buf (the fd is closed again).");
     m.def(
+        "vmm_segments",
+        [](uintptr_t ptr, size_t len) {
+            std::vector<vmm::VmmSegment> segs;
+            const int e = vmm::vmm_segments(reinterpret_cast<void *>(ptr), len, 1u << 20, &segs);
+            py::list out;
+            for (const auto &g : segs) out.append(py::make_tuple(g.base, g.size));
+            return py::make_tuple(e, out);
+        },
+        py::arg("ptr"), py::arg("length"),
+        "(err, [(base, size), ...]): the VMM allocations behind [ptr, ptr+length) (err != 0 for memory that is "
+        "not VMM-mapped, e.g. cudaMalloc).");
+    m.def(
         "multicast_group",
         [](const std::string &name, size_t bytes, int members, bool create, int timeout_ms) {
             mpcomm::MulticastGroup g;

@@ -147,24 +147,37 @@ static void test_wire_layout() {
           kQosControlFrameMagic == 0x4D505146);
 }
 
-// Descriptor hand-off (VMM handles between processes): an offered fd is
-// fetched back by key through the server's socket as a new descriptor of
-// the same file; unknown and withdrawn keys answer 1, a missing server -1.
+// Descriptor hand-off (VMM handles between processes): an offer's provider
+// runs per request and its descriptors arrive as new descriptors of the same
+// files, with their offsets, also past one message (64 per message);
+// unknown and withdrawn keys and a failing provider answer 1, a missing
+// server -1.
 static void test_fd_share() {
     const std::string name = "mpcomm-test-fd." + std::to_string(getpid());
     int f = memfd_create("fdshare", 0);
     CHECK(f >= 0 && ftruncate(f, 4096) == 0);
     CHECK(pwrite(f, "B200", 4, 0) == 4);
-    CHECK(ctrl::fd_offer(name, 7, f) == 0);
-    int g = -1;
-    CHECK(ctrl::fd_fetch(name, 7, 2000, &g) == 0 && g >= 0 && g != f);
-    char buf[4] = {0};
-    CHECK(pread(g, buf, 4, 0) == 4 && std::memcmp(buf, "B200", 4) == 0);
-    close(g);
-    CHECK(ctrl::fd_fetch(name, 8, 2000, &g) == 1);
+    int calls = 0;
+    CHECK(ctrl::fd_offer(name, 7, [f, &calls](std::vector<ctrl::FdSegment> *out) {
+              ++calls;
+              for (int i = 0; i < 70; ++i) out->push_back(ctrl::FdSegment{uint64_t(i) * 4096, 4096, dup(f)});
+              return true;
+          }) == 0);
+    CHECK(ctrl::fd_offer(name, 9, [](std::vector<ctrl::FdSegment> *) { return false; }) == 0);
+    std::vector<ctrl::FdSegment> got;
+    CHECK(ctrl::fd_fetch(name, 7, 2000, &got) == 0 && got.size() == 70 && calls == 1);
+    for (size_t i = 0; i < got.size(); ++i) {
+        char buf[4] = {0};
+        CHECK(got[i].offset == i * 4096 && got[i].size == 4096 && got[i].fd != f);
+        CHECK(pread(got[i].fd, buf, 4, 0) == 4 && std::memcmp(buf, "B200", 4) == 0);
+        close(got[i].fd);
+    }
+    CHECK(ctrl::fd_fetch(name, 8, 2000, &got) == 1 && got.empty());
+    CHECK(ctrl::fd_fetch(name, 9, 2000, &got) == 1 && got.empty());
     ctrl::fd_withdraw(7);
-    CHECK(ctrl::fd_fetch(name, 7, 2000, &g) == 1);
-    CHECK(ctrl::fd_fetch(name + ".absent", 7, 200, &g) == -1);
+    CHECK(ctrl::fd_fetch(name, 7, 2000, &got) == 1);
+    CHECK(ctrl::fd_fetch(name + ".absent", 7, 200, &got) == -1);
+    close(f);
     // Multicast group names map to one non-zero identity in every process.
     CHECK(vmm::mc_group_token("grp") == vmm::mc_group_token("grp"));
     CHECK(vmm::mc_group_token("grp") != vmm::mc_group_token("grp2") && vmm::mc_group_token("") != 0);

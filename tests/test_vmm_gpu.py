@@ -1,12 +1,14 @@
 """VMM (cuMemCreate) memory between processes over the GPU fabric.
 
 CUDA IPC cannot export VMM allocations (NVLS group copies, GPUDirect
-buffers from gdr_alloc, allocator pools built on cuMemMap), so the nvl
-fabric offers such a registration as the allocation's POSIX handle on the
-owner's descriptor server; a peer fetches it over the Unix socket, maps it
-and its kernels then PUT/GET it like cudaMalloc memory. Two processes on
-one GPU: the target serves a gdr_alloc buffer, the initiator writes it,
-reads it back, and the target checks its own bytes.
+buffers from gdr_alloc, PyTorch's expandable segments), so the nvl fabric
+offers such a registration as the POSIX handles of the allocations behind
+it on the owner's descriptor server; a peer fetches them over the Unix
+socket, maps them back to back, and its kernels then PUT/GET the range like
+cudaMalloc memory. Two processes on one GPU: the target serves a gdr_alloc
+buffer (one allocation) or a tensor of an expandable segment (several
+allocations), the initiator writes it, reads it back, and the target checks
+its own bytes.
 """
 import os
 import subprocess
@@ -20,12 +22,19 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 TARGET = r"""
 import os, sys, time, zlib, torch, mpcomm
 from mpcomm import parallel
-d = sys.argv[1]
+d, kind = sys.argv[1], sys.argv[2]
 torch.cuda.set_device(0)
-n = 24 << 20
-err, ptr, size = mpcomm._native.gdr_alloc(0, n)
-assert err == 0 and size >= n, (err, size)
-buf = parallel.device_view(ptr, n)
+n = 64 << 20
+if kind == "gdr":
+    err, ptr, size = mpcomm._native.gdr_alloc(0, n)
+    assert err == 0 and size >= n, (err, size)
+    buf = parallel.device_view(ptr, n)
+else:  # PYTORCH_CUDA_ALLOC_CONF=expandable_segments:True
+    torch.empty(3 << 20, dtype=torch.uint8, device="cuda")  # start mid-page
+    buf = torch.empty(n, dtype=torch.uint8, device="cuda")
+    ptr = buf.data_ptr()
+    err, segs = mpcomm._native.vmm_segments(ptr, n)
+    assert err == 0 and len(segs) >= 2, (err, segs)
 buf.zero_(); torch.cuda.synchronize()
 c = mpcomm.MPComm()
 assert c.init("vt") == 0 and c.get_fabric_name() == "nvl"
@@ -42,7 +51,8 @@ torch.cuda.synchronize()
 got = zlib.crc32(buf.cpu().numpy().tobytes())
 c.unpublish_buffer(ptr); c.unregister_memory(ptr)
 c.shutdown()
-mpcomm._native.gdr_free(ptr, size)
+if kind == "gdr":
+    mpcomm._native.gdr_free(ptr, size)
 assert got == want, (got, want)
 print("target bytes ok")
 """
@@ -51,7 +61,7 @@ INITIATOR = r"""
 import os, sys, time, zlib, torch, mpcomm
 d = sys.argv[1]
 torch.cuda.set_device(0)
-n = 24 << 20
+n = 64 << 20
 deadline = time.time() + 120
 while not os.path.exists(os.path.join(d, "port")):
     assert time.time() < deadline, "target never served"
@@ -81,10 +91,12 @@ print("initiator vmm ok")
 """
 
 
-def test_put_get_vmm_buffer_of_another_process(tmp_path):
+@pytest.mark.parametrize("kind", ["gdr", "expandable"])
+def test_put_get_vmm_buffer_of_another_process(tmp_path, kind):
     env = dict(os.environ, MPCOMM_LOG_LEVEL="1", MPCOMM_FABRIC="nvl")
-    t = subprocess.Popen(["timeout", "-k", "10", "180", sys.executable, "-c", TARGET, str(tmp_path)], cwd=ROOT,
-                         env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    tenv = dict(env, PYTORCH_CUDA_ALLOC_CONF="expandable_segments:True") if kind == "expandable" else env
+    t = subprocess.Popen(["timeout", "-k", "10", "180", sys.executable, "-c", TARGET, str(tmp_path), kind], cwd=ROOT,
+                         env=tenv, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
     try:
         r = subprocess.run(["timeout", "-k", "10", "180", sys.executable, "-c", INITIATOR, str(tmp_path)], cwd=ROOT,
                            env=env, capture_output=True, text=True)
