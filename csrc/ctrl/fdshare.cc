@@ -7,7 +7,9 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cctype>
 #include <cerrno>
+#include <cstdio>
 #include <chrono>
 #include <cstring>
 #include <map>
@@ -172,6 +174,20 @@ class Server {
 };
 
 }  // namespace
+
+std::string fd_service_name(long pid) {
+    static const std::string boot = [] {
+        std::string s;
+        if (FILE *f = std::fopen("/proc/sys/kernel/random/boot_id", "r")) {
+            int c;
+            while ((c = std::fgetc(f)) != EOF && s.size() < 8)
+                if (std::isxdigit(c)) s.push_back(static_cast<char>(c));
+            std::fclose(f);
+        }
+        return s.empty() ? std::string("00000000") : s;
+    }();
+    return "mpcomm-fd." + boot + "." + std::to_string(pid);
+}
 
 int fd_offer(const std::string &name, uint64_t key, FdProvider provider) {
     return Server::get().offer(name, key, std::move(provider));

@@ -28,6 +28,9 @@ using FdProvider = std::function<bool(std::vector<FdSegment> *)>;
 
 constexpr size_t kFdMaxSegments = 4096;
 
+// Abstract socket name of process `pid`'s server on this host (boot-unique).
+std::string fd_service_name(long pid);
+
 // Offers `provider` under `key` on this process's server, whose abstract
 // socket name is `name` (the same for every offer of the process). 0, or -1
 // when the server cannot listen.

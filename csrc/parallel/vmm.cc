@@ -6,6 +6,7 @@
 
 #include <cstring>
 
+#include "ctrl/fdshare.h"
 #include "cuda/gpu.h"
 #include "mpcomm_log.h"
 
@@ -337,6 +338,69 @@ int dmabuf_export(const void *ptr, size_t size, unsigned long long flags, int *f
         "cuMemGetHandleForAddressRange");
     if (!fn) return kNoDriver;
     return fn(fd, reinterpret_cast<CUdeviceptr>(ptr), size, CU_MEM_RANGE_HANDLE_TYPE_DMA_BUF_FD, flags);
+}
+
+int vmm_offer(const void *ptr, size_t len, uint64_t key, uintptr_t *base, size_t *span) {
+    std::vector<VmmSegment> segs;
+    int e = vmm_segments(ptr, len, ctrl::kFdMaxSegments, &segs);
+    if (e) return e;
+    int fd = -1;
+    if ((e = vmm_export_fd(segs[0].base, &fd))) return e;  // created without a POSIX handle type?
+    close(fd);
+    const uintptr_t b = segs[0].base;
+    auto provide = [segs, b](std::vector<ctrl::FdSegment> *out) {
+        for (const auto &g : segs) {
+            ctrl::FdSegment f;
+            f.offset = g.base - b;
+            f.size = g.size;
+            if (vmm_export_fd(g.base, &f.fd) != 0) {
+                for (auto &o : *out) close(o.fd);
+                out->clear();
+                return false;
+            }
+            out->push_back(f);
+        }
+        return true;
+    };
+    if (ctrl::fd_offer(ctrl::fd_service_name(getpid()), key, provide) != 0) return -1;
+    *base = b;
+    *span = segs.back().base + segs.back().size - b;
+    return 0;
+}
+
+void vmm_withdraw(uint64_t key) { ctrl::fd_withdraw(key); }
+
+int vmm_open(long pid, uint64_t key, int dev, int timeout_ms, void **va, std::vector<size_t> *sizes) {
+    std::vector<ctrl::FdSegment> segs;
+    const int fr = ctrl::fd_fetch(ctrl::fd_service_name(pid), key, timeout_ms, &segs);
+    if (fr != 0) return fr;
+    // The owner's layout, back to back from offset 0.
+    std::vector<int> fds;
+    sizes->clear();
+    uint64_t next = 0;
+    bool shaped = true;
+    for (const auto &g : segs) {
+        shaped &= g.offset == next && g.size > 0;
+        next = g.offset + g.size;
+        fds.push_back(g.fd);
+        sizes->push_back(static_cast<size_t>(g.size));
+    }
+    const int e = shaped ? vmm_import_map(fds.data(), sizes->data(), fds.size(), dev, va) : CUDA_ERROR_INVALID_VALUE;
+    for (int f : fds) close(f);
+    return e;
+}
+
+int vmm_unmap(void *va, const std::vector<size_t> &sizes) {
+    auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
+    auto vfree = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree");
+    if (!unmap || !vfree) return kNoDriver;
+    const CUdeviceptr p = reinterpret_cast<CUdeviceptr>(va);
+    size_t off = 0;
+    for (size_t n : sizes) {
+        unmap(p + off, n);
+        off += n;
+    }
+    return vfree(p, off);
 }
 
 }  // namespace vmm

@@ -49,7 +49,6 @@
 
 #include "core/core.h"
 #include "core/nvtx.h"
-#include "ctrl/fdshare.h"
 #include "cuda/gpu.h"
 #include "kernels/launch.h"
 #include "mpcomm.h"
@@ -137,9 +136,6 @@ std::string dir_path(long pid) {
     return "/dev/shm/mpcomm-nvl." + boot_tag() + "." + std::to_string(pid);
 }
 
-// Abstract socket of process `pid`'s descriptor server (VMM handles).
-std::string fd_service(long pid) { return "mpcomm-fd." + boot_tag() + "." + std::to_string(pid); }
-
 struct Region {
     uint32_t key;
     uintptr_t addr;
@@ -199,34 +195,15 @@ class Registry {
                 // Not a cudaMalloc allocation: offer it as a VMM handle, else
                 // it stays usable in-process only.
                 std::memset(ipc, 0, sizeof(ipc));
-                std::vector<vmm::VmmSegment> segs;
-                int fd = -1;
-                if (vmm::vmm_segments(addr, len, ctrl::kFdMaxSegments, &segs) != 0 ||
-                    vmm::vmm_export_fd(segs[0].base, &fd) != 0) {
+                uintptr_t vb = 0;
+                size_t span = 0;
+                if (vmm::vmm_offer(addr, len, next_key_, &vb, &span) == 0) {
+                    r.vmm = true;  // offered under the key assigned below
+                    r.base = vb;
+                    r.alloc_size = span;
+                } else {
                     MPCOMM_LOG_DEBUG("MPComm[nvl]: device range %p+%zu is not exportable; other processes "
                                      "will not reach it\n", addr, len);
-                } else {
-                    close(fd);  // exportable; the server exports afresh per request
-                    const uintptr_t vb = segs[0].base;
-                    auto provide = [segs, vb](std::vector<ctrl::FdSegment> *out) {
-                        for (const auto &g : segs) {
-                            ctrl::FdSegment f;
-                            f.offset = g.base - vb;
-                            f.size = g.size;
-                            if (vmm::vmm_export_fd(g.base, &f.fd) != 0) {
-                                for (auto &o : *out) close(o.fd);
-                                out->clear();
-                                return false;
-                            }
-                            out->push_back(f);
-                        }
-                        return true;
-                    };
-                    if (ctrl::fd_offer(fd_service(getpid()), next_key_, provide) == 0) {
-                        r.vmm = true;  // offered under the key assigned below
-                        r.base = vb;
-                        r.alloc_size = segs.back().base + segs.back().size - vb;
-                    }
                 }
             }
         } else {
@@ -265,7 +242,7 @@ class Registry {
         if (it == regions_.end()) return MPCOMM_ERR_INVALID_ARG;
         if (--it->second.refs > 0) return 0;
         if (it->second.pinned_by_us) gpu::host_unpin(reinterpret_cast<void *>(it->second.addr));
-        if (it->second.vmm) ctrl::fd_withdraw(key);
+        if (it->second.vmm) vmm::vmm_withdraw(key);
         if (dir_ && it->second.slot < kDirSlots) {
             DirRecord *rec = records() + it->second.slot;
             __atomic_store_n(&rec->state, 0u, __ATOMIC_RELEASE);
@@ -517,31 +494,19 @@ class RemoteMaps {
         auto mk = std::make_tuple(pid, rec.key, dev);
         auto it = vmm_opened_.find(mk);
         if (it == vmm_opened_.end()) {
-            std::vector<ctrl::FdSegment> segs;
-            const int fr = ctrl::fd_fetch(fd_service(pid), rec.key, 5000, &segs);
-            if (fr != 0) {
-                MPCOMM_LOG_ERROR("MPComm[nvl]: VMM handles of pid %ld's buffer 0x%lx: %s\n", pid,
-                                 static_cast<unsigned long>(rec.addr), fr == 1 ? "withdrawn" : "server unreachable");
-                return kWcRemAccessErr;
-            }
-            // The owner's layout, back to back from offset 0 to alloc_size.
-            std::vector<int> fds;
-            std::vector<size_t> sizes;
-            uint64_t next = 0;
-            bool shaped = true;
-            for (const auto &g : segs) {
-                shaped &= g.offset == next;
-                next = g.offset + g.size;
-                fds.push_back(g.fd);
-                sizes.push_back(static_cast<size_t>(g.size));
-            }
-            shaped &= next == rec.alloc_size;
             void *p = nullptr;
-            const int e = shaped ? vmm::vmm_import_map(fds.data(), sizes.data(), fds.size(), dev, &p) : -1;
-            for (int f : fds) close(f);
+            std::vector<size_t> sizes;
+            int e = vmm::vmm_open(pid, rec.key, dev, 5000, &p, &sizes);
+            size_t span = 0;
+            for (size_t n : sizes) span += n;
+            if (e == 0 && span != rec.alloc_size) {
+                vmm::vmm_unmap(p, sizes);
+                e = -2;
+            }
             if (e != 0) {
-                MPCOMM_LOG_ERROR("MPComm[nvl]: mapping pid %ld's VMM buffer (%zu allocations) failed (%d)\n", pid,
-                                 segs.size(), e);
+                MPCOMM_LOG_ERROR("MPComm[nvl]: pid %ld's VMM buffer 0x%lx: %s (%d)\n", pid,
+                                 static_cast<unsigned long>(rec.addr),
+                                 e == 1 ? "withdrawn" : e == -1 ? "owner unreachable" : "cannot map", e);
                 return kWcRemAccessErr;
             }
             it = vmm_opened_.emplace(mk, reinterpret_cast<uintptr_t>(p)).first;

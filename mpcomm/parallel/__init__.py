@@ -68,36 +68,64 @@ def _all_gather_object(obj):
 
 
 class PeerBuffers:
-    """``nbytes`` of HBM per rank, addressable by every rank's kernels."""
+    """``nbytes`` of HBM per rank, addressable by every rank's kernels.
+
+    The buffers are shared with CUDA IPC; when the allocator hands out VMM
+    memory that CUDA IPC cannot export (``PYTORCH_CUDA_ALLOC_CONF=
+    expandable_segments:True``), through each rank's descriptor server
+    instead (``vmm_offer`` / ``vmm_open``: the allocations' POSIX handles,
+    mapped back to back by the peer)."""
 
     def __init__(self, nbytes: int, dtype=torch.uint8):
         self.nbytes = nbytes
         self.rank = dist.get_rank() if dist.is_initialized() else 0
         self.local = torch.zeros(nbytes // torch.empty((), dtype=dtype).element_size(), dtype=dtype,
                                  device="cuda")
-        err, handle, off = _native.ipc_export(self.local.data_ptr())
+        ptr = self.local.data_ptr()
+        self._vmm_key = 0
+        err, handle, off = _native.ipc_export(ptr)
         if err:
-            raise RuntimeError(f"ipc_export failed ({err})")
-        infos = _all_gather_object((handle, off))
-        self._imported = []
+            verr, key, base, _ = _native.vmm_offer(ptr, self.local.numel() * self.local.element_size())
+            if verr:
+                raise RuntimeError(f"neither CUDA IPC ({err}) nor a VMM offer ({verr}) can share this buffer")
+            self._vmm_key = key
+            info = ("vmm", os.getpid(), key, ptr - base)
+        else:
+            info = ("ipc", handle, off)
+        infos = _all_gather_object(info)
+        self._imported = []  # (kind, address, sizes)
         self.ptrs = []
-        for r, (h, o) in enumerate(infos):
+        dev = torch.cuda.current_device()
+        for r, inf in enumerate(infos):
             if r == self.rank:
-                self.ptrs.append(self.local.data_ptr())
+                self.ptrs.append(ptr)
                 continue
-            err, base = _native.ipc_import(h)
-            if err:
-                raise RuntimeError(f"ipc_import of rank {r} failed ({err})")
-            self._imported.append(base)
-            self.ptrs.append(base + o)
+            if inf[0] == "vmm":
+                err, va, sizes = _native.vmm_open(inf[1], inf[2], dev)
+                if err:
+                    raise RuntimeError(f"vmm_open of rank {r} failed ({err})")
+                self._imported.append(("vmm", va, sizes))
+                self.ptrs.append(va + inf[3])
+            else:
+                err, base = _native.ipc_import(inf[1])
+                if err:
+                    raise RuntimeError(f"ipc_import of rank {r} failed ({err})")
+                self._imported.append(("ipc", base, None))
+                self.ptrs.append(base + inf[2])
 
     def peer_view(self, r: int) -> torch.Tensor:
         return device_view(self.ptrs[r], self.nbytes)
 
     def close(self):
-        for b in self._imported:
-            _native.ipc_release(b)
+        for kind, b, sizes in self._imported:
+            if kind == "vmm":
+                _native.vmm_unmap(b, sizes)
+            else:
+                _native.ipc_release(b)
         self._imported = []
+        if self._vmm_key:
+            _native.vmm_withdraw(self._vmm_key)
+            self._vmm_key = 0
 
 
 class SharedHostPool:

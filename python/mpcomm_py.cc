@@ -8,6 +8,7 @@
 
 #include <unistd.h>
 
+#include <atomic>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -698,6 +699,38 @@ PYBIND11_MODULE(_mpcomm, m) {
         py::arg("ptr"), py::arg("length"),
         "(err, [(base, size), ...]): the VMM allocations behind [ptr, ptr+length) (err != 0 for memory that is "
         "not VMM-mapped, e.g. cudaMalloc).");
+    m.def(
+        "vmm_offer",
+        [](uintptr_t ptr, size_t len) {
+            static std::atomic<uint64_t> next{1ull << 40};  // apart from the fabric's registration keys
+            const uint64_t key = next++;
+            uintptr_t base = 0;
+            size_t span = 0;
+            const int e = vmm::vmm_offer(reinterpret_cast<void *>(ptr), len, key, &base, &span);
+            return py::make_tuple(e, e ? 0 : key, base, span);
+        },
+        py::arg("ptr"), py::arg("length"),
+        "(err, key, base, span): offers VMM memory [ptr, ptr+length) to peer processes of this host (what CUDA IPC "
+        "cannot export); a peer maps it with vmm_open(pid, key, device), where its address stands for `base`.");
+    m.def("vmm_withdraw", &vmm::vmm_withdraw, py::arg("key"));
+    m.def(
+        "vmm_open",
+        [](long pid, uint64_t key, int dev, int timeout_ms) {
+            void *va = nullptr;
+            std::vector<size_t> sizes;
+            int e;
+            {
+                py::gil_scoped_release r;
+                e = vmm::vmm_open(pid, key, dev, timeout_ms, &va, &sizes);
+            }
+            return py::make_tuple(e, reinterpret_cast<uintptr_t>(va), sizes);
+        },
+        py::arg("pid"), py::arg("key"), py::arg("device"), py::arg("timeout_ms") = 5000,
+        "(err, va, sizes): maps what process `pid` offered under `key` for `device`; release with vmm_unmap.");
+    m.def(
+        "vmm_unmap",
+        [](uintptr_t va, const std::vector<size_t> &sizes) { return vmm::vmm_unmap(reinterpret_cast<void *>(va), sizes); },
+        py::arg("va"), py::arg("sizes"));
     m.def(
         "multicast_group",
         [](const std::string &name, size_t bytes, int members, bool create, int timeout_ms) {

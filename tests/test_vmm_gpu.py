@@ -107,3 +107,52 @@ def test_put_get_vmm_buffer_of_another_process(tmp_path, kind):
         if t.poll() is None:
             t.kill()
             t.wait()
+
+
+PEERS = r"""
+import os, sys, torch, torch.distributed as dist
+from mpcomm import _native, parallel
+rank, world = int(sys.argv[1]), 2
+dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{sys.argv[2]}", rank=rank, world_size=world)
+torch.cuda.set_device(0)
+torch.empty(5 << 20, dtype=torch.uint8, device="cuda")  # start mid-page
+pb = parallel.PeerBuffers(48 << 20)
+err, segs = _native.vmm_segments(pb.local.data_ptr(), pb.nbytes)
+assert err == 0 and len(segs) >= 2, (err, segs)
+pb.local.copy_(torch.arange(pb.nbytes, device="cuda", dtype=torch.int64).to(torch.uint8) ^ (rank + 1))
+torch.cuda.synchronize()
+dist.barrier()
+peer = 1 - rank
+# The library's own copy kernel moves bytes to and from the peer's mapping.
+got = torch.empty(pb.nbytes, dtype=torch.uint8, device="cuda")
+assert _native.copy_spans([pb.ptrs[peer]], [got.data_ptr()], [pb.nbytes]) == 0
+want = torch.arange(pb.nbytes, device="cuda", dtype=torch.int64).to(torch.uint8) ^ (peer + 1)
+torch.cuda.synchronize()
+assert torch.equal(got, want), "peer view differs"
+mark = torch.full((4096,), 0xA0 + rank, dtype=torch.uint8, device="cuda")
+assert _native.copy_spans([mark.data_ptr()], [pb.ptrs[peer]], [4096]) == 0  # a store into the peer's buffer
+torch.cuda.synchronize()
+dist.barrier()
+assert bool((pb.local[:4096] == 0xA0 + peer).all()), "the peer's store did not land"
+dist.barrier()
+pb.close()
+dist.destroy_process_group()
+print(f"rank {rank} peer buffers ok")
+"""
+
+
+def test_peer_buffers_over_expandable_segments():
+    """PeerBuffers when the allocator hands out expandable-segment memory
+    (CUDA IPC cannot export it): two ranks on one GPU share their buffers
+    through the descriptor servers, read each other's bytes and store into
+    each other's buffers."""
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, PYTORCH_CUDA_ALLOC_CONF="expandable_segments:True", MPCOMM_LOG_LEVEL="1")
+    ps = [subprocess.Popen(["timeout", "-k", "10", "180", sys.executable, "-c", PEERS, str(r), str(port)], cwd=ROOT,
+                           env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True) for r in range(2)]
+    outs = [p.communicate(timeout=240)[0] for p in ps]
+    for r, (p, out) in enumerate(zip(ps, outs)):
+        assert p.returncode == 0 and f"rank {r} peer buffers ok" in out, out[-3000:]
