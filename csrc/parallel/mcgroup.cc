@@ -89,6 +89,12 @@ bool recv_handle(int fd, int *handle_fd, uint64_t *size, Clock::time_point deadl
 
 }  // namespace
 
+const McOps &mc_driver_ops() {
+    static const McOps ops{multicast_granularity, multicast_create, multicast_import, multicast_add_device,
+                           multicast_bind_local, multicast_map, multicast_teardown};
+    return ops;
+}
+
 uint64_t mc_group_token(const std::string &name) {
     uint64_t h = 1469598103934665603ull;  // FNV-1a
     for (unsigned char ch : name) {
@@ -99,19 +105,28 @@ uint64_t mc_group_token(const std::string &name) {
 }
 
 int mc_group_create(const std::string &name, size_t bytes, int members, int timeout_ms, McGroup *out) {
+    return mc_group_create_with(mc_driver_ops(), gpu::current_device(), name, bytes, members, timeout_ms, out);
+}
+
+int mc_group_join(const std::string &name, size_t bytes, int members, int timeout_ms, McGroup *out) {
+    return mc_group_join_with(mc_driver_ops(), gpu::current_device(), name, bytes, members, timeout_ms, out);
+}
+
+int mc_group_create_with(const McOps &ops, int dev, const std::string &name, size_t bytes, int members,
+                         int timeout_ms, McGroup *out) {
     if (members < 2 || bytes == 0) return -1;
     const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
     McGroup g;
-    g.dev = gpu::current_device();
+    g.dev = dev;
     g.members = members;
     g.token = mc_group_token(name);
     size_t gran = 0;
-    int e = multicast_granularity(bytes, members, &gran);
+    int e = ops.granularity(bytes, members, &gran);
     if (e) return e;
     if (gran == 0) gran = 2u << 20;
     g.size = (bytes + gran - 1) / gran * gran;
     int hfd = -1;
-    e = multicast_create(g.size, members, &g.mc, &hfd);
+    e = ops.create(g.size, members, &g.mc, &hfd);
     if (e) return e;
     int lfd = socket(AF_UNIX, SOCK_STREAM | SOCK_CLOEXEC, 0);
     sockaddr_un a;
@@ -125,12 +140,12 @@ int mc_group_create(const std::string &name, size_t bytes, int members, int time
         }
         if (lfd >= 0) close(lfd);
         if (hfd >= 0) close(hfd);
-        multicast_teardown(g.mc, g.mem, g.uc, g.mcva, g.size, g.dev);
+        ops.teardown(g.mc, g.mem, g.uc, g.mcva, g.size, g.dev);
         return rc;
     };
     if (lfd < 0 || bind(lfd, reinterpret_cast<sockaddr *>(&a), alen) != 0 || listen(lfd, members) != 0)
         return fail(-1, "cannot listen (is another group of this name open?)");
-    if ((e = multicast_add_device(g.mc, g.dev))) return fail(e, "cuMulticastAddDevice");
+    if ((e = ops.add_device(g.mc, g.dev))) return fail(e, "cuMulticastAddDevice");
     // Hand the object to every other member; each adds its GPU.
     while (static_cast<int>(peers.size()) < members - 1) {
         if (!wait_fd(lfd, POLLIN, deadline)) return fail(-1, "timed out waiting for members");
@@ -149,12 +164,12 @@ int mc_group_create(const std::string &name, size_t bytes, int members, int time
     // Every device is added: bind, then map.
     for (int p : peers)
         if (!send_byte(p, 'B')) return fail(-1, "bind signal");
-    if ((e = multicast_bind_local(g.mc, g.size, g.dev, &g.mem, &g.uc))) return fail(e, "bind");
+    if ((e = ops.bind(g.mc, g.size, g.dev, &g.mem, &g.uc))) return fail(e, "bind");
     for (int p : peers)
         if (!recv_byte(p, &c, deadline) || c != 'b') return fail(-1, "a member could not bind");
     for (int p : peers)
         if (!send_byte(p, 'M')) return fail(-1, "map signal");
-    if ((e = multicast_map(g.mc, g.size, g.dev, &g.mcva))) return fail(e, "map");
+    if ((e = ops.map(g.mc, g.size, g.dev, &g.mcva))) return fail(e, "map");
     for (int p : peers)
         if (!recv_byte(p, &c, deadline) || c != 'm') return fail(-1, "a member could not map");
     for (int p : peers) close(p);
@@ -162,11 +177,12 @@ int mc_group_create(const std::string &name, size_t bytes, int members, int time
     return 0;
 }
 
-int mc_group_join(const std::string &name, size_t bytes, int members, int timeout_ms, McGroup *out) {
+int mc_group_join_with(const McOps &ops, int dev, const std::string &name, size_t bytes, int members,
+                       int timeout_ms, McGroup *out) {
     if (members < 2 || bytes == 0) return -1;
     const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
     McGroup g;
-    g.dev = gpu::current_device();
+    g.dev = dev;
     g.members = members;
     g.token = mc_group_token(name);
     sockaddr_un a;
@@ -188,23 +204,23 @@ int mc_group_join(const std::string &name, size_t bytes, int members, int timeou
         MPCOMM_LOG_ERROR("MPComm: multicast group '%s' (member): %s\n", name.c_str(), what);
         send_byte(fd, 'E');
         close(fd);
-        multicast_teardown(g.mc, g.mem, g.uc, g.mcva, g.size, g.dev);
+        ops.teardown(g.mc, g.mem, g.uc, g.mcva, g.size, g.dev);
         return rc;
     };
     int hfd = -1;
     uint64_t size = 0;
     if (!recv_handle(fd, &hfd, &size, deadline)) return fail(-1, "no handle from the creator");
     g.size = size;
-    int e = multicast_import(hfd, &g.mc);
+    int e = ops.import(hfd, &g.mc);
     close(hfd);
     if (e) return fail(e, "import");
     if (size < bytes) return fail(-1, "group smaller than requested");
-    if ((e = multicast_add_device(g.mc, g.dev))) return fail(e, "cuMulticastAddDevice");
+    if ((e = ops.add_device(g.mc, g.dev))) return fail(e, "cuMulticastAddDevice");
     char c = 0;
     if (!send_byte(fd, 'A') || !recv_byte(fd, &c, deadline) || c != 'B') return fail(-1, "no bind signal");
-    if ((e = multicast_bind_local(g.mc, g.size, g.dev, &g.mem, &g.uc))) return fail(e, "bind");
+    if ((e = ops.bind(g.mc, g.size, g.dev, &g.mem, &g.uc))) return fail(e, "bind");
     if (!send_byte(fd, 'b') || !recv_byte(fd, &c, deadline) || c != 'M') return fail(-1, "no map signal");
-    if ((e = multicast_map(g.mc, g.size, g.dev, &g.mcva))) return fail(e, "map");
+    if ((e = ops.map(g.mc, g.size, g.dev, &g.mcva))) return fail(e, "map");
     send_byte(fd, 'm');
     close(fd);
     *out = g;

@@ -35,6 +35,24 @@ int mc_group_join(const std::string &name, size_t bytes, int members, int timeou
 // Unmaps, unbinds and releases this member's part of the group.
 int mc_group_release(McGroup *g);
 
+// The driver steps a member takes, replaceable so that the hand-off and
+// lock-step protocol runs (and fails) in tests without a GPU. Each returns
+// 0 or an error code, like the vmm functions they default to.
+struct McOps {
+    int (*granularity)(size_t size, int ndev, size_t *gran);
+    int (*create)(size_t size, int ndev, uint64_t *mc, int *fd);
+    int (*import)(int fd, uint64_t *mc);
+    int (*add_device)(uint64_t mc, int dev);
+    int (*bind)(uint64_t mc, size_t size, int dev, uint64_t *mem, void **uc);
+    int (*map)(uint64_t mc, size_t size, int dev, void **mcva);
+    int (*teardown)(uint64_t mc, uint64_t mem, void *uc, void *mcva, size_t size, int dev);
+};
+const McOps &mc_driver_ops();
+int mc_group_create_with(const McOps &ops, int dev, const std::string &name, size_t bytes, int members,
+                         int timeout_ms, McGroup *out);
+int mc_group_join_with(const McOps &ops, int dev, const std::string &name, size_t bytes, int members,
+                       int timeout_ms, McGroup *out);
+
 }  // namespace vmm
 }  // namespace mpcomm
 

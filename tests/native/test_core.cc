@@ -1,10 +1,13 @@
 // Native unit tests of the engine's building blocks (no GPU, no network).
 // Run by tests/test_native.py; exits non-zero on the first failure.
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
 #include <set>
+#include <atomic>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -183,6 +186,102 @@ static void test_fd_share() {
     CHECK(vmm::mc_group_token("grp") != vmm::mc_group_token("grp2") && vmm::mc_group_token("") != 0);
 }
 
+// NVLS group formation without a GPU: fake driver steps record what each
+// member did, so the hand-off (the creator's object arrives over the socket),
+// the lock step (every device added before any bind, every bind before any
+// map) and failure propagation (a member that fails, or never comes, ends
+// every call with an error within the timeout) are checked on the host.
+namespace fake_mc {
+std::mutex mu;
+std::vector<std::string> log;
+int members = 0, fail_dev = -1;
+std::string fail_step;
+std::atomic<int> teardowns{0};
+int step(const char *what, int dev) {
+    std::lock_guard<std::mutex> g(mu);
+    log.push_back(std::string(what) + std::to_string(dev));
+    return (fail_dev == dev && fail_step == what) ? 999 : 0;
+}
+int count(const char *what) {
+    int n = 0;
+    for (auto &e : log) n += e.rfind(what, 0) == 0;
+    return n;
+}
+int gran(size_t, int, size_t *g) { *g = 4096; return 0; }
+int create(size_t, int, uint64_t *mc, int *fd) {
+    *fd = memfd_create("mcg", 0);
+    if (*fd < 0 || pwrite(*fd, "MCOBJ", 5, 0) != 5) return 1;
+    *mc = 0xC0FFEE;
+    return 0;
+}
+int import(int fd, uint64_t *mc) {
+    char b[5] = {0};
+    if (pread(fd, b, 5, 0) != 5 || std::memcmp(b, "MCOBJ", 5) != 0) return 2;  // not the creator's object
+    *mc = 0xC0FFEE;
+    return 0;
+}
+int add(uint64_t, int dev) { return step("add", dev); }
+int bind(uint64_t, size_t, int dev, uint64_t *mem, void **uc) {
+    std::lock_guard<std::mutex> g(mu);  // the lock step: all adds happen before any bind
+    if (count("add") != members) log.push_back("EARLY-BIND");
+    log.push_back("bind" + std::to_string(dev));
+    *mem = 1;
+    *uc = reinterpret_cast<void *>(0x1000);
+    return (fail_dev == dev && fail_step == "bind") ? 999 : 0;
+}
+int map(uint64_t, size_t, int dev, void **va) {
+    std::lock_guard<std::mutex> g(mu);
+    if (count("bind") != members) log.push_back("EARLY-MAP");
+    log.push_back("map" + std::to_string(dev));
+    *va = reinterpret_cast<void *>(0x2000);
+    return 0;
+}
+int teardown(uint64_t, uint64_t, void *, void *, size_t, int) { ++teardowns; return 0; }
+const vmm::McOps ops{gran, create, import, add, bind, map, teardown};
+
+// Runs a group of `n` members (dev 0 creates); `absent` members never come.
+std::vector<int> run(const std::string &name, int n, int absent, int timeout_ms) {
+    log.clear();
+    teardowns = 0;
+    members = n;
+    std::vector<int> rc(n - absent, 123);
+    std::vector<std::thread> ts;
+    for (int d = 0; d < n - absent; ++d)
+        ts.emplace_back([&, d] {
+            vmm::McGroup g;
+            rc[d] = d == 0 ? vmm::mc_group_create_with(ops, d, name, 10000, n, timeout_ms, &g)
+                           : vmm::mc_group_join_with(ops, d, name, 10000, n, timeout_ms, &g);
+            if (rc[d] == 0) CHECK(g.size == 12288 && g.mc == 0xC0FFEE && g.uc && g.mcva && g.members == n);
+        });
+    for (auto &t : ts) t.join();
+    return rc;
+}
+}  // namespace fake_mc
+
+static void test_mc_group_protocol() {
+    const std::string base = "mpcomm-test-mcg." + std::to_string(getpid());
+    auto rc = fake_mc::run(base + ".ok", 4, 0, 5000);
+    for (int r : rc) CHECK(r == 0);
+    CHECK(fake_mc::count("add") == 4 && fake_mc::count("bind") == 4 && fake_mc::count("map") == 4);
+    CHECK(fake_mc::count("EARLY") == 0 && fake_mc::teardowns == 0);
+    // A member whose bind fails: every call fails, each member tears down.
+    fake_mc::fail_dev = 2;
+    fake_mc::fail_step = "bind";
+    auto t0 = std::chrono::steady_clock::now();
+    rc = fake_mc::run(base + ".bindfail", 4, 0, 3000);
+    for (int r : rc) CHECK(r != 0);
+    CHECK(fake_mc::teardowns == 4 && fake_mc::count("map") == 0);
+    CHECK(std::chrono::steady_clock::now() - t0 < std::chrono::seconds(3));
+    fake_mc::fail_dev = -1;
+    // A member that never comes: the creator gives up at its timeout and
+    // releases the members that did come.
+    t0 = std::chrono::steady_clock::now();
+    rc = fake_mc::run(base + ".absent", 3, 1, 400);
+    for (int r : rc) CHECK(r == -1);
+    CHECK(fake_mc::count("bind") == 0 && fake_mc::teardowns == 2);
+    CHECK(std::chrono::steady_clock::now() - t0 < std::chrono::seconds(3));
+}
+
 int main() {
     test_wrid();
     test_handle_pool();
@@ -192,6 +291,7 @@ int main() {
     test_topology_parsers();
     test_wire_layout();
     test_fd_share();
+    test_mc_group_protocol();
     std::printf("native core tests passed (%d checks)\n", g_checks);
     return 0;
 }
