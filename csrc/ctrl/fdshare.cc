@@ -6,7 +6,6 @@
 #include <unistd.h>
 
 #include <algorithm>
-#include <atomic>
 #include <cctype>
 #include <cerrno>
 #include <cstdio>
@@ -88,9 +87,12 @@ bool send_part(int c, uint8_t st, const std::vector<FdSegment> &segs, size_t fir
 
 class Server {
  public:
+    // Never destroyed: offers may be withdrawn by other objects' destructors
+    // at exit, after function-local statics are gone; the thread ends with
+    // the process.
     static Server &get() {
-        static Server s;
-        return s;
+        static Server *s = new Server;
+        return *s;
     }
 
     int offer(const std::string &name, uint64_t key, FdProvider p) {
@@ -105,12 +107,6 @@ class Server {
         offers_.erase(key);
     }
 
-    ~Server() {
-        stop_ = true;
-        if (th_.joinable()) th_.join();
-        if (lfd_ >= 0) close(lfd_);
-    }
-
  private:
     int start(const std::string &name) {
         int s = socket(AF_UNIX, SOCK_SEQPACKET | SOCK_CLOEXEC, 0);
@@ -122,13 +118,16 @@ class Server {
             return -1;
         }
         lfd_ = s;
-        th_ = std::thread([this] { run(); });
+        std::thread([this] { run(); }).detach();
         return 0;
     }
 
     void run() {
-        while (!stop_.load()) {
-            if (!wait_in(lfd_, 100)) continue;
+        for (;;) {
+            if (!wait_in(lfd_, -1)) {
+                std::this_thread::sleep_for(std::chrono::milliseconds(100));
+                continue;
+            }
             const int c = accept4(lfd_, nullptr, nullptr, SOCK_CLOEXEC);
             if (c < 0) continue;
             serve(c);
@@ -169,8 +168,6 @@ class Server {
     std::mutex mu_;
     std::map<uint64_t, FdProvider> offers_;
     int lfd_ = -1;
-    std::thread th_;
-    std::atomic<bool> stop_{false};
 };
 
 }  // namespace
