@@ -190,6 +190,10 @@ int memset_device_async(void *p, int v, size_t bytes, void *stream) {
     return cudaMemsetAsync(p, v, bytes, static_cast<cudaStream_t>(stream));
 }
 
+int copy_engine_async(void *dst, const void *src, size_t bytes, void *stream) {
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+}
+
 int copy_d2h_sync(void *dst, const void *src, size_t bytes) {
     cudaStream_t s = helper_stream();
     if (!s) return cudaMemcpy(dst, src, bytes, cudaMemcpyDeviceToHost);

@@ -50,6 +50,9 @@ void device_free(void *p);
 int memset_device(void *p, int v, size_t bytes);
 int memset_device_async(void *p, int v, size_t bytes, void *stream);
 int copy_d2h_sync(void *dst, const void *src, size_t bytes);
+// Copy-engine copy (cudaMemcpyDefault: any UVA addresses, peers included) on
+// `stream`; benches use it as the comparator of the data-mover kernels.
+int copy_engine_async(void *dst, const void *src, size_t bytes, void *stream);
 
 // CUDA IPC (legacy handles; device memory from cudaMalloc).
 constexpr size_t kIpcHandleBytes = 64;

@@ -634,6 +634,14 @@ PYBIND11_MODULE(_mpcomm, m) {
         py::arg("bytes"), py::arg("threads") = 0, py::arg("node") = -1, py::arg("reps") = 3,
         "Host DRAM write (memset) and read bandwidth of `threads` CPU threads over a `bytes` buffer, GB/s; "
         "no device involved. Empty dict if the buffer cannot be allocated.");
+    m.def(
+        "copy_engine_async",
+        [](uintptr_t dst, uintptr_t src, size_t bytes, uintptr_t stream) {
+            return gpu::copy_engine_async(reinterpret_cast<void *>(dst), reinterpret_cast<const void *>(src), bytes,
+                                          reinterpret_cast<void *>(stream));
+        },
+        py::arg("dst"), py::arg("src"), py::arg("bytes"), py::arg("stream") = 0,
+        "cudaMemcpyAsync(cudaMemcpyDefault) on `stream` (the copy engine; a comparator for the benches).");
     m.def("enable_peer_access", &gpu::enable_peer_access, py::arg("device"), py::arg("peer"),
           "Lets kernels on `device` access memory of `peer` (0 or a CUDA error).");
     m.def("multicast_supported", &vmm::multicast_supported, py::arg("device"));
