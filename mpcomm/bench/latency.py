@@ -11,7 +11,10 @@ MPComm in the same process (connect-to-self over the TCP control plane).
 
 --device cuda places the source in HBM and the target in pinned host
 memory (the GPU fabric's HBM <-> DRAM-pool path); the default uses host
-memory on both sides. The reference publishes no latency numbers.
+memory on both sides. On the GPU fabric the line also carries
+"kernel_floor": the same copy kernel launched bare and timed to its
+host-visible done word, i.e. what is left without the engine. The
+reference publishes no latency numbers.
 """
 from __future__ import annotations
 
@@ -77,10 +80,24 @@ def main(argv=None):
                 q = lambda f: round(lat[min(len(lat) - 1, int(f * len(lat)))], 1)
                 rows.append({"op": op, "bytes": size, "gap_ms": gap_ms, "p50_us": q(0.5), "p90_us": q(0.9),
                              "p99_us": q(0.99)})
+    floor = []
+    if a.device == "cuda" and a.fabric == "nvl":
+        # What the engine adds: the same copy kernel launched bare, timed to
+        # its host-visible done word (no queue, worker, handle or Python).
+        from mpcomm import _native
+        for size in sizes:
+            lat = sorted(_native.copy_roundtrip_us(src, dst, size, a.iters + 10)[10:])
+            if lat:
+                q = lambda f: round(lat[min(len(lat) - 1, int(f * len(lat)))], 1)
+                floor.append({"op": "put (bare kernel round trip)", "bytes": size, "p50_us": q(0.5),
+                              "p90_us": q(0.9), "p99_us": q(0.99)})
     ini.shutdown()
     tgt.shutdown()
-    print(json.dumps({"metric": "small-transfer latency (submit -> wait_transfer returns)", "fabric": a.fabric,
-                      "device": a.device, "iters": a.iters, "rows": rows}), flush=True)
+    out = {"metric": "small-transfer latency (submit -> wait_transfer returns)", "fabric": a.fabric,
+           "device": a.device, "iters": a.iters, "rows": rows}
+    if floor:
+        out["kernel_floor"] = floor
+    print(json.dumps(out), flush=True)
 
 
 if __name__ == "__main__":

@@ -9,6 +9,7 @@
 #include <unistd.h>
 
 #include <atomic>
+#include <chrono>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -562,6 +563,54 @@ PYBIND11_MODULE(_mpcomm, m) {
           },
           py::arg("flag"), py::arg("value"), py::arg("budget_ns"), py::arg("stream") = 0, py::arg("status") = 0);
     m.def("kernel_launch_count", [] { return kern::launch_count(); });
+    m.def(
+        "copy_roundtrip_us",
+        [](uintptr_t src, uintptr_t dst, size_t bytes, int iters, int ctas) {
+            // The floor under one engine WR: a copy_batch launch that stores
+            // its done word into pinned host memory, timed from the launch
+            // call until this thread sees the word (the engine's path minus
+            // the engine). Spins are bounded (1 s per launch).
+            py::list out;
+            auto *word = static_cast<uint64_t *>(gpu::host_alloc_mapped(64));
+            auto *ctr = static_cast<uint32_t *>(gpu::device_alloc(64));
+            void *stream = gpu::stream_create(gpu::current_device());
+            if (!word || !ctr || !stream || gpu::memset_device(ctr, 0, 64) != 0) {
+                if (word) gpu::host_free(word);
+                if (ctr) gpu::device_free(ctr);
+                if (stream) gpu::stream_destroy(stream);
+                return out;
+            }
+            {
+                py::gil_scoped_release r;
+                kern::CopyDesc d{reinterpret_cast<const void *>(src), reinterpret_cast<void *>(dst), bytes};
+                using C = std::chrono::steady_clock;
+                std::vector<double> us;
+                for (int i = 1; i <= iters; ++i) {
+                    const auto t0 = C::now();
+                    if (kern::copy_batch(&d, 1, ctas, stream, nullptr, nullptr, kern::kModeAuto, nullptr, 0, word,
+                                         static_cast<uint64_t>(i), ctr) != 0)
+                        break;
+                    bool seen = false;
+                    while (C::now() - t0 < std::chrono::seconds(1))
+                        if (__atomic_load_n(word, __ATOMIC_ACQUIRE) >= static_cast<uint64_t>(i)) {
+                            seen = true;
+                            break;
+                        }
+                    if (!seen) break;
+                    us.push_back(std::chrono::duration<double, std::micro>(C::now() - t0).count());
+                }
+                gpu::stream_sync(stream);
+                py::gil_scoped_acquire a;
+                for (double v : us) out.append(v);
+            }
+            gpu::stream_destroy(stream);
+            gpu::device_free(ctr);
+            gpu::host_free(word);
+            return out;
+        },
+        py::arg("src"), py::arg("dst"), py::arg("bytes"), py::arg("iters") = 200, py::arg("ctas") = 4,
+        "Per-launch round trips (us) of one copy_batch launch to its host-visible done word: the floor under "
+        "an engine transfer of `bytes`.");
     m.def("kernel_trace", [] {
         std::vector<kern::TraceRecord> raw;
         int e;
