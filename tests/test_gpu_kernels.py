@@ -448,3 +448,14 @@ def test_qos_remote_pause_around_gather_windows(monkeypatch):
     finally:
         b.shutdown()
         a.shutdown()
+
+
+def test_copy_roundtrip_floor_copies_and_times():
+    """copy_roundtrip_us (the latency bench's floor): every launch copies the
+    bytes and is timed to its host-visible done word."""
+    n = 64 << 10
+    src = torch.randint(0, 256, (n,), dtype=torch.uint8, device="cuda")
+    dst = torch.zeros(n, dtype=torch.uint8).pin_memory()
+    us = mpcomm._native.copy_roundtrip_us(src.data_ptr(), dst.data_ptr(), n, 20)
+    assert len(us) == 20 and all(0 < u < 1e6 for u in us), us
+    assert torch.equal(dst, src.cpu())
