@@ -22,7 +22,7 @@
 
 using namespace mpcomm;
 
-static int g_checks = 0;
+static std::atomic<int> g_checks{0};  // CHECKs also run on member threads
 #define CHECK(cond)                                                                    \
     do {                                                                               \
         ++g_checks;                                                                    \
@@ -292,6 +292,6 @@ int main() {
     test_wire_layout();
     test_fd_share();
     test_mc_group_protocol();
-    std::printf("native core tests passed (%d checks)\n", g_checks);
+    std::printf("native core tests passed (%d checks)\n", g_checks.load());
     return 0;
 }

@@ -359,15 +359,17 @@ def test_kernel_trace_off_by_default():
     assert mpcomm.MPComm.get_kernel_launch_count() >= 0
 
 
-@pytest.mark.parametrize("name", ["test_core", "test_engine", "test_engine_san", "test_engine_tsan"])
+@pytest.mark.parametrize("name", ["test_core", "test_engine", "test_engine_san", "test_engine_tsan", "test_core_san",
+                                  "test_core_tsan"])
 def test_native_binaries(name):
-    """Core unit tests, the multi-threaded engine stress, and the same stress
-    built with AddressSanitizer + UBSan (memory errors in the engine's
-    lifetime and completion protocol abort with a report) and with
-    ThreadSanitizer (any data race between the submitting threads, the
-    worker, the publish/query thread and the throttle toggler fails it)."""
+    """Core unit tests, the multi-threaded engine stress, and both built
+    with AddressSanitizer + UBSan (memory errors in the engine's lifetime and
+    completion protocol abort with a report) and with ThreadSanitizer (any
+    data race between the submitting threads, the worker, the publish/query
+    thread and the throttle toggler, or in the descriptor server and the
+    multicast-group protocol threads, fails it)."""
     exe = os.path.join(ROOT, "tests", "native", "bin", name)
-    if name == "test_engine_tsan" and not os.path.exists(exe):
+    if name.endswith("_tsan") and not os.path.exists(exe):
         pytest.skip("toolchain has no ThreadSanitizer runtime")
     assert os.path.exists(exe), "native tests not built (run __graft_entry__.build())"
     env = dict(os.environ, ASAN_OPTIONS="detect_leaks=0:abort_on_error=1", MPCOMM_LOG_LEVEL="1",
