@@ -2,7 +2,8 @@
 
 Verifies, without any RDMA hardware or GPU: the package imports, the native
 module and libmpcomm.so load and resolve their shared-library dependencies,
-the exported API is present, an MPComm object initialises on the loopback
+the exported API is present (Python names and the library's C entry
+point), an MPComm object initialises on the loopback
 fabric, and the C++ headers are where get_include_dir() says.
 
     python -m mpcomm.check_install      # exit code 0 = OK
@@ -30,6 +31,13 @@ def main() -> int:
         check(hasattr(mpcomm, sym), f"export {sym}")
     lib = os.path.join(mpcomm.get_lib_dir(), "libmpcomm.so")
     check(os.path.exists(lib), f"shared library {lib}")
+    if os.path.exists(lib):
+        import ctypes
+        try:
+            so = ctypes.CDLL(lib)
+            check(hasattr(so, "mpcomm_crc32_blocks_noalloc"), "C entry point mpcomm_crc32_blocks_noalloc")
+        except OSError as e:
+            check(False, f"load {lib}: {e}")
     for path in (mpcomm.native_library_path(), lib):
         if os.path.exists(path):
             out = subprocess.run(["ldd", path], capture_output=True, text=True).stdout

@@ -488,3 +488,18 @@ def test_multicast_group_bounded_without_peers():
     assert _native.multicast_group(name, 1 << 20, 1, True, 300)[0] == -7
     assert _native.multicast_group(name, 0, 2, False, 300)[0] == -7
     assert _native.multicast_group("", 1 << 20, 2, False, 300)[0] == -7
+
+
+def test_nvls_group_from_name_fails_cleanly_without_gpus():
+    """NvlsGroup.from_name raises (never hangs) where no group can form: on a
+    host without multicast-capable GPUs the creator fails at once, a joiner
+    after its timeout."""
+    import time
+
+    from mpcomm import parallel
+    name = f"mpcomm-cpu-from-name-{os.getpid()}"
+    t0 = time.monotonic()
+    for create in (True, False):
+        with pytest.raises(RuntimeError):
+            parallel.NvlsGroup.from_name(name, 1 << 20, 2, create=create, timeout_ms=300)
+    assert time.monotonic() - t0 < 10
