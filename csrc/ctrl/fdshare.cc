@@ -8,10 +8,11 @@
 #include <algorithm>
 #include <cctype>
 #include <cerrno>
-#include <cstdio>
 #include <chrono>
+#include <cstdio>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <thread>
 
@@ -24,20 +25,23 @@ namespace {
 enum : uint8_t { kOk = 0, kNoKey = 1, kDenied = 2 };
 
 // Reply: messages of this header, `count` wire segments and `count`
-// descriptors (SCM_RIGHTS), until `total` segments have been sent. A refusal
-// is one header with count = total = 0.
+// descriptors (SCM_RIGHTS), until `total` segments have been sent. A
+// refusal, or an export that fails part-way, is a header with that status
+// and count 0.
 struct ReplyHeader {
     uint8_t status;
     uint8_t pad[3];
     uint32_t count;
     uint32_t total;
     uint32_t pad2;
+    uint64_t total_bytes;
 };
 struct WireSegment {
     uint64_t offset;
     uint64_t size;
 };
 constexpr size_t kPerMessage = 64;
+constexpr size_t kMsgBytes = sizeof(ReplyHeader) + kPerMessage * sizeof(WireSegment);
 
 socklen_t abstract_addr(const std::string &name, sockaddr_un *a) {
     std::memset(a, 0, sizeof(*a));
@@ -56,15 +60,13 @@ bool wait_in(int fd, int ms) {
     }
 }
 
-bool send_part(int c, uint8_t st, const std::vector<FdSegment> &segs, size_t first, size_t n) {
-    char buf[sizeof(ReplyHeader) + kPerMessage * sizeof(WireSegment)];
-    ReplyHeader h{};
-    h.status = st;
+bool send_part(int c, const ReplyHeader &hdr, const FdSegment *segs, size_t n) {
+    char buf[kMsgBytes];
+    ReplyHeader h = hdr;
     h.count = static_cast<uint32_t>(n);
-    h.total = static_cast<uint32_t>(segs.size());
     std::memcpy(buf, &h, sizeof(h));
     for (size_t i = 0; i < n; ++i) {
-        WireSegment w{segs[first + i].offset, segs[first + i].size};
+        WireSegment w{segs[i].offset, segs[i].size};
         std::memcpy(buf + sizeof(h) + i * sizeof(w), &w, sizeof(w));
     }
     iovec io{buf, sizeof(h) + n * sizeof(WireSegment)};
@@ -80,7 +82,7 @@ bool send_part(int c, uint8_t st, const std::vector<FdSegment> &segs, size_t fir
         c0->cmsg_level = SOL_SOCKET;
         c0->cmsg_type = SCM_RIGHTS;
         c0->cmsg_len = CMSG_LEN(n * sizeof(int));
-        for (size_t i = 0; i < n; ++i) std::memcpy(CMSG_DATA(c0) + i * sizeof(int), &segs[first + i].fd, sizeof(int));
+        for (size_t i = 0; i < n; ++i) std::memcpy(CMSG_DATA(c0) + i * sizeof(int), &segs[i].fd, sizeof(int));
     }
     return sendmsg(c, &m, MSG_NOSIGNAL) == static_cast<ssize_t>(io.iov_len);
 }
@@ -95,10 +97,10 @@ class Server {
         return *s;
     }
 
-    int offer(const std::string &name, uint64_t key, FdProvider p) {
+    int offer(const std::string &name, uint64_t key, FdOffer o) {
         std::lock_guard<std::mutex> g(mu_);
         if (lfd_ < 0 && start(name) != 0) return -1;
-        offers_[key] = std::move(p);
+        offers_[key] = std::make_shared<const FdOffer>(std::move(o));
         return 0;
     }
 
@@ -135,38 +137,53 @@ class Server {
         }
     }
 
-    // One request: u64 key in; the segments out, when the key is offered,
-    // its provider succeeds and the peer runs as our user.
+    // One request: u64 key in; the segments out, exported and sent one
+    // message at a time, when the key is offered and the peer runs as our
+    // user.
     void serve(int c) {
         uint64_t key = 0;
         if (!wait_in(c, 1000) || recv(c, &key, sizeof(key), 0) != static_cast<ssize_t>(sizeof(key))) return;
         ucred cred{};
         socklen_t cl = sizeof(cred);
-        uint8_t st = kOk;
-        if (getsockopt(c, SOL_SOCKET, SO_PEERCRED, &cred, &cl) != 0 || cred.uid != geteuid()) st = kDenied;
-        std::vector<FdSegment> segs;
-        if (st == kOk) {
-            FdProvider p;
-            {
-                std::lock_guard<std::mutex> g(mu_);
-                auto it = offers_.find(key);
-                if (it != offers_.end()) p = it->second;
-            }
-            if (!p || !p(&segs) || segs.empty() || segs.size() > kFdMaxSegments) st = kNoKey;
+        ReplyHeader h{};
+        h.status = kOk;
+        if (getsockopt(c, SOL_SOCKET, SO_PEERCRED, &cred, &cl) != 0 || cred.uid != geteuid()) h.status = kDenied;
+        std::shared_ptr<const FdOffer> o;
+        if (h.status == kOk) {
+            std::lock_guard<std::mutex> g(mu_);
+            auto it = offers_.find(key);
+            if (it != offers_.end()) o = it->second;
         }
-        if (st != kOk) {
-            for (auto &s : segs) close(s.fd);
-            segs.clear();
-            send_part(c, st, segs, 0, 0);
+        if (h.status == kOk && (!o || o->segments.empty() || o->segments.size() > kFdMaxSegments || !o->export_fd))
+            h.status = kNoKey;
+        if (h.status != kOk) {
+            send_part(c, h, nullptr, 0);
             return;
         }
-        for (size_t i = 0; i < segs.size(); i += kPerMessage)
-            if (!send_part(c, kOk, segs, i, std::min(kPerMessage, segs.size() - i))) break;
-        for (auto &s : segs) close(s.fd);
+        h.total = static_cast<uint32_t>(o->segments.size());
+        for (const auto &s : o->segments) h.total_bytes += s.size;
+        FdSegment part[kPerMessage];
+        for (size_t i = 0; i < o->segments.size(); i += kPerMessage) {
+            const size_t n = std::min(kPerMessage, o->segments.size() - i);
+            size_t ok = 0;
+            for (; ok < n; ++ok) {
+                part[ok] = o->segments[i + ok];
+                part[ok].fd = o->export_fd(i + ok);
+                if (part[ok].fd < 0) break;
+            }
+            const bool sent = ok == n && send_part(c, h, part, n);
+            for (size_t k = 0; k < ok; ++k) close(part[k].fd);
+            if (ok != n) {
+                ReplyHeader e = h;
+                e.status = kNoKey;
+                send_part(c, e, nullptr, 0);
+            }
+            if (!sent) return;
+        }
     }
 
     std::mutex mu_;
-    std::map<uint64_t, FdProvider> offers_;
+    std::map<uint64_t, std::shared_ptr<const FdOffer>> offers_;
     int lfd_ = -1;
 };
 
@@ -186,14 +203,15 @@ std::string fd_service_name(long pid) {
     return "mpcomm-fd." + boot + "." + std::to_string(pid);
 }
 
-int fd_offer(const std::string &name, uint64_t key, FdProvider provider) {
-    return Server::get().offer(name, key, std::move(provider));
+int fd_offer(const std::string &name, uint64_t key, FdOffer offer) {
+    return Server::get().offer(name, key, std::move(offer));
 }
 
 void fd_withdraw(uint64_t key) { Server::get().withdraw(key); }
 
-int fd_fetch(const std::string &name, uint64_t key, int timeout_ms, std::vector<FdSegment> *out) {
-    out->clear();
+int fd_fetch(const std::string &name, uint64_t key, int timeout_ms,
+             const std::function<bool(size_t count, uint64_t bytes)> &on_begin,
+             const std::function<bool(const FdSegment &)> &on_segment) {
     int s = socket(AF_UNIX, SOCK_SEQPACKET | SOCK_CLOEXEC, 0);
     if (s < 0) return -1;
     sockaddr_un a;
@@ -206,9 +224,11 @@ int fd_fetch(const std::string &name, uint64_t key, int timeout_ms, std::vector<
     int rc = -1;
     if (connect(s, reinterpret_cast<sockaddr *>(&a), n) == 0 &&
         send(s, &key, sizeof(key), MSG_NOSIGNAL) == static_cast<ssize_t>(sizeof(key))) {
-        size_t total = SIZE_MAX;
-        while (out->size() < total) {
-            char buf[sizeof(ReplyHeader) + kPerMessage * sizeof(WireSegment)];
+        size_t total = SIZE_MAX, got_segments = 0;
+        uint64_t total_bytes = 0;
+        bool stop = false;
+        while (!stop && got_segments < total) {
+            char buf[kMsgBytes];
             alignas(cmsghdr) char ctl[CMSG_SPACE(kPerMessage * sizeof(int))];
             iovec io{buf, sizeof(buf)};
             msghdr m{};
@@ -221,41 +241,46 @@ int fd_fetch(const std::string &name, uint64_t key, int timeout_ms, std::vector<
             if (got < static_cast<ssize_t>(sizeof(ReplyHeader))) break;
             ReplyHeader h;
             std::memcpy(&h, buf, sizeof(h));
-            // Descriptors first, so every one that arrived is closed on error.
-            std::vector<int> fds;
+            // Every descriptor that arrived is closed, whatever happens next.
+            int fds[kPerMessage];
+            size_t nfd = 0;
             for (cmsghdr *c = CMSG_FIRSTHDR(&m); c; c = CMSG_NXTHDR(&m, c)) {
                 if (c->cmsg_level != SOL_SOCKET || c->cmsg_type != SCM_RIGHTS) continue;
                 const size_t k = (c->cmsg_len - CMSG_LEN(0)) / sizeof(int);
                 for (size_t i = 0; i < k; ++i) {
                     int f;
                     std::memcpy(&f, CMSG_DATA(c) + i * sizeof(int), sizeof(int));
-                    fds.push_back(f);
+                    if (nfd < kPerMessage) fds[nfd++] = f;
+                    else close(f);
                 }
             }
-            const bool shaped = h.status == kOk && h.count == fds.size() && h.count <= kPerMessage &&
+            const bool shaped = h.status == kOk && h.count == nfd && h.count > 0 && h.count <= kPerMessage &&
                                 (m.msg_flags & MSG_CTRUNC) == 0 &&
                                 static_cast<size_t>(got) == sizeof(h) + h.count * sizeof(WireSegment) &&
                                 h.total > 0 && h.total <= kFdMaxSegments &&
-                                (total == SIZE_MAX || h.total == total) && out->size() + h.count <= h.total;
+                                (total == SIZE_MAX || (h.total == total && h.total_bytes == total_bytes)) &&
+                                got_segments + h.count <= h.total;
             if (!shaped) {
-                for (int f : fds) close(f);
-                if (h.status == kNoKey || h.status == kDenied) rc = h.status == kNoKey ? 1 : -1;
+                for (size_t i = 0; i < nfd; ++i) close(fds[i]);
+                if (h.status == kNoKey) rc = 1;
                 break;
             }
-            total = h.total;
+            if (total == SIZE_MAX) {
+                total = h.total;
+                total_bytes = h.total_bytes;
+                if (!on_begin(total, total_bytes)) stop = true;
+            }
             for (size_t i = 0; i < h.count; ++i) {
                 WireSegment w;
                 std::memcpy(&w, buf + sizeof(h) + i * sizeof(w), sizeof(w));
-                out->push_back(FdSegment{w.offset, w.size, fds[i]});
+                if (!stop && !on_segment(FdSegment{w.offset, w.size, fds[i]})) stop = true;
+                close(fds[i]);
             }
+            got_segments += h.count;
         }
-        if (total != SIZE_MAX && out->size() == total) rc = 0;
+        if (!stop && total != SIZE_MAX && got_segments == total) rc = 0;
     }
     close(s);
-    if (rc != 0) {
-        for (auto &f : *out) close(f.fd);
-        out->clear();
-    }
     return rc;
 }
 

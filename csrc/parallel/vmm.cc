@@ -225,53 +225,84 @@ int vmm_export_fd(uintptr_t base, int *fd) {
     return 0;
 }
 
-int vmm_import_map(const int *fds, const size_t *sizes, size_t n, int dev, void **va) {
-    auto imp = sym<CUresult (*)(CUmemGenericAllocationHandle *, void *, CUmemAllocationHandleType)>(
-        "cuMemImportFromShareableHandle");
-    auto reserve = sym<CUresult (*)(CUdeviceptr *, size_t, size_t, CUdeviceptr, unsigned long long)>(
-        "cuMemAddressReserve");
-    auto map = sym<CUresult (*)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long)>(
-        "cuMemMap");
-    auto access = sym<CUresult (*)(CUdeviceptr, size_t, const CUmemAccessDesc *, size_t)>("cuMemSetAccess");
-    auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
-    auto vfree = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree");
-    auto rel = sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease");
-    if (!imp || !reserve || !map || !access || !unmap || !vfree || !rel) return kNoDriver;
-    if (n == 0) return CUDA_ERROR_INVALID_VALUE;
-    size_t total = 0;
-    for (size_t i = 0; i < n; ++i) total += sizes[i];
-    CUdeviceptr p = 0;
-    CUresult r = reserve(&p, total, 0, 0, 0);
-    if (r != CUDA_SUCCESS) return r;
-    size_t mapped = 0;  // bytes mapped so far, from p
-    for (size_t i = 0; i < n && r == CUDA_SUCCESS; ++i) {
-        CUmemGenericAllocationHandle h = 0;
-        r = imp(&h, reinterpret_cast<void *>(static_cast<uintptr_t>(fds[i])), CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
-        if (r != CUDA_SUCCESS) break;
-        r = map(p + mapped, sizes[i], 0, h, 0);
-        rel(h);  // the mapping holds the allocation from here on
-        if (r == CUDA_SUCCESS) mapped += sizes[i];
+namespace {
+
+// Maps imported allocations back to back into one reserved range, one at a
+// time (so a caller never holds more than one handle), then grants `dev`
+// access to the whole range. abort() undoes whatever was mapped.
+class BackToBack {
+ public:
+    BackToBack()
+        : imp_(sym<CUresult (*)(CUmemGenericAllocationHandle *, void *, CUmemAllocationHandleType)>(
+              "cuMemImportFromShareableHandle")),
+          reserve_(sym<CUresult (*)(CUdeviceptr *, size_t, size_t, CUdeviceptr, unsigned long long)>(
+              "cuMemAddressReserve")),
+          map_(sym<CUresult (*)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long)>(
+              "cuMemMap")),
+          access_(sym<CUresult (*)(CUdeviceptr, size_t, const CUmemAccessDesc *, size_t)>("cuMemSetAccess")),
+          unmap_(sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap")),
+          vfree_(sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemAddressFree")),
+          rel_(sym<CUresult (*)(CUmemGenericAllocationHandle)>("cuMemRelease")) {}
+
+    int begin(size_t total) {
+        if (!imp_ || !reserve_ || !map_ || !access_ || !unmap_ || !vfree_ || !rel_) return kNoDriver;
+        if (total == 0) return CUDA_ERROR_INVALID_VALUE;
+        total_ = total;
+        return reserve_(&base_, total, 0, 0, 0);
     }
-    if (r == CUDA_SUCCESS) {
+    // The next allocation, at `offset` (must continue where the last ended).
+    int add(int fd, size_t offset, size_t size) {
+        if (!base_ || offset != mapped_ || size == 0 || offset + size > total_) return CUDA_ERROR_INVALID_VALUE;
+        CUmemGenericAllocationHandle h = 0;
+        CUresult r = imp_(&h, reinterpret_cast<void *>(static_cast<uintptr_t>(fd)), CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR);
+        if (r != CUDA_SUCCESS) return r;
+        r = map_(base_ + mapped_, size, 0, h, 0);
+        rel_(h);  // the mapping holds the allocation from here on
+        if (r != CUDA_SUCCESS) return r;
+        sizes_.push_back(size);
+        mapped_ += size;
+        return 0;
+    }
+    int finish(int dev, void **va, std::vector<size_t> *sizes) {
+        if (mapped_ != total_) return CUDA_ERROR_INVALID_VALUE;
         CUmemAccessDesc a;
         std::memset(&a, 0, sizeof(a));
         a.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
         a.location.id = dev;
         a.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
-        r = access(p, total, &a, 1);
+        const CUresult r = access_(base_, total_, &a, 1);
+        if (r != CUDA_SUCCESS) return r;
+        *va = reinterpret_cast<void *>(base_);
+        if (sizes) *sizes = sizes_;
+        base_ = 0;  // handed over
+        return 0;
     }
-    if (r != CUDA_SUCCESS) {
+    void abort() {
+        if (!base_) return;
         size_t off = 0;
-        for (size_t i = 0; i < n && off < mapped; ++i) {
-            unmap(p + off, sizes[i]);
-            off += sizes[i];
+        for (size_t n : sizes_) {
+            unmap_(base_ + off, n);
+            off += n;
         }
-        vfree(p, total);
-        return r;
+        vfree_(base_, total_);
+        base_ = 0;
     }
-    *va = reinterpret_cast<void *>(p);
-    return 0;
-}
+    ~BackToBack() { abort(); }
+
+ private:
+    CUresult (*imp_)(CUmemGenericAllocationHandle *, void *, CUmemAllocationHandleType);
+    CUresult (*reserve_)(CUdeviceptr *, size_t, size_t, CUdeviceptr, unsigned long long);
+    CUresult (*map_)(CUdeviceptr, size_t, size_t, CUmemGenericAllocationHandle, unsigned long long);
+    CUresult (*access_)(CUdeviceptr, size_t, const CUmemAccessDesc *, size_t);
+    CUresult (*unmap_)(CUdeviceptr, size_t);
+    CUresult (*vfree_)(CUdeviceptr, size_t);
+    CUresult (*rel_)(CUmemGenericAllocationHandle);
+    CUdeviceptr base_ = 0;
+    size_t total_ = 0, mapped_ = 0;
+    std::vector<size_t> sizes_;
+};
+
+}  // namespace
 
 int multicast_teardown(uint64_t mc, uint64_t mem, void *uc_va, void *mc_va, size_t size, int dev) {
     auto unmap = sym<CUresult (*)(CUdeviceptr, size_t)>("cuMemUnmap");
@@ -348,21 +379,20 @@ int vmm_offer(const void *ptr, size_t len, uint64_t key, uintptr_t *base, size_t
     if ((e = vmm_export_fd(segs[0].base, &fd))) return e;  // created without a POSIX handle type?
     close(fd);
     const uintptr_t b = segs[0].base;
-    auto provide = [segs, b](std::vector<ctrl::FdSegment> *out) {
-        for (const auto &g : segs) {
-            ctrl::FdSegment f;
-            f.offset = g.base - b;
-            f.size = g.size;
-            if (vmm_export_fd(g.base, &f.fd) != 0) {
-                for (auto &o : *out) close(o.fd);
-                out->clear();
-                return false;
-            }
-            out->push_back(f);
-        }
-        return true;
+    ctrl::FdOffer o;
+    std::vector<uintptr_t> bases;
+    for (const auto &g : segs) {
+        ctrl::FdSegment f;
+        f.offset = g.base - b;
+        f.size = g.size;
+        o.segments.push_back(f);
+        bases.push_back(g.base);
+    }
+    o.export_fd = [bases](size_t i) {
+        int f = -1;
+        return i < bases.size() && vmm_export_fd(bases[i], &f) == 0 ? f : -1;
     };
-    if (ctrl::fd_offer(ctrl::fd_service_name(getpid()), key, provide) != 0) return -1;
+    if (ctrl::fd_offer(ctrl::fd_service_name(getpid()), key, std::move(o)) != 0) return -1;
     *base = b;
     *span = segs.back().base + segs.back().size - b;
     return 0;
@@ -371,23 +401,17 @@ int vmm_offer(const void *ptr, size_t len, uint64_t key, uintptr_t *base, size_t
 void vmm_withdraw(uint64_t key) { ctrl::fd_withdraw(key); }
 
 int vmm_open(long pid, uint64_t key, int dev, int timeout_ms, void **va, std::vector<size_t> *sizes) {
-    std::vector<ctrl::FdSegment> segs;
-    const int fr = ctrl::fd_fetch(ctrl::fd_service_name(pid), key, timeout_ms, &segs);
-    if (fr != 0) return fr;
-    // The owner's layout, back to back from offset 0.
-    std::vector<int> fds;
-    sizes->clear();
-    uint64_t next = 0;
-    bool shaped = true;
-    for (const auto &g : segs) {
-        shaped &= g.offset == next && g.size > 0;
-        next = g.offset + g.size;
-        fds.push_back(g.fd);
-        sizes->push_back(static_cast<size_t>(g.size));
-    }
-    const int e = shaped ? vmm_import_map(fds.data(), sizes->data(), fds.size(), dev, va) : CUDA_ERROR_INVALID_VALUE;
-    for (int f : fds) close(f);
-    return e;
+    BackToBack m;
+    int e = 0;
+    const int fr = ctrl::fd_fetch(
+        ctrl::fd_service_name(pid), key, timeout_ms,
+        [&](size_t, uint64_t bytes) { return (e = m.begin(static_cast<size_t>(bytes))) == 0; },
+        [&](const ctrl::FdSegment &g) {
+            return (e = m.add(g.fd, static_cast<size_t>(g.offset), static_cast<size_t>(g.size))) == 0;
+        });
+    if (e) return e;
+    if (fr) return fr == 1 ? kVmmNotOffered : kVmmUnreachable;
+    return m.finish(dev, va, sizes);
 }
 
 int vmm_unmap(void *va, const std::vector<size_t> &sizes) {

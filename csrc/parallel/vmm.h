@@ -58,19 +58,19 @@ int vmm_segments(const void *ptr, size_t len, size_t max_segments, std::vector<V
 // (owned by the caller); fails for allocations created without that handle
 // type.
 int vmm_export_fd(uintptr_t base, int *fd);
-// vmm_import_map: imports `n` allocations (fds[i] of sizes[i] bytes; the
-// descriptors are not consumed) and maps them back to back at a new address
-// readable and writable by device `dev`.
-int vmm_import_map(const int *fds, const size_t *sizes, size_t n, int dev, void **va);
 // vmm_offer: offers [ptr, ptr + len) of VMM memory under `key` on this
 // process's descriptor server (handles exported afresh per request); 0 with
 // the owner's base and span of the allocations behind it, else non-zero.
 int vmm_offer(const void *ptr, size_t len, uint64_t key, uintptr_t *base, size_t *span);
 void vmm_withdraw(uint64_t key);
 // vmm_open: fetches what process `pid` offered under `key` and maps it back
-// to back for device `dev`: *va stands for the owner's base; *sizes gets
-// the allocation sizes (for vmm_unmap). 1 if the key is not (or no longer)
-// offered, -1 if the owner is unreachable, else 0 or a CUresult.
+// to back for device `dev`, one allocation at a time as the handles arrive:
+// *va stands for the owner's base; *sizes gets the allocation sizes (for
+// vmm_unmap). 0, kVmmNotOffered if the key is not (or no longer) offered,
+// kVmmUnreachable if the owner did not answer, else the CUresult of the
+// failed mapping step.
+constexpr int kVmmNotOffered = -3;
+constexpr int kVmmUnreachable = -1;
 int vmm_open(long pid, uint64_t key, int dev, int timeout_ms, void **va, std::vector<size_t> *sizes);
 int vmm_unmap(void *va, const std::vector<size_t> &sizes);
 

@@ -506,7 +506,10 @@ class RemoteMaps {
             if (e != 0) {
                 MPCOMM_LOG_ERROR("MPComm[nvl]: pid %ld's VMM buffer 0x%lx: %s (%d)\n", pid,
                                  static_cast<unsigned long>(rec.addr),
-                                 e == 1 ? "withdrawn" : e == -1 ? "owner unreachable" : "cannot map", e);
+                                 e == vmm::kVmmNotOffered ? "withdrawn"
+                                 : e == vmm::kVmmUnreachable ? "owner unreachable"
+                                                             : "cannot map",
+                                 e);
                 return kWcRemAccessErr;
             }
             it = vmm_opened_.emplace(mk, reinterpret_cast<uintptr_t>(p)).first;

@@ -6,12 +6,14 @@
 #include <cstring>
 #include <string>
 #include <set>
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <thread>
 #include <vector>
 
 #include <sys/mman.h>
+#include <sys/resource.h>
 #include <unistd.h>
 
 #include "core/core.h"
@@ -150,36 +152,60 @@ static void test_wire_layout() {
           kQosControlFrameMagic == 0x4D505146);
 }
 
-// Descriptor hand-off (VMM handles between processes): an offer's provider
-// runs per request and its descriptors arrive as new descriptors of the same
-// files, with their offsets, also past one message (64 per message);
-// unknown and withdrawn keys and a failing provider answer 1, a missing
-// server -1.
+// Descriptor hand-off (VMM handles between processes): an offer exports its
+// segments per request and they arrive, in order and with their offsets, as
+// new descriptors of the same files, 64 per message; unknown and withdrawn
+// keys and a failing export answer 1, a missing server -1. 300 segments go
+// through under a descriptor limit far below 2 x 300, since each side holds
+// at most one message's worth open.
 static void test_fd_share() {
     const std::string name = "mpcomm-test-fd." + std::to_string(getpid());
     int f = memfd_create("fdshare", 0);
     CHECK(f >= 0 && ftruncate(f, 4096) == 0);
     CHECK(pwrite(f, "B200", 4, 0) == 4);
-    int calls = 0;
-    CHECK(ctrl::fd_offer(name, 7, [f, &calls](std::vector<ctrl::FdSegment> *out) {
-              ++calls;
-              for (int i = 0; i < 70; ++i) out->push_back(ctrl::FdSegment{uint64_t(i) * 4096, 4096, dup(f)});
-              return true;
-          }) == 0);
-    CHECK(ctrl::fd_offer(name, 9, [](std::vector<ctrl::FdSegment> *) { return false; }) == 0);
-    std::vector<ctrl::FdSegment> got;
-    CHECK(ctrl::fd_fetch(name, 7, 2000, &got) == 0 && got.size() == 70 && calls == 1);
-    for (size_t i = 0; i < got.size(); ++i) {
-        char buf[4] = {0};
-        CHECK(got[i].offset == i * 4096 && got[i].size == 4096 && got[i].fd != f);
-        CHECK(pread(got[i].fd, buf, 4, 0) == 4 && std::memcmp(buf, "B200", 4) == 0);
-        close(got[i].fd);
-    }
-    CHECK(ctrl::fd_fetch(name, 8, 2000, &got) == 1 && got.empty());
-    CHECK(ctrl::fd_fetch(name, 9, 2000, &got) == 1 && got.empty());
+    const size_t nseg = 300;
+    std::atomic<int> exports{0};
+    ctrl::FdOffer o;
+    for (size_t i = 0; i < nseg; ++i) o.segments.push_back(ctrl::FdSegment{i * 4096, 4096, -1});
+    o.export_fd = [f, &exports](size_t) {
+        ++exports;
+        return dup(f);
+    };
+    CHECK(ctrl::fd_offer(name, 7, o) == 0);
+    ctrl::FdOffer bad = o;
+    bad.export_fd = [f](size_t i) { return i < 100 ? dup(f) : -1; };  // fails in the second message
+    CHECK(ctrl::fd_offer(name, 9, bad) == 0);
+    rlimit old{};
+    CHECK(getrlimit(RLIMIT_NOFILE, &old) == 0);
+    rlimit low = old;
+    low.rlim_cur = std::min<rlim_t>(old.rlim_cur, 256);
+    CHECK(setrlimit(RLIMIT_NOFILE, &low) == 0);
+    size_t count = 0, seen = 0;
+    uint64_t bytes = 0;
+    bool ordered = true, same_file = true;
+    const int rc = ctrl::fd_fetch(
+        name, 7, 5000, [&](size_t c, uint64_t b) { count = c; bytes = b; return true; },
+        [&](const ctrl::FdSegment &g) {
+            char buf[4] = {0};
+            ordered &= g.offset == seen * 4096 && g.size == 4096 && g.fd != f;
+            same_file &= pread(g.fd, buf, 4, 0) == 4 && std::memcmp(buf, "B200", 4) == 0;
+            ++seen;
+            return true;
+        });
+    CHECK(setrlimit(RLIMIT_NOFILE, &old) == 0);
+    CHECK(rc == 0 && count == nseg && bytes == nseg * 4096 && seen == nseg && ordered && same_file);
+    CHECK(exports.load() == static_cast<int>(nseg));
+    auto none = [](size_t, uint64_t) { return true; };
+    auto any = [](const ctrl::FdSegment &) { return true; };
+    CHECK(ctrl::fd_fetch(name, 8, 2000, none, any) == 1);
+    CHECK(ctrl::fd_fetch(name, 9, 2000, none, any) == 1);
+    // A receiver that stops early ends the fetch with -1 and leaks nothing.
+    size_t taken = 0;
+    CHECK(ctrl::fd_fetch(name, 7, 2000, none, [&](const ctrl::FdSegment &) { return ++taken < 10; }) == -1);
+    CHECK(taken == 10);
     ctrl::fd_withdraw(7);
-    CHECK(ctrl::fd_fetch(name, 7, 2000, &got) == 1);
-    CHECK(ctrl::fd_fetch(name + ".absent", 7, 200, &got) == -1);
+    CHECK(ctrl::fd_fetch(name, 7, 2000, none, any) == 1);
+    CHECK(ctrl::fd_fetch(name + ".absent", 7, 200, none, any) == -1);
     close(f);
     // Multicast group names map to one non-zero identity in every process.
     CHECK(vmm::mc_group_token("grp") == vmm::mc_group_token("grp"));
