@@ -14,6 +14,8 @@
 
 #include <sys/mman.h>
 #include <sys/resource.h>
+#include <sys/socket.h>
+#include <sys/un.h>
 #include <unistd.h>
 
 #include "core/core.h"
@@ -206,6 +208,21 @@ static void test_fd_share() {
     ctrl::fd_withdraw(7);
     CHECK(ctrl::fd_fetch(name, 7, 2000, none, any) == 1);
     CHECK(ctrl::fd_fetch(name + ".absent", 7, 200, none, any) == -1);
+    // A server that accepts and never answers: the fetch gives up at its timeout.
+    {
+        const std::string mute = name + ".mute";
+        int l = socket(AF_UNIX, SOCK_SEQPACKET, 0);
+        sockaddr_un a{};
+        a.sun_family = AF_UNIX;
+        std::memcpy(a.sun_path + 1, mute.data(), mute.size());
+        const socklen_t alen = static_cast<socklen_t>(offsetof(sockaddr_un, sun_path) + 1 + mute.size());
+        CHECK(l >= 0 && bind(l, reinterpret_cast<sockaddr *>(&a), alen) == 0 && listen(l, 4) == 0);
+        const auto t0 = std::chrono::steady_clock::now();
+        CHECK(ctrl::fd_fetch(mute, 7, 300, none, any) == -1);
+        const auto dt = std::chrono::steady_clock::now() - t0;
+        CHECK(dt >= std::chrono::milliseconds(250) && dt < std::chrono::seconds(3));
+        close(l);
+    }
     close(f);
     // Multicast group names map to one non-zero identity in every process.
     CHECK(vmm::mc_group_token("grp") == vmm::mc_group_token("grp"));
