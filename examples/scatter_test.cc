@@ -3,7 +3,7 @@
 // behind its README numbers; option names kept where they overlap).
 //
 //   target:     scatter_test --mode target --host-id T --tcp-port 5000 --buffer-size 4G [--gpu 0]
-//   initiator:  scatter_test --target T:10.0.0.2:5000 --size 1G --batch-size 4 \
+//   initiator:  scatter_test --target T:10.0.0.2:5000 --size 1G --batch-size 4
 //                            --test-type put,get --iterations 10 --warmup 3 [--gpu 0]
 //   both:       scatter_test --mode both --buffer-size 4G --size 1G ...  (serves its own
 //               buffer and targets itself: the single-box memory-pool setup; with
