@@ -323,6 +323,23 @@ static void test_mc_group_protocol() {
     for (int r : rc) CHECK(r == -1);
     CHECK(fake_mc::count("bind") == 0 && fake_mc::teardowns == 2);
     CHECK(std::chrono::steady_clock::now() - t0 < std::chrono::seconds(3));
+    // A creator that accepts and then stalls: the joiner gives up at its timeout.
+    {
+        const std::string name = base + ".stall";
+        const std::string path = "mpcomm-mcg-" + std::to_string(vmm::mc_group_token(name));
+        int l = socket(AF_UNIX, SOCK_STREAM, 0);
+        sockaddr_un a{};
+        a.sun_family = AF_UNIX;
+        std::memcpy(a.sun_path + 1, path.data(), path.size());
+        const socklen_t alen = static_cast<socklen_t>(offsetof(sockaddr_un, sun_path) + 1 + path.size());
+        CHECK(l >= 0 && bind(l, reinterpret_cast<sockaddr *>(&a), alen) == 0 && listen(l, 4) == 0);
+        vmm::McGroup g;
+        t0 = std::chrono::steady_clock::now();
+        CHECK(vmm::mc_group_join_with(fake_mc::ops, 1, name, 4096, 2, 300, &g) == -1);
+        const auto dt = std::chrono::steady_clock::now() - t0;
+        CHECK(dt >= std::chrono::milliseconds(250) && dt < std::chrono::seconds(3) && g.mc == 0);
+        close(l);
+    }
 }
 
 int main() {
