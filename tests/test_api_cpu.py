@@ -503,3 +503,20 @@ def test_nvls_group_from_name_fails_cleanly_without_gpus():
         with pytest.raises(RuntimeError):
             parallel.NvlsGroup.from_name(name, 1 << 20, 2, create=create, timeout_ms=300)
     assert time.monotonic() - t0 < 10
+
+
+def test_bench_comparators_fail_cleanly_without_gpus():
+    """The bench comparators report failure, never crash, on a host without
+    a usable GPU: the copy engine call returns a CUDA error and the
+    round-trip floor an empty list."""
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from mpcomm import _native
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.addressof(buf)
+    assert _native.copy_engine_async(p, p + 2048, 1024, 0) != 0
+    assert _native.copy_roundtrip_us(p, p + 2048, 1024, 4) == []
+    err, segs = _native.vmm_segments(p, 4096)
+    assert err != 0 and segs == []
